@@ -1,0 +1,1058 @@
+// build.cu -- on-device IMI index build (sm_100a).
+//
+// Reproduces, bit for bit, the reference's CPU index build with one worker
+// thread:
+//   k-means++ seeding         kmeans_core.cpp:138-186
+//   Lloyd iterations          kmeans_core.cpp:190-314
+//   per-subspace executors    kmeans_core.cpp:384-772
+//   compact + CSR reorganize  reorganize_core.cpp:18-311
+//
+// Exactness strategy:
+//   * distances use the reference's 8-lane fma order (common.cuh);
+//   * the k-means++ cumulative weight, a sequential double sum in the
+//     reference, is computed as an exact 128-bit fixed-point sum; the kernel
+//     proves that the reference's double cumsum never rounds (every prefix is
+//     representable) and otherwise falls back to the sequential double loop;
+//   * M-step sums run in sample order per cell over a stable counting-sort
+//     member list; the early-stop inertia is a sequential fp32 sum, evaluated
+//     only at iterations where the stop test can fire;
+//   * random draws (mt19937_64 seeds 42.., mt19937(iter + 12345)) are taken on
+//     the host with the same standard library and uploaded.
+#include "common.cuh"
+#include "imi_internal.h"
+
+#include <float.h>
+#include <limits.h>
+
+#include <algorithm>
+#include <random>
+#include <vector>
+
+namespace imi {
+
+constexpr int BT = 256;     // threads per block for the streaming kernels
+constexpr int SPB = 1024;   // samples per block (4 per thread)
+
+struct Dev {
+    int heads, n, dim, S, sub, T, kmax, NB;
+    int kst;               // stride of the per-cell work arrays (max k)
+    int ks[4];
+    const uint16_t* keys;
+    long long hstride, tstride;
+    float* cent;           // [T][kmax][sub]
+    int32_t* labels;       // [T][n]
+    float* md;             // [T][n]
+    int32_t* perm_a;       // [T][n]
+    int32_t* perm_b;       // [T][n]
+    unsigned long long* part_lo;  // [T][NB]
+    unsigned long long* part_hi;
+    int32_t* part_minl;    // [T][NB]
+    int32_t* part_bad;     // [T][NB]
+    int32_t* hist;         // [T][NB][256]
+    int32_t* dig_off;      // [T][256]
+    int32_t* dig_tot;      // [T][256]
+    int32_t* counts;       // [T][kmax]
+    int32_t* offs;         // [T][kmax+1]
+    int32_t* erank;        // [T][kmax]
+    const double* draws_u; // [S][kmax]
+    const int32_t* first;  // [S]
+    const int32_t* reseed; // [iters][kmax]
+    int32_t* done;         // [T]
+    float* prev_inertia;   // [T]
+    int32_t* iters_run;    // [T]
+    uint8_t* used;         // [heads][G]
+    int32_t* g2c;          // [heads][G]
+    int G;
+};
+
+IMI_DEV int task_h(const Dev& b, int t) { return t / b.S; }
+IMI_DEV int task_s(const Dev& b, int t) { return t % b.S; }
+
+IMI_DEV const uint16_t* sample_ptr(const Dev& b, int t, int i) {
+    return b.keys + (size_t)task_h(b, t) * b.hstride + (size_t)i * b.tstride + (size_t)task_s(b, t) * b.sub;
+}
+
+template <int SUB>
+IMI_DEV void load_sample(const Dev& b, int t, int i, float (&x)[SUB]) {
+    const uint4* p = reinterpret_cast<const uint4*>(sample_ptr(b, t, i));
+#pragma unroll
+    for (int q = 0; q < SUB / 8; ++q) {
+        const uint4 v = __ldg(p + q);
+        x[8 * q + 0] = bf16lo(v.x);
+        x[8 * q + 1] = bf16hi(v.x);
+        x[8 * q + 2] = bf16lo(v.y);
+        x[8 * q + 3] = bf16hi(v.y);
+        x[8 * q + 4] = bf16lo(v.z);
+        x[8 * q + 5] = bf16hi(v.z);
+        x[8 * q + 6] = bf16lo(v.w);
+        x[8 * q + 7] = bf16hi(v.w);
+    }
+}
+
+// float (>= 0) -> Q64.64 fixed point.  bad = not exactly representable within
+// the bounds that keep a sum of up to 2^24 values below 2^128.
+IMI_DEV u128 to_units(float v, int& lsb, int& bad) {
+    u128 r{0ull, 0ull};
+    lsb = INT_MAX;
+    if (v == 0.0f) return r;
+    const uint32_t bits = __float_as_uint(v);
+    const int E = (bits >> 23) & 0xff;
+    if (E == 0 || E == 255 || (bits >> 31)) {
+        bad = 1;
+        return r;
+    }
+    const uint32_t mant = (bits & 0x7fffffu) | 0x800000u;
+    const int e2 = E - 127 - 23;
+    lsb = e2 + __ffs(mant) - 1;
+    const int sh = e2 + 64;
+    if (sh > 80) {
+        bad = 1;
+        return r;
+    }
+    if (sh >= 64) {
+        r.hi = (unsigned long long)mant << (sh - 64);
+    } else if (sh >= 0) {
+        r.lo = (unsigned long long)mant << sh;
+        r.hi = sh > 40 ? ((unsigned long long)mant >> (64 - sh)) : 0ull;
+    } else {
+        const int rs = -sh;
+        if (rs >= 32 || (mant & ((1u << rs) - 1u))) {
+            bad = 1;
+            return r;
+        }
+        r.lo = mant >> rs;
+    }
+    return r;
+}
+
+IMI_DEV int u128_bitlen(u128 v) { return v.hi ? 128 - __clzll(v.hi) : (v.lo ? 64 - __clzll(v.lo) : 0); }
+
+IMI_DEV double u128_to_double_units(u128 v) {
+    // exact when v has <= 53 significant bits (checked by the caller)
+    return ((double)v.hi * 18446744073709551616.0 + (double)v.lo) * 5.421010862427522170037264e-20;  // * 2^-64
+}
+
+// ceil(target * 2^64) as u128 (target >= 0, finite)
+IMI_DEV u128 ceil_units(double target) {
+    u128 r{0ull, 0ull};
+    if (!(target > 0.0)) return r;
+    const unsigned long long bits = __double_as_longlong(target);
+    const int E = (int)((bits >> 52) & 0x7ff);
+    unsigned long long m = bits & 0xfffffffffffffull;
+    int e2;
+    if (E == 0) {
+        e2 = -1074;
+    } else {
+        m |= 1ull << 52;
+        e2 = E - 1075;
+    }
+    const int sh = e2 + 64;
+    if (sh >= 0) {
+        if (sh >= 64) {
+            r.hi = m << (sh - 64);
+        } else {
+            r.lo = m << sh;
+            r.hi = sh ? (m >> (64 - sh)) : 0ull;
+        }
+    } else {
+        const int rs = -sh;
+        if (rs >= 64) {
+            r.lo = 1ull;  // 0 < target*2^64 < 1
+        } else {
+            r.lo = m >> rs;
+            if (m & ((1ull << rs) - 1ull)) r.lo += 1ull;
+        }
+    }
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// k-means++
+// ---------------------------------------------------------------------------
+__global__ void kpp_first_kernel(Dev b) {
+    const int t = blockIdx.x;
+    const int s = task_s(b, t);
+    const int i = b.first[s];
+    const uint16_t* x = sample_ptr(b, t, i);
+    for (int d = threadIdx.x; d < b.sub; d += blockDim.x)
+        b.cent[(size_t)t * b.kmax * b.sub + d] = bf16_bits_to_f32(x[d]);
+}
+
+template <int SUB>
+__global__ void __launch_bounds__(BT) kpp_update_kernel(Dev b, int c) {
+    const int t = blockIdx.y;
+    if (c >= b.ks[task_s(b, t)]) return;
+    __shared__ __align__(16) float cp[SUB];
+    __shared__ unsigned long long rlo[BT / 32], rhi[BT / 32];
+    __shared__ int rl[BT / 32], rb[BT / 32];
+    const float* cprev = b.cent + ((size_t)t * b.kmax + (c - 1)) * SUB;
+    for (int d = threadIdx.x; d < SUB; d += BT) cp[d] = cprev[d];
+    __syncthreads();
+    u128 acc{0ull, 0ull};
+    int minl = INT_MAX, bad = 0;
+    float* md = b.md + (size_t)t * b.n;
+#pragma unroll 1
+    for (int j = 0; j < SPB / BT; ++j) {
+        const int i = blockIdx.x * SPB + j * BT + threadIdx.x;
+        if (i >= b.n) break;
+        float x[SUB];
+        load_sample<SUB>(b, t, i, x);
+        const float d = dist_lanes8<SUB>(x, cp);
+        const float prev = (c == 1) ? FLT_MAX : md[i];
+        const float m = (d < prev) ? d : prev;
+        md[i] = m;
+        int l;
+        acc = u128_add(acc, to_units(m, l, bad));
+        minl = min(minl, l);
+    }
+    // block reduce
+    for (int o = 16; o > 0; o >>= 1) {
+        u128 other;
+        other.lo = __shfl_xor_sync(0xffffffffu, acc.lo, o);
+        other.hi = __shfl_xor_sync(0xffffffffu, acc.hi, o);
+        acc = u128_add(acc, other);
+        minl = min(minl, __shfl_xor_sync(0xffffffffu, minl, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        rlo[w] = acc.lo;
+        rhi[w] = acc.hi;
+        rl[w] = minl;
+        rb[w] = bad;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        u128 s{0ull, 0ull};
+        int ml = INT_MAX, bb = 0;
+        for (int q = 0; q < BT / 32; ++q) {
+            s = u128_add(s, u128{rlo[q], rhi[q]});
+            ml = min(ml, rl[q]);
+            bb |= rb[q];
+        }
+        const size_t o = (size_t)t * b.NB + blockIdx.x;
+        b.part_lo[o] = s.lo;
+        b.part_hi[o] = s.hi;
+        b.part_minl[o] = ml;
+        b.part_bad[o] = bb;
+    }
+}
+
+// One CTA (1024 threads) per task: exact total, target, first crossing index.
+__global__ void __launch_bounds__(1024) kpp_pick_kernel(Dev b, int c) {
+    const int t = blockIdx.x;
+    const int s = task_s(b, t);
+    if (c >= b.ks[s]) return;
+    extern __shared__ __align__(16) unsigned char ksm[];
+    unsigned long long* plo = reinterpret_cast<unsigned long long*>(ksm);  // inclusive prefix per block
+    unsigned long long* phi = plo + b.NB;
+    __shared__ int s_minl, s_bad, s_sel, s_blk;
+    __shared__ unsigned long long s_tlo, s_thi;
+    __shared__ unsigned long long wlo[32], whi[32];
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        // sequential inclusive prefix over the block partials (NB is small)
+        u128 run{0ull, 0ull};
+        int ml = INT_MAX, bb = 0;
+        for (int q = 0; q < b.NB; ++q) {
+            const size_t o = (size_t)t * b.NB + q;
+            run = u128_add(run, u128{b.part_lo[o], b.part_hi[o]});
+            plo[q] = run.lo;
+            phi[q] = run.hi;
+            ml = min(ml, b.part_minl[o]);
+            bb |= b.part_bad[o];
+        }
+        s_minl = ml;
+        s_bad = bb;
+        s_sel = -1;
+        s_blk = -1;
+        s_tlo = run.lo;
+        s_thi = run.hi;
+    }
+    __syncthreads();
+    const u128 total{s_tlo, s_thi};
+    const float* md = b.md + (size_t)t * b.n;
+    const double u = b.draws_u[s * b.kst + c];
+    bool exact = !s_bad;
+    if (exact && (total.lo | total.hi)) exact = (u128_bitlen(total) - (s_minl + 64)) <= 53;
+    if (!exact) {
+        // the reference's own sequential double loop (kmeans_core.cpp:164-182)
+        if (tid == 0) {
+            double tot = 0.0;
+            for (int i = 0; i < b.n; ++i) tot += (double)md[i];
+            const double target = u * tot + 0.0;
+            double run = 0.0;
+            int sel = 0;
+            for (int i = 0; i < b.n; ++i) {
+                run += (double)md[i];
+                if (run >= target) {
+                    sel = i;
+                    break;
+                }
+            }
+            s_sel = sel;
+        }
+    } else {
+        const double totd = u128_to_double_units(total);
+        const double target = u * totd + 0.0;
+        const u128 tgt = ceil_units(target);
+        if (tid == 0) {
+            int blk = b.NB - 1;
+            for (int q = 0; q < b.NB; ++q) {
+                if (u128_ge(u128{plo[q], phi[q]}, tgt)) {
+                    blk = q;
+                    break;
+                }
+            }
+            s_blk = blk;
+        }
+        __syncthreads();
+        const int blk = s_blk;
+        u128 base{0ull, 0ull};
+        if (blk > 0) base = u128{plo[blk - 1], phi[blk - 1]};
+        // inclusive scan of this block's samples in order (1 per thread)
+        const int i = blk * SPB + tid;
+        int l, bad = 0;
+        u128 v = (i < b.n) ? to_units(md[i], l, bad) : u128{0ull, 0ull};
+        u128 x = v;
+        const int lane = tid & 31, w = tid >> 5;
+        for (int o = 1; o < 32; o <<= 1) {
+            u128 y = u128_shfl_up(x, o);
+            if (lane >= o) x = u128_add(x, y);
+        }
+        if (lane == 31) {
+            wlo[w] = x.lo;
+            whi[w] = x.hi;
+        }
+        __syncthreads();
+        if (w == 0) {
+            u128 y{wlo[lane], whi[lane]};
+            for (int o = 1; o < 32; o <<= 1) {
+                u128 z = u128_shfl_up(y, o);
+                if (lane >= o) y = u128_add(y, z);
+            }
+            wlo[lane] = y.lo;
+            whi[lane] = y.hi;
+        }
+        __syncthreads();
+        if (w > 0) x = u128_add(x, u128{wlo[w - 1], whi[w - 1]});
+        x = u128_add(x, base);
+        const bool hit = (i < b.n) && u128_ge(x, tgt);
+        if (hit) atomicMin(reinterpret_cast<unsigned int*>(&s_sel), (unsigned int)i);  // s_sel = -1 -> 0xffffffff
+    }
+    __syncthreads();
+    int sel = s_sel;
+    if (sel < 0 || sel >= b.n) sel = 0;
+    const uint16_t* xs = sample_ptr(b, t, sel);
+    for (int d = tid; d < b.sub; d += blockDim.x)
+        b.cent[((size_t)t * b.kmax + c) * b.sub + d] = bf16_bits_to_f32(xs[d]);
+}
+
+// ---------------------------------------------------------------------------
+// Lloyd E-step: first-min argmin over the task's centroids
+// ---------------------------------------------------------------------------
+template <int SUB>
+__global__ void __launch_bounds__(BT) estep_kernel(Dev b) {
+    const int t = blockIdx.y;
+    if (b.done[t]) return;
+    extern __shared__ __align__(16) float cs[];
+    const int k = b.ks[task_s(b, t)];
+    const int chunk = min(k, 32768 / SUB);
+    const int i = blockIdx.x * BT + threadIdx.x;
+    float x[SUB];
+    if (i < b.n) load_sample<SUB>(b, t, i, x);
+    float best = FLT_MAX;
+    int bi = 0;
+    const float* cg = b.cent + (size_t)t * b.kmax * SUB;
+    for (int c0 = 0; c0 < k; c0 += chunk) {
+        const int cn = min(chunk, k - c0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < cn * SUB / 4; e += BT)
+            reinterpret_cast<float4*>(cs)[e] = reinterpret_cast<const float4*>(cg + (size_t)c0 * SUB)[e];
+        __syncthreads();
+        if (i < b.n) {
+            for (int c = 0; c < cn; ++c) {
+                const float d = dist_lanes8<SUB>(x, cs + c * SUB);
+                if (d < best) {
+                    best = d;
+                    bi = c0 + c;
+                }
+            }
+        }
+    }
+    if (i < b.n) {
+        b.labels[(size_t)t * b.n + i] = bi;
+        b.md[(size_t)t * b.n + i] = best;
+    }
+}
+
+// Sequential fp32 inertia and the early-stop test (kmeans_core.cpp:216-262).
+__global__ void inertia_kernel(Dev b, int it, int max_iters, int min_iter, float tol, float rel_tol, int eval) {
+    const int t = blockIdx.x;
+    if (threadIdx.x != 0 || b.done[t]) return;
+    float inertia = 0.0f;
+    if (eval) {
+        const float* md = b.md + (size_t)t * b.n;
+        int i = 0;
+        for (; i + 4 <= b.n; i += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(md + i);
+            inertia = __fadd_rn(inertia, v.x);
+            inertia = __fadd_rn(inertia, v.y);
+            inertia = __fadd_rn(inertia, v.z);
+            inertia = __fadd_rn(inertia, v.w);
+        }
+        for (; i < b.n; ++i) inertia = __fadd_rn(inertia, md[i]);
+    }
+    const int iters = it + 1;
+    if (eval) {
+        const float prev = b.prev_inertia[t];
+        const float change = fabsf(__fsub_rn(prev, inertia));
+        const float rel = (prev > 0.0f) ? __fdiv_rn(change, prev) : 0.0f;
+        if (iters >= max(1, min_iter) && (rel <= fmaxf(0.0f, rel_tol) || change <= fmaxf(0.0f, tol))) {
+            b.done[t] = 1;
+            b.iters_run[t] = iters;
+            return;
+        }
+        b.prev_inertia[t] = inertia;
+    }
+    b.iters_run[t] = iters;
+}
+
+// ---------------------------------------------------------------------------
+// Stable counting sort by an 8-bit digit (one LSD radix pass).
+//   key(t, i) = (keys[t*key_tstride + i] >> shift) & 255
+//   element at position p is perm_in[t][p] (or p when perm_in is null)
+// ---------------------------------------------------------------------------
+struct Radix {
+    int T, n, NB, shift;
+    const int32_t* keys;
+    long long key_tstride;
+    const int32_t* perm_in;   // [T][n] or null
+    int32_t* perm_out;        // [T][n]
+    int32_t* hist;            // [T][NB][256]
+    int32_t* dig_off;         // [T][256]
+    int32_t* dig_tot;         // [T][256]
+    const int32_t* gate;      // [T] skip tasks with gate[t] != 0 (may be null)
+};
+
+__global__ void __launch_bounds__(BT) radix_hist_kernel(Radix r) {
+    const int t = blockIdx.y;
+    if (r.gate && r.gate[t]) return;
+    __shared__ int h[256];
+    h[threadIdx.x] = 0;
+    __syncthreads();
+    for (int j = 0; j < SPB / BT; ++j) {
+        const int p = blockIdx.x * SPB + j * BT + threadIdx.x;
+        if (p >= r.n) break;
+        const int i = r.perm_in ? r.perm_in[(size_t)t * r.n + p] : p;
+        const int v = (r.keys[(size_t)t * r.key_tstride + i] >> r.shift) & 255;
+        atomicAdd(&h[v], 1);
+    }
+    __syncthreads();
+    r.hist[((size_t)t * r.NB + blockIdx.x) * 256 + threadIdx.x] = h[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(256) radix_scan_kernel(Radix r) {
+    const int t = blockIdx.x;
+    if (r.gate && r.gate[t]) return;
+    const int v = threadIdx.x;
+    int run = 0;
+    for (int q = 0; q < r.NB; ++q) {
+        const size_t o = ((size_t)t * r.NB + q) * 256 + v;
+        const int x = r.hist[o];
+        r.hist[o] = run;
+        run += x;
+    }
+    __shared__ int tot[256];
+    tot[v] = run;
+    __syncthreads();
+    if (v == 0) {
+        int acc = 0;
+        for (int q = 0; q < 256; ++q) {
+            r.dig_off[(size_t)t * 256 + q] = acc;
+            r.dig_tot[(size_t)t * 256 + q] = tot[q];
+            acc += tot[q];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(BT) radix_scatter_kernel(Radix r) {
+    const int t = blockIdx.y;
+    if (r.gate && r.gate[t]) return;
+    __shared__ int run[256];
+    __shared__ int wc[BT / 32][257];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    run[threadIdx.x] = 0;
+    for (int q = 0; q < BT / 32; ++q) wc[q][threadIdx.x] = 0;
+    if (threadIdx.x < BT / 32) wc[threadIdx.x][256] = 0;
+    __syncthreads();
+    const int32_t* hb = r.hist + ((size_t)t * r.NB + blockIdx.x) * 256;
+    const int32_t* doff = r.dig_off + (size_t)t * 256;
+    for (int j = 0; j < SPB / BT; ++j) {
+        const int p = blockIdx.x * SPB + j * BT + threadIdx.x;
+        const bool valid = p < r.n;
+        int i = 0, v = 256;
+        if (valid) {
+            i = r.perm_in ? r.perm_in[(size_t)t * r.n + p] : p;
+            v = (r.keys[(size_t)t * r.key_tstride + i] >> r.shift) & 255;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, v);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        if (rank == 0) wc[w][v] = __popc(peers);
+        __syncthreads();
+        if (valid) {
+            int before = run[v];
+            for (int q = 0; q < w; ++q) before += wc[q][v];
+            r.perm_out[(size_t)t * r.n + doff[v] + hb[v] + before + rank] = i;
+        }
+        __syncthreads();
+        {
+            int add = 0;
+            for (int q = 0; q < BT / 32; ++q) {
+                add += wc[q][threadIdx.x];
+                wc[q][threadIdx.x] = 0;
+            }
+            run[threadIdx.x] += add;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// M-step
+// ---------------------------------------------------------------------------
+// Label counts for k > 256 (one smem histogram per block, then global adds).
+__global__ void __launch_bounds__(BT) label_count_kernel(Dev b) {
+    const int t = blockIdx.y;
+    if (b.done[t]) return;
+    const int k = b.ks[task_s(b, t)];
+    for (int e = blockIdx.x * BT + threadIdx.x; e < b.n; e += gridDim.x * BT)
+        atomicAdd(&b.counts[(size_t)t * b.kst + b.labels[(size_t)t * b.n + e]], 1);
+    (void)k;
+}
+
+// offsets, empty ranks (one CTA per task).  When from_radix, counts are the
+// single-pass digit totals.
+__global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix) {
+    const int t = blockIdx.x;
+    if (b.done[t]) return;
+    const int k = b.ks[task_s(b, t)];
+    __shared__ int red[32];
+    __shared__ int carry_c, carry_e;
+    if (threadIdx.x == 0) {
+        carry_c = 0;
+        carry_e = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < k; base += blockDim.x) {
+        const int c = base + threadIdx.x;
+        int cnt = 0;
+        if (c < k) {
+            cnt = from_radix ? b.dig_tot[(size_t)t * 256 + c] : b.counts[(size_t)t * b.kst + c];
+            if (from_radix) b.counts[(size_t)t * b.kst + c] = cnt;
+        }
+        // two block scans (counts, empties)
+        int tot;
+        int x = cnt, e = (c < k && cnt == 0) ? 1 : 0;
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+        int xs = x, es = e;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a1 = __shfl_up_sync(0xffffffffu, xs, o);
+            const int a2 = __shfl_up_sync(0xffffffffu, es, o);
+            if (lane >= o) {
+                xs += a1;
+                es += a2;
+            }
+        }
+        __shared__ int wsx[32], wse[32];
+        if (lane == 31) {
+            wsx[w] = xs;
+            wse[w] = es;
+        }
+        __syncthreads();
+        if (w == 0) {
+            int y1 = wsx[lane], y2 = wse[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a1 = __shfl_up_sync(0xffffffffu, y1, o);
+                const int a2 = __shfl_up_sync(0xffffffffu, y2, o);
+                if (lane >= o) {
+                    y1 += a1;
+                    y2 += a2;
+                }
+            }
+            wsx[lane] = y1;
+            wse[lane] = y2;
+        }
+        __syncthreads();
+        const int bx = (w ? wsx[w - 1] : 0) + carry_c;
+        const int be = (w ? wse[w - 1] : 0) + carry_e;
+        if (c < k) {
+            b.offs[(size_t)t * (b.kst + 1) + c] = bx + xs - x;
+            b.erank[(size_t)t * b.kst + c] = be + es - e;
+        }
+        tot = wsx[31];
+        const int tote = wse[31];
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            carry_c += tot;
+            carry_e += tote;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) b.offs[(size_t)t * (b.kst + 1) + k] = carry_c;
+    (void)red;
+}
+
+// centroid[c][d] = (sum over members in sample order) * (1 / size); empty cells
+// take the iteration's next reseed draw (kmeans_core.cpp:268-311).
+__global__ void __launch_bounds__(BT) msum_kernel(Dev b, int it, const int32_t* perm) {
+    const int t = blockIdx.y;
+    if (b.done[t]) return;
+    const int k = b.ks[task_s(b, t)];
+    const int e = blockIdx.x * BT + threadIdx.x;
+    const int c = e / b.sub, d = e - c * b.sub;
+    if (c >= k) return;
+    const int cnt = b.counts[(size_t)t * b.kst + c];
+    float* out = b.cent + ((size_t)t * b.kmax + c) * b.sub + d;
+    if (cnt > 0) {
+        const int off = b.offs[(size_t)t * (b.kst + 1) + c];
+        const int32_t* pm = perm + (size_t)t * b.n + off;
+        float s = 0.0f;
+        int m = 0;
+        for (; m + 8 <= cnt; m += 8) {
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v[q] = bf16_bits_to_f32(sample_ptr(b, t, pm[m + q])[d]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) s = __fadd_rn(s, v[q]);
+        }
+        for (; m < cnt; ++m) s = __fadd_rn(s, bf16_bits_to_f32(sample_ptr(b, t, pm[m])[d]));
+        const float inv = __fdiv_rn(1.0f, (float)cnt);
+        *out = __fmul_rn(s, inv);
+    } else {
+        const int r = b.erank[(size_t)t * b.kst + c];
+        const int i = b.reseed[(size_t)it * b.kst + r];
+        *out = bf16_bits_to_f32(sample_ptr(b, t, i)[d]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Reorganize (per head; reorganize_core.cpp:18-311)
+// ---------------------------------------------------------------------------
+IMI_DEV int comb_id(const Dev& b, const int32_t* sl, int h, int i) {
+    int g = 0;
+    for (int s = 0; s < b.S; ++s) g = g * b.ks[s] + sl[((size_t)h * b.S + s) * b.n + i];
+    return g;
+}
+
+__global__ void reorg_mark_kernel(Dev b) {
+    const int h = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= b.n) return;
+    b.used[(size_t)h * b.G + comb_id(b, b.labels, h, i)] = 1;
+}
+
+// compact ids in ascending Cartesian order; cell codes; n_active
+__global__ void __launch_bounds__(1024) reorg_compact_kernel(Dev b, BuildArgs a) {
+    const int h = blockIdx.x;
+    __shared__ int wsum[32];
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int base = 0; base < b.G; base += blockDim.x) {
+        const int g = base + threadIdx.x;
+        const int f = (g < b.G) ? b.used[(size_t)h * b.G + g] : 0;
+        int x = f;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[w] = x;
+        __syncthreads();
+        if (w == 0) {
+            int y = wsum[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int z = __shfl_up_sync(0xffffffffu, y, o);
+                if (lane >= o) y += z;
+            }
+            wsum[lane] = y;
+        }
+        __syncthreads();
+        const int cidx = carry + (w ? wsum[w - 1] : 0) + x - f;
+        if (g < b.G) {
+            b.g2c[(size_t)h * b.G + g] = f ? cidx : -1;
+            if (f && cidx < a.n_slots) {
+                // packed digits, byte s = digit of subspace s
+                int rem = g, code = 0;
+                for (int s = b.S - 1; s >= 0; --s) {
+                    const int dg = rem % b.ks[s];
+                    rem /= b.ks[s];
+                    code |= dg << (8 * s);
+                }
+                a.cell_code[(size_t)h * a.n_slots + cidx] = (b.S == 1) ? g : code;
+            }
+        }
+        const int tot = wsum[31];
+        __syncthreads();
+        if (threadIdx.x == 0) carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) a.n_active[h] = carry;
+}
+
+// CSR offsets from the sorted member list: a new compact id starts at p
+__global__ void reorg_offsets_kernel(Dev b, BuildArgs a, const int32_t* perm) {
+    const int h = blockIdx.y;
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= b.n) return;
+    const int32_t* pm = perm + (size_t)h * b.n;
+    const int f = b.g2c[(size_t)h * b.G + comb_id(b, b.labels, h, pm[p])];
+    const int pf = p ? b.g2c[(size_t)h * b.G + comb_id(b, b.labels, h, pm[p - 1])] : -1;
+    if (f != pf && f < a.n_slots) a.cell_offsets[(size_t)h * (a.n_slots + 1) + f] = p;
+}
+
+// padded per-slot metadata (indexing.py:108-174 layout)
+__global__ void reorg_meta_kernel(Dev b, BuildArgs a) {
+    const int h = blockIdx.y;
+    const int na = a.n_active[h];
+    const int c = blockIdx.x;
+    if (c > a.n_slots) return;
+    int32_t* offs = a.cell_offsets + (size_t)h * (a.n_slots + 1);
+    if (c == a.n_slots || c >= na) {
+        if (threadIdx.x == 0) offs[c] = b.n;
+    }
+    if (c == a.n_slots) return;
+    const bool active = c < na;
+    if (threadIdx.x == 0) {
+        const int next = (c + 1 < na) ? offs[c + 1] : b.n;
+        a.cell_sizes[(size_t)h * a.n_slots + c] = active ? next - offs[c] : 0;
+        a.cell_mask[(size_t)h * a.n_slots + c] = active ? 0 : 1;
+        if (!active) a.cell_code[(size_t)h * a.n_slots + c] = -1;
+    }
+    float* row = a.centroids + ((size_t)h * a.n_slots + c) * b.dim;
+    const int code = active ? a.cell_code[(size_t)h * a.n_slots + c] : 0;
+    for (int d = threadIdx.x; d < b.dim; d += blockDim.x) {
+        float v = 0.0f;
+        if (active) {
+            const int s = d / b.sub, dd = d - s * b.sub;
+            const int dg = (b.S == 1) ? code : ((code >> (8 * s)) & 0xff);
+            v = b.cent[(((size_t)h * b.S + s) * b.kmax + dg) * b.sub + dd];
+        }
+        row[d] = v;
+    }
+}
+
+// list rows in member order (reorganize_core.cpp:298-308)
+__global__ void reorg_gather_kernel(Dev b, BuildArgs a, const int32_t* perm) {
+    const int h = blockIdx.y;
+    const int row = blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4);
+    const int q = threadIdx.x & 15;
+    if (row >= b.n) return;
+    const int src = perm[(size_t)h * b.n + row];
+    const int n16 = b.dim * 2 / 16;
+    for (int qq = q; qq < n16; qq += 16) {
+        const uint4* sk = reinterpret_cast<const uint4*>(a.keys + (size_t)h * a.head_stride + (size_t)src * a.token_stride);
+        const uint4* sv = reinterpret_cast<const uint4*>(a.values + (size_t)h * a.head_stride + (size_t)src * a.token_stride);
+        reinterpret_cast<uint4*>(a.list_keys + ((size_t)h * a.list_rows + row) * b.dim)[qq] = __ldg(sk + qq);
+        reinterpret_cast<uint4*>(a.list_values + ((size_t)h * a.list_rows + row) * b.dim)[qq] = __ldg(sv + qq);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host orchestration
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Layout {
+    size_t labels, md, perm_a, perm_b, part_lo, part_hi, part_minl, part_bad, hist, dig_off, dig_tot, counts, offs,
+        erank, draws_u, first, reseed, done, prev, iters, used, g2c, total;
+};
+
+Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters, bool own_labels) {
+    const int S = parts == 0 ? 1 : parts;
+    const int T = heads * S;
+    int kmax = 1;
+    long long G = 1;
+    for (int s = 0; s < S; ++s) {
+        kmax = std::max(kmax, ks[s]);
+        G *= ks[s];
+    }
+    const int NB = (n + SPB - 1) / SPB;
+    Layout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        size_t r = o;
+        o += (bytes + 255) & ~size_t(255);
+        return r;
+    };
+    L.labels = own_labels ? take((size_t)T * n * 4) : 0;
+    L.md = take((size_t)T * n * 4);
+    L.perm_a = take((size_t)T * n * 4);
+    L.perm_b = take((size_t)T * n * 4);
+    L.part_lo = take((size_t)T * NB * 8);
+    L.part_hi = take((size_t)T * NB * 8);
+    L.part_minl = take((size_t)T * NB * 4);
+    L.part_bad = take((size_t)T * NB * 4);
+    L.hist = take((size_t)T * NB * 256 * 4);
+    L.dig_off = take((size_t)T * 256 * 4);
+    L.dig_tot = take((size_t)T * 256 * 4);
+    L.counts = take((size_t)T * kmax * 4);
+    L.offs = take((size_t)T * (kmax + 1) * 4);
+    L.erank = take((size_t)T * kmax * 4);
+    L.draws_u = take((size_t)S * kmax * 8);
+    L.first = take((size_t)S * 4);
+    L.reseed = take((size_t)std::max(1, max_iters) * kmax * 4);
+    L.done = take((size_t)T * 4);
+    L.prev = take((size_t)T * 4);
+    L.iters = take((size_t)T * 4);
+    L.used = take((size_t)heads * G);
+    L.g2c = take((size_t)heads * G * 4);
+    L.total = o;
+    return L;
+}
+
+}  // namespace
+
+size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks) {
+    // sized for up to 64 Lloyd iterations of reseed draws
+    return layout(heads, n, dim, parts, ks, 64, true).total;
+}
+
+template <int SUB>
+static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
+    cudaError_t e;
+    // ---- k-means++
+    kpp_first_kernel<<<d.T, 128, 0, st>>>(d);
+    int kmax_all = 0;
+    for (int s = 0; s < d.S; ++s) kmax_all = std::max(kmax_all, d.ks[s]);
+    const size_t pick_smem = (size_t)d.NB * 16;
+    if ((e = cudaFuncSetAttribute(kpp_pick_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pick_smem)) !=
+        cudaSuccess)
+        return e;
+    for (int c = 1; c < kmax_all; ++c) {
+        kpp_update_kernel<SUB><<<dim3(d.NB, d.T), BT, 0, st>>>(d, c);
+        kpp_pick_kernel<<<d.T, 1024, pick_smem, st>>>(d, c);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // ---- Lloyd
+    const int chunk = std::min(kmax_all, 32768 / SUB);
+    const size_t es_smem = (size_t)chunk * SUB * 4;
+    if ((e = cudaFuncSetAttribute(estep_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)es_smem)) !=
+        cudaSuccess)
+        return e;
+    const int two_pass = kmax_all > 256;
+    for (int it = 0; it < a.max_iters; ++it) {
+        estep_kernel<SUB><<<dim3((d.n + BT - 1) / BT, d.T), BT, es_smem, st>>>(d);
+        const int eval = it >= std::max(0, a.early_stop_min_iter - 2) ? 1 : 0;
+        inertia_kernel<<<d.T, 32, 0, st>>>(d, it, a.max_iters, a.early_stop_min_iter, a.tol, a.early_stop_rel_tol,
+                                            eval);
+        Radix r{};
+        r.T = d.T;
+        r.n = d.n;
+        r.NB = d.NB;
+        r.keys = d.labels;
+        r.key_tstride = d.n;
+        r.hist = d.hist;
+        r.dig_off = d.dig_off;
+        r.dig_tot = d.dig_tot;
+        r.gate = d.done;
+        r.shift = 0;
+        r.perm_in = nullptr;
+        r.perm_out = d.perm_a;
+        radix_hist_kernel<<<dim3(d.NB, d.T), BT, 0, st>>>(r);
+        radix_scan_kernel<<<d.T, 256, 0, st>>>(r);
+        radix_scatter_kernel<<<dim3(d.NB, d.T), BT, 0, st>>>(r);
+        const int32_t* perm = d.perm_a;
+        if (two_pass) {
+            r.shift = 8;
+            r.perm_in = d.perm_a;
+            r.perm_out = d.perm_b;
+            radix_hist_kernel<<<dim3(d.NB, d.T), BT, 0, st>>>(r);
+            radix_scan_kernel<<<d.T, 256, 0, st>>>(r);
+            radix_scatter_kernel<<<dim3(d.NB, d.T), BT, 0, st>>>(r);
+            perm = d.perm_b;
+            cudaMemsetAsync(d.counts, 0, (size_t)d.T * d.kst * 4, st);
+            label_count_kernel<<<dim3(std::min(d.NB, 64), d.T), BT, 0, st>>>(d);
+        }
+        cell_prefix_kernel<<<d.T, 1024, 0, st>>>(d, two_pass ? 0 : 1);
+        msum_kernel<<<dim3((kmax_all * d.sub + BT - 1) / BT, d.T), BT, 0, st>>>(d, it, perm);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
+    const int S = a.parts == 0 ? 1 : a.parts;
+    if (!(a.parts == 0 || a.parts == 2 || a.parts == 4)) {
+        *why = "parts must be 0, 2 or 4";
+        return cudaErrorInvalidValue;
+    }
+    if (a.dim % (8 * S) != 0 || a.dim != 128) {
+        *why = "dim must be 128";
+        return cudaErrorInvalidValue;
+    }
+    const int sub = a.dim / S;
+    int kmax = 1;
+    long long G = 1;
+    for (int s = 0; s < S; ++s) {
+        if (a.ks[s] < 1 || (S > 1 && a.ks[s] > 255) || a.ks[s] > 65536) {
+            *why = "k per subspace must be in [1, 255] (IMI) or [1, 65536] (IVF)";
+            return cudaErrorInvalidValue;
+        }
+        kmax = std::max(kmax, a.ks[s]);
+        G *= a.ks[s];
+    }
+    if (G > (1ll << 26)) {
+        *why = "product of k over subspaces too large";
+        return cudaErrorInvalidValue;
+    }
+    if (a.n_tokens < 1 || a.n_tokens > (1 << 23)) {
+        *why = "token count must be in [1, 2^23]";
+        return cudaErrorInvalidValue;
+    }
+    if (a.kmax < kmax) {
+        *why = "sub_centroids stride kmax smaller than max k";
+        return cudaErrorInvalidValue;
+    }
+    if (a.max_iters < 1 || a.max_iters > 64) {
+        *why = "max_iters must be in [1, 64]";
+        return cudaErrorInvalidValue;
+    }
+    if ((a.token_stride * 2) % 16 != 0 || (a.head_stride * 2) % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(a.keys) & 15) || (reinterpret_cast<uintptr_t>(a.values) & 15)) {
+        *why = "keys/values and their strides must be 16-byte aligned";
+        return cudaErrorInvalidValue;
+    }
+    const bool own_labels = a.sub_labels == nullptr;
+    const Layout L = layout(a.heads, a.n_tokens, a.dim, a.parts, a.ks, 64, own_labels);
+    if (a.workspace_bytes < L.total || a.workspace == nullptr) {
+        *why = "workspace too small (see imi_build_workspace_size)";
+        return cudaErrorInvalidValue;
+    }
+    unsigned char* ws = static_cast<unsigned char*>(a.workspace);
+    Dev d{};
+    d.heads = a.heads;
+    d.n = a.n_tokens;
+    d.dim = a.dim;
+    d.S = S;
+    d.sub = sub;
+    d.T = a.heads * S;
+    d.kmax = a.kmax;
+    d.kst = kmax;
+    d.NB = (a.n_tokens + SPB - 1) / SPB;
+    for (int s = 0; s < 4; ++s) d.ks[s] = s < S ? a.ks[s] : 1;
+    d.keys = a.keys;
+    d.hstride = a.head_stride;
+    d.tstride = a.token_stride;
+    d.cent = a.sub_centroids;
+    d.labels = own_labels ? reinterpret_cast<int32_t*>(ws + L.labels) : a.sub_labels;
+    d.md = reinterpret_cast<float*>(ws + L.md);
+    d.perm_a = reinterpret_cast<int32_t*>(ws + L.perm_a);
+    d.perm_b = reinterpret_cast<int32_t*>(ws + L.perm_b);
+    d.part_lo = reinterpret_cast<unsigned long long*>(ws + L.part_lo);
+    d.part_hi = reinterpret_cast<unsigned long long*>(ws + L.part_hi);
+    d.part_minl = reinterpret_cast<int32_t*>(ws + L.part_minl);
+    d.part_bad = reinterpret_cast<int32_t*>(ws + L.part_bad);
+    d.hist = reinterpret_cast<int32_t*>(ws + L.hist);
+    d.dig_off = reinterpret_cast<int32_t*>(ws + L.dig_off);
+    d.dig_tot = reinterpret_cast<int32_t*>(ws + L.dig_tot);
+    d.counts = reinterpret_cast<int32_t*>(ws + L.counts);
+    d.offs = reinterpret_cast<int32_t*>(ws + L.offs);
+    d.erank = reinterpret_cast<int32_t*>(ws + L.erank);
+    d.draws_u = reinterpret_cast<const double*>(ws + L.draws_u);
+    d.first = reinterpret_cast<const int32_t*>(ws + L.first);
+    d.reseed = reinterpret_cast<const int32_t*>(ws + L.reseed);
+    d.done = reinterpret_cast<int32_t*>(ws + L.done);
+    d.prev_inertia = reinterpret_cast<float*>(ws + L.prev);
+    d.iters_run = reinterpret_cast<int32_t*>(ws + L.iters);
+    d.used = ws + L.used;
+    d.g2c = reinterpret_cast<int32_t*>(ws + L.g2c);
+    d.G = (int)G;
+    // per-cell work arrays use stride d.kst (max k); sub-centroids use a.kmax
+    // ---- host draws (the reference's seeds, the same <random> algorithms)
+    {
+        const int dkmax = kmax;
+        std::vector<double> du((size_t)S * dkmax, 0.0);
+        std::vector<int32_t> first(S, 0);
+        for (int s = 0; s < S; ++s) {
+            std::mt19937_64 rng(42 + s);
+            std::uniform_int_distribution<int32_t> pick(0, a.n_tokens - 1);
+            first[s] = pick(rng);
+            for (int c = 1; c < a.ks[s]; ++c) {
+                std::uniform_real_distribution<double> ud(0.0, 1.0);
+                du[(size_t)s * dkmax + c] = ud(rng);
+            }
+        }
+        std::vector<int32_t> rs((size_t)a.max_iters * dkmax, 0);
+        for (int it = 0; it < a.max_iters; ++it) {
+            std::mt19937 rng(it + 12345);
+            std::uniform_int_distribution<int32_t> pick(0, a.n_tokens - 1);
+            for (int r = 0; r < dkmax; ++r) rs[(size_t)it * dkmax + r] = pick(rng);
+        }
+        cudaError_t e;
+        if ((e = cudaMemcpyAsync(ws + L.draws_u, du.data(), du.size() * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            return e;
+        if ((e = cudaMemcpyAsync(ws + L.first, first.data(), first.size() * 4, cudaMemcpyHostToDevice, st)) !=
+            cudaSuccess)
+            return e;
+        if ((e = cudaMemcpyAsync(ws + L.reseed, rs.data(), rs.size() * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            return e;
+        // pageable copies are staged before return; keep the vectors alive
+        // until the stream has consumed them anyway
+        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
+    }
+    cudaMemsetAsync(d.done, 0, (size_t)d.T * 4, st);
+    cudaMemsetAsync(d.iters_run, 0, (size_t)d.T * 4, st);
+    {
+        // prev_inertia = FLT_MAX
+        std::vector<float> pv(d.T, FLT_MAX);
+        cudaMemcpyAsync(d.prev_inertia, pv.data(), pv.size() * 4, cudaMemcpyHostToDevice, st);
+        cudaStreamSynchronize(st);
+    }
+    cudaError_t e;
+    if (sub == 64) e = run_kmeans_sub<64>(d, a, st);
+    else if (sub == 32) e = run_kmeans_sub<32>(d, a, st);
+    else e = run_kmeans_sub<128>(d, a, st);
+    if (e != cudaSuccess) return e;
+    if (a.iters_run) cudaMemcpyAsync(a.iters_run, d.iters_run, (size_t)d.T * 4, cudaMemcpyDeviceToDevice, st);
+    // ---- reorganize
+    cudaMemsetAsync(d.used, 0, (size_t)a.heads * G, st);
+    reorg_mark_kernel<<<dim3((a.n_tokens + 255) / 256, a.heads), 256, 0, st>>>(d);
+    reorg_compact_kernel<<<a.heads, 1024, 0, st>>>(d, a);
+    // stable sort of token indices by (digit_0, ..., digit_{S-1}): LSD passes
+    Radix r{};
+    r.T = a.heads;
+    r.n = a.n_tokens;
+    r.NB = d.NB;
+    r.hist = d.hist;
+    r.dig_off = d.dig_off;
+    r.dig_tot = d.dig_tot;
+    r.gate = nullptr;
+    const int32_t* perm = nullptr;
+    int32_t* bufs[2] = {d.perm_a, d.perm_b};
+    int which = 0;
+    auto pass = [&](const int32_t* keys, long long tstride, int shift) {
+        r.keys = keys;
+        r.key_tstride = tstride;
+        r.shift = shift;
+        r.perm_in = perm;
+        r.perm_out = bufs[which];
+        radix_hist_kernel<<<dim3(d.NB, a.heads), BT, 0, st>>>(r);
+        radix_scan_kernel<<<a.heads, 256, 0, st>>>(r);
+        radix_scatter_kernel<<<dim3(d.NB, a.heads), BT, 0, st>>>(r);
+        perm = bufs[which];
+        which ^= 1;
+    };
+    if (S == 1) {
+        pass(d.labels, a.n_tokens, 0);
+        if (kmax > 256) pass(d.labels, a.n_tokens, 8);
+    } else {
+        for (int s = S - 1; s >= 0; --s) pass(d.labels + (size_t)s * a.n_tokens, (long long)S * a.n_tokens, 0);
+    }
+    reorg_offsets_kernel<<<dim3((a.n_tokens + 255) / 256, a.heads), 256, 0, st>>>(d, a, perm);
+    reorg_meta_kernel<<<dim3(a.n_slots + 1, a.heads), 128, 0, st>>>(d, a);
+    reorg_gather_kernel<<<dim3((a.n_tokens + 15) / 16, a.heads), 256, 0, st>>>(d, a, perm);
+    return cudaGetLastError();
+}
+
+}  // namespace imi

@@ -1,0 +1,33 @@
+// imi_internal.h -- kernel argument blocks and launchers shared by the .cu
+// files and the C-ABI layer (capi.cpp).  Not part of the public interface.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/imi_b200.h"
+
+namespace imi {
+
+using SelectArgs = imi_select_desc;
+using AttnArgs = imi_attn_desc;
+using AppendArgs = imi_append_desc;
+using AsyncArgs = imi_async_desc;
+using ApplyArgs = imi_apply_desc;
+using BuildArgs = imi_build_desc;
+
+cudaError_t launch_similarity(const uint16_t* q, const float* cent, float* out, int bg, int G, int n_cells, int dim,
+                              long long out_stride, cudaStream_t st);
+size_t select_smem_bytes(const SelectArgs& a);
+cudaError_t launch_select(const SelectArgs& a, cudaStream_t st);
+size_t attn_smem_bytes();
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+cudaError_t launch_append(const AppendArgs& a, cudaStream_t st);
+size_t async_smem_bytes(const AsyncArgs& a);
+cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st);
+cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st);
+
+size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks);
+cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why);
+
+}  // namespace imi

@@ -1,0 +1,197 @@
+/*
+ * imi_b200.h -- C ABI of the B200 (sm_100a) implementation of AdaptiveIMI's
+ * inverted-multi-index (IMI) KV-cache path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream, allocates no
+ * memory (scratch is passed in by the caller), and returns 0 on success or a
+ * nonzero status; imi_last_error() then describes the failure (thread-local).
+ *
+ * Tensor layouts (all row-major, contiguous unless a stride is given):
+ *   bf16 values are passed as their 16-bit patterns.
+ *   bg = batch * kv_heads ("KV groups"), G = query heads per KV group,
+ *   D = head dim (128), S = subspace parts (2, 4; 0 means IVF with one part),
+ *   n_slots = cell slots per group (padded, = reference n_centroids).
+ *
+ * Reference interfaces replaced (paths relative to the AdaptiveIMI project):
+ *   imi_build_index        imi::kmeans_execute{,_4,_ivf} (kmeans_core.cpp:822-1174)
+ *                          + imi::reorganize_from_kmeans{,_4,_ivf}
+ *                          (reorganize_core.cpp:313-569) + metadata padding
+ *                          (pipeline_bindings.cpp:206-276, indexing.py:108-174),
+ *                          i.e. the LayerPipeline merge path
+ *                          (layer_pipeline.cpp:1077-1401)
+ *   imi_query_group_similarities
+ *                          gpu_cluster_manager_cpp.fused_query_group_similarities
+ *                          (compute_wrappers.cpp:39-104, compute_impl.cu:62-103)
+ *   imi_select_cells       AdaptiveIMIRetrievalMixin._select_clusters
+ *                          (retrieval.py:295-303) + AdpIMI_Index.batch_access
+ *                          page truncation (wave_buffer_cpu_hotcold.cpp:303-371,
+ *                          897-929) + the execution-buffer layout of
+ *                          Copy.gather_copy_and_concat (gather_copy.cu:100-213)
+ *                          + the delta-row match of _append_delta_to_execution
+ *                          (async_update.py:20-76)
+ *   imi_sparse_attention   the gather of gather_copy_and_concat fused with
+ *                          weighted_flash_decoding (retrieval.py:439-447)
+ *   imi_decode_append      decode_update_kv_cache (runtime.py:378-392) and the
+ *                          async-update batch buffer (async_update.py:112-117)
+ *   imi_async_assign       _schedule_async_update batch step (async_update.py:118-161)
+ *   imi_apply_updates      _apply_async_centroid_updates (async_update.py:7-19)
+ */
+#ifndef IMI_B200_H_
+#define IMI_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IMI_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define IMI_API __attribute__((visibility("default")))
+#else
+#define IMI_API
+#endif
+
+#define IMI_OK 0
+#define IMI_ERR_INVALID 1
+#define IMI_ERR_CUDA 2
+
+/* Row-list entries written by imi_select_cells: (source << 30) | row, where
+ * source 0 = IMI list row, 1 = steady-zone row, 2 = delta-ring row. */
+#define IMI_ROW_SOURCE_SHIFT 30
+
+typedef struct imi_build_desc {
+    int32_t heads, n_tokens, dim, parts;   /* parts: 0 (IVF), 2 or 4 */
+    int32_t ks[4];                         /* k per subspace (ks[0] for IVF) */
+    const uint16_t* keys;                  /* bf16, element (h,i,d) at keys[h*head_stride + i*token_stride + d] */
+    const uint16_t* values;
+    int64_t head_stride, token_stride;     /* in elements; 16-byte aligned */
+    int32_t max_iters, early_stop_min_iter;
+    float tol, early_stop_rel_tol;
+    uint16_t* list_keys;                   /* [heads, list_rows, dim] out: rows in cell (CSR) order */
+    uint16_t* list_values;
+    int64_t list_rows;                     /* >= n_tokens */
+    int32_t n_slots, kmax;                 /* padded slots per head; sub-centroid stride (>= max k) */
+    int32_t* cell_sizes;                   /* [heads, n_slots] */
+    int32_t* cell_offsets;                 /* [heads, n_slots + 1] */
+    uint8_t* cell_mask;                    /* [heads, n_slots] 1 = empty / padding */
+    int32_t* cell_code;                    /* [heads, n_slots] packed subspace digits, -1 = padding */
+    float* centroids;                      /* [heads, n_slots, dim] merged centroids (zeros for padding) */
+    float* sub_centroids;                  /* [heads, S, kmax, dim/S] */
+    int32_t* sub_labels;                   /* [heads, S, n_tokens] or NULL (kept in the workspace) */
+    int32_t* n_active;                     /* [heads] active cells */
+    int32_t* iters_run;                    /* [heads, S] Lloyd iterations entered, or NULL */
+    void* workspace;
+    size_t workspace_bytes;
+} imi_build_desc;
+
+typedef struct imi_select_desc {
+    int32_t bg, G, dim, n_slots, parts, kmax;
+    int32_t ks[4];
+    const uint16_t* q;                     /* [bg, G, dim] */
+    const float* sub_centroids;            /* [bg, S, kmax, dim/S] */
+    const int32_t* cell_code;              /* [bg, n_slots] */
+    const int32_t* cell_sizes;             /* [bg, n_slots] */
+    const int32_t* cell_offsets;           /* [bg, n_slots + 1] */
+    const uint8_t* cell_mask;              /* [bg, n_slots] */
+    const float* centroids;                /* [bg, n_slots, dim] live merged centroids */
+    const uint8_t* cell_dirty;             /* [bg, n_slots] or NULL: 1 = live centroid was updated */
+    int32_t nprobe, max_tokens, buffer_pages, page_size, padding_id;
+    int32_t static_len;
+    const int32_t* delta_cell_ids;         /* [bg, delta_capacity] or NULL */
+    const int32_t* delta_count;            /* [bg] or NULL */
+    int32_t delta_capacity;
+    int32_t exec_capacity;                 /* row-list capacity (>= static_len + buffer_pages*page_size) */
+    int32_t* sel_cells;                    /* [bg, nprobe] out: selected cells in score order */
+    int32_t* sel_count;                    /* [bg] out */
+    int32_t* kept_count;                   /* [bg] out or NULL: cells kept before page truncation */
+    int32_t* row_index;                    /* [bg, exec_capacity] out */
+    int32_t* row_count;                    /* [bg] out */
+    float* scores_out;                     /* [bg, n_slots] out or NULL */
+} imi_select_desc;
+
+typedef struct imi_attn_desc {
+    int32_t bg, G, splits, exec_capacity;  /* dim is 128 */
+    float scale;
+    const uint16_t* q;                     /* [bg, G, 128] */
+    const int32_t* row_index;              /* [bg, exec_capacity] */
+    const int32_t* row_count;              /* [bg] */
+    const void* list_keys;                 /* [bg, list_rows, 128] */
+    const void* list_values;
+    int64_t list_rows;
+    const void* static_keys;               /* [bg, static_rows, 128] */
+    const void* static_values;
+    int64_t static_rows;
+    const void* delta_keys;                /* [bg, delta_rows, 128] or NULL */
+    const void* delta_values;
+    int64_t delta_rows;
+    float* part_o;                         /* scratch [bg, splits, G, 128] */
+    float* part_ml;                        /* scratch [bg, splits, G, 2] */
+    void* out;                             /* [bg, G, 128] bf16 out */
+} imi_attn_desc;
+
+typedef struct imi_append_desc {
+    int32_t bg, dim;
+    const void* new_keys;                  /* group h at new_keys + h*src_head_stride elements */
+    const void* new_values;
+    int64_t src_head_stride;
+    void* zone_keys;                       /* [bg, zone_rows, dim] */
+    void* zone_values;
+    int64_t zone_rows;
+    int32_t pos;
+    void* batch_keys;                      /* [bg, batch_cap, dim] or NULL */
+    void* batch_values;
+    int32_t batch_cap, batch_slot;
+} imi_append_desc;
+
+typedef struct imi_async_desc {
+    int32_t bg, dim, n_slots, parts, kmax, batch, batch_cap, threshold, ring_cap;
+    int32_t ks[4];
+    const uint16_t* batch_keys;            /* [bg, batch_cap, dim] */
+    const uint16_t* batch_values;
+    const float* sub_centroids;            /* [bg, S, kmax, dim/S] */
+    const int32_t* cell_code;              /* [bg, n_slots] */
+    float* shadow;                         /* [bg, n_slots, dim] */
+    uint8_t* shadow_dirty;                 /* [bg, n_slots] */
+    uint8_t* pending;                      /* [bg, n_slots] */
+    int32_t* counts;                       /* [bg, n_slots] */
+    int32_t* delta_counts;                 /* [bg, n_slots] */
+    float* delta_sums;                     /* [bg, n_slots, dim] */
+    uint16_t* ring_keys;                   /* [bg, ring_cap, dim] */
+    uint16_t* ring_values;
+    int32_t* ring_cell_ids;                /* [bg, ring_cap] */
+    int32_t* ring_write_pos;               /* [bg] */
+    int32_t* ring_count;                   /* [bg] */
+    int32_t* ids_out;                      /* [bg, batch] or NULL */
+} imi_async_desc;
+
+typedef struct imi_apply_desc {
+    int32_t bg, n_slots, dim;
+    const float* shadow;
+    float* live;
+    uint8_t* pending;
+    uint8_t* live_dirty;
+} imi_apply_desc;
+
+IMI_API int imi_abi_version(void);
+IMI_API const char* imi_last_error(void);
+
+IMI_API size_t imi_build_workspace_size(int32_t heads, int32_t n_tokens, int32_t dim, int32_t parts, const int32_t* ks);
+IMI_API int imi_build_index(const imi_build_desc* desc, void* stream);
+
+IMI_API int imi_query_group_similarities(const uint16_t* q, const float* centroids, float* out, int32_t kv_heads,
+                                 int32_t groups, int32_t n_clusters, int32_t dim, int64_t out_stride, void* stream);
+IMI_API int imi_select_cells(const imi_select_desc* desc, void* stream);
+IMI_API int imi_sparse_attention(const imi_attn_desc* desc, void* stream);
+IMI_API int imi_decode_append(const imi_append_desc* desc, void* stream);
+IMI_API int imi_async_assign(const imi_async_desc* desc, void* stream);
+IMI_API int imi_apply_updates(const imi_apply_desc* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IMI_B200_H_ */
