@@ -1,0 +1,410 @@
+"""``adpimi_cache``: the reference's IMI KV-cache object, device-resident.
+
+Keeps the public surface of ``cache_hub/adaptive_imi`` (``cache.py:43-518``,
+``indexing.py:548-628``, ``runtime.py:9-403``, ``retrieval.py:320-602``,
+``async_update.py:7-162``) so the reference's model wrappers drive it
+unchanged:
+
+* constructor arguments and sizing attributes (``list_capacity``,
+  ``static_capacity``, ``n_centroids``, ``nprobe``, ``buffer_size`` ...);
+* ``prefill_update_kv_cache`` builds the layer's IMI on the GPU from the
+  prefill K/V already in HBM (no host copy) and fills the steady zone;
+* ``prepare_cache`` sizes the decode buffers and switches ``attn_func``;
+* ``decode_update_kv_cache`` appends the new token (and feeds the optional
+  decode-time cell assignment);
+* ``attn_func`` / ``sparse_attention`` scores cells, selects them under the
+  token budget and page truncation, and attends over the steady zone, the
+  selected cells' rows and matching delta rows, all on the device with no host
+  synchronisation.
+
+Differences from the reference that do not change results: the IMI lists live
+in HBM, so there is no host page cache (every access is what the reference
+calls a miss) and ``execution_buffer_*_dict`` hold the per-group execution row
+list instead of copied rows; ``valid_lengths_dict`` holds the row counts.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from typing import Dict, List, Optional
+
+import torch
+
+from . import _lib, ops
+from .imi_adapter import IMIPipeline, IMIRuntimeConfig
+from .sizing import RetrievalSizes
+
+
+class adpimi_cache:  # noqa: N801  (reference class name)
+    def __init__(self, valid_start, layer_num: int, batch_size: int, max_length: int, num_key_value_heads: int,
+                 num_heads: int, head_dim: int, dtype: torch.dtype, layer_mapping: dict, max_new_length: int,
+                 input_length: Optional[int], static_pattern_start: int, static_pattern_end: int, core: int,
+                 pages_per_cluster: int, retrieval_budget: float, cache_ratio: float, buffer_cluster_num: int,
+                 prefill_bsz: int, num_gpus: int, model_size: int, subspace_parts: int = 4,
+                 runtime_config: Optional[Dict[str, Dict[str, object]]] = None) -> None:
+        # KV_Cache fields (cache_hub/base.py:9-45)
+        self.layer_num = layer_num
+        self.batch_size = batch_size
+        self.max_length = max_length
+        self.kv_head = num_key_value_heads
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.layer_mapping = layer_mapping
+        self.prefill_bsz = min(prefill_bsz, batch_size)
+        self.context = 0
+        self.num_gpus = num_gpus
+        self.model_size = model_size
+        if batch_size != 1:
+            raise ValueError("IMI cache currently supports batch_size=1.")
+        if dtype != torch.bfloat16:
+            raise ValueError("the B200 IMI cache stores bfloat16 K/V")
+        if head_dim != 128:
+            raise ValueError("the B200 IMI kernels support head_dim 128")
+        self.device_list = sorted(set(self.layer_mapping.values()), key=lambda x: int(x.split(":")[-1]))
+        self.valid_start_list = valid_start
+        self.static_pattern_start = static_pattern_start
+        self.static_pattern_end = static_pattern_end
+        self.static_pattern_total = static_pattern_start + static_pattern_end
+        self.group_size = self.num_heads // self.kv_head
+        self.batch_groups = self.batch_size * self.kv_head
+        self.page_size = 8
+        self.pages_per_cluster = pages_per_cluster
+        self.retrieval_budget = retrieval_budget
+        self.cache_ratio = cache_ratio
+        self.buffer_cluster_num = buffer_cluster_num
+        if subspace_parts not in (0, 2, 4):
+            raise ValueError("subspace_parts must be 0, 2 or 4")
+        self.subspace_parts = subspace_parts
+        self.core = core
+        runtime_config = runtime_config or {}
+        self.runtime_config = {
+            "pipeline": dict(runtime_config.get("pipeline") or {}),
+            "kmeans": dict(runtime_config.get("kmeans") or {}),
+            "async_update": dict(runtime_config.get("async_update") or {}),
+            "prefetch": dict(runtime_config.get("prefetch") or {}),
+        }
+        self.input_length = int(input_length) if input_length is not None else self.max_length - max_new_length
+        self.actual_gen_len = max_new_length - 1
+        self.capacity_input_length = int(self.max_length - max_new_length)
+        if self.input_length <= 0:
+            raise ValueError(f"input length({self.input_length}) should be larger than 0")
+        if self.capacity_input_length <= 0:
+            raise ValueError(f"capacity input length({self.capacity_input_length}) should be larger than 0")
+        self.list_capacity = max(self.capacity_input_length - self.static_pattern_total, 0)
+        self.list_stride = max(self.input_length - self.static_pattern_total, 0)
+        self.build_index_when_prefilling = self.list_capacity > 0
+        if self.build_index_when_prefilling:
+            self.static_capacity = self.static_pattern_total + self.actual_gen_len
+            self.static_stride = self.static_pattern_total + self.actual_gen_len
+        else:
+            self.static_capacity = self.capacity_input_length + self.actual_gen_len
+            self.static_stride = self.input_length + self.actual_gen_len
+        self.static_capacity = max(self.static_capacity, 1)
+        # sizing (runtime.py:31-63), fixed at construction from the capacity
+        self.sizes = RetrievalSizes.from_capacity(self.list_capacity, self.subspace_parts, self.retrieval_budget,
+                                                  self.buffer_cluster_num, self.static_capacity, self.page_size)
+        self.n_centroids = self.sizes.n_centroids
+        self.padding_cluster_id = self.sizes.padding_cluster_id
+        self.nprobe = self.sizes.nprobe
+        self.max_retrieval_tokens = self.sizes.max_retrieval_tokens
+        self.budget_tokens = self.max_retrieval_tokens
+        self.buffer_size = self.sizes.buffer_size
+        self.execution_stride = self.sizes.execution_stride
+        self.retrieval_execution_stride = self.buffer_size * self.page_size
+        self.max_retrieval_pages = max((self.max_retrieval_tokens + 7) // 8, 1)
+        self.cache_size = 0  # no host page cache: lists are HBM-resident
+        self.steady_zone_keys: List[torch.Tensor] = []
+        self.steady_zone_values: List[torch.Tensor] = []
+        for ldx in range(layer_num):
+            dev = self.layer_mapping[str(ldx)]
+            self.steady_zone_keys.append(torch.zeros((batch_size, self.kv_head, self.static_capacity, head_dim),
+                                                     dtype=dtype, device=dev))
+            self.steady_zone_values.append(torch.zeros_like(self.steady_zone_keys[-1]))
+        self.list_keys: List[Optional[torch.Tensor]] = [None] * layer_num
+        self.list_values: List[Optional[torch.Tensor]] = [None] * layer_num
+        self.index: List[Optional[ops.IMIIndex]] = [None] * layer_num
+        self.imi_pipelines: List[Optional[IMIPipeline]] = []
+        if self.build_index_when_prefilling:
+            for ldx in range(layer_num):
+                self.imi_pipelines.append(IMIPipeline(
+                    layer_idx=ldx, kv_heads=self.kv_head, head_dim=head_dim, dtype=dtype,
+                    device_id=int(self.layer_mapping[str(ldx)].split(":")[-1]), max_tokens=self.list_capacity,
+                    subspace_parts=self.subspace_parts, n_slots=self.n_centroids,
+                    runtime_config=IMIRuntimeConfig(pipeline=self.runtime_config["pipeline"],
+                                                    kmeans=self.runtime_config["kmeans"])))
+        else:
+            self.imi_pipelines = [None] * layer_num
+        self.layer_ready = [False] * layer_num
+        self.layer_started = [False] * layer_num
+        self.cache_prepared = False
+        self.attn_func = self.dense_attention
+        # async centroid update (async_update.py; off unless enabled)
+        acfg = self.runtime_config["async_update"]
+        self.async_update_enabled = bool(acfg.get("enabled", False))
+        self.async_update_batch = max(int(acfg.get("batch", 16)), 1)
+        self.async_update_threshold = max(int(acfg.get("threshold", 16)), 1)
+        self.async_update_delta_tokens = max(int(acfg.get("delta_tokens", 512)), 1)
+        self._async: List[Optional[Dict[str, object]]] = [None] * layer_num
+        # per-device decode buffers (filled by prepare_cache)
+        self.execution_buffer_keys_dict: Dict[str, torch.Tensor] = {}
+        self.execution_buffer_values_dict: Dict[str, torch.Tensor] = {}
+        self.valid_lengths_dict: Dict[str, torch.Tensor] = {}
+        self._dec: Dict[str, Dict[str, torch.Tensor]] = {}
+        self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity)
+        # optional measurement hooks (bench.py): per-call row counts and CUDA
+        # events around the attention launch, both on the launching stream
+        self.row_count_log: Optional[torch.Tensor] = None
+        self.attn_event_log: Optional[list] = None
+        self._log_pos = 0
+
+    # ------------------------------------------------------------------------
+    # prefill (indexing.py:548-611)
+    # ------------------------------------------------------------------------
+    def prefill_update_kv_cache(self, query_states, key_states, value_states, layer_idx, start_bdx):
+        bsz, seq_len, _, _ = key_states.shape
+        if bsz != 1:
+            raise ValueError("IMI cache currently supports batch_size=1 for prefilling.")
+        valid_start = self.valid_start_list[start_bdx]
+        if self.build_index_when_prefilling:
+            middle_start = valid_start + self.static_pattern_start
+            middle_end = seq_len - self.static_pattern_end
+            if middle_end - middle_start <= 0:
+                raise ValueError("IMI cache requires a non-empty middle segment.")
+            if not self.layer_started[layer_idx]:
+                pipe = self.imi_pipelines[layer_idx]
+                pipe.start_index_chunked(key_states, value_states, middle_start, middle_end, 0)
+                self.index[layer_idx] = pipe.index
+                self.list_keys[layer_idx] = pipe.index.list_keys.unsqueeze(0)
+                self.list_values[layer_idx] = pipe.index.list_values.unsqueeze(0)
+                self.layer_started[layer_idx] = True
+            end = start_bdx + bsz
+            sp = self.static_pattern_start
+            zk, zv = self.steady_zone_keys[layer_idx], self.steady_zone_values[layer_idx]
+            zk[start_bdx:end, :, :sp] = key_states[:, valid_start:valid_start + sp].transpose(1, 2)
+            zv[start_bdx:end, :, :sp] = value_states[:, valid_start:valid_start + sp].transpose(1, 2)
+            zk[start_bdx:end, :, sp:self.static_pattern_total] = \
+                key_states[:, seq_len - self.static_pattern_end:seq_len].transpose(1, 2)
+            zv[start_bdx:end, :, sp:self.static_pattern_total] = \
+                value_states[:, seq_len - self.static_pattern_end:seq_len].transpose(1, 2)
+        else:
+            end = start_bdx + bsz
+            self.steady_zone_keys[layer_idx][start_bdx:end, :, :seq_len].copy_(key_states.transpose(1, 2))
+            self.steady_zone_values[layer_idx][start_bdx:end, :, :seq_len].copy_(value_states.transpose(1, 2))
+        if layer_idx == self.layer_num - 1 and start_bdx + bsz == self.batch_size:
+            self.context += seq_len
+            if self.build_index_when_prefilling:
+                self.attn_func = self.sparse_attention
+            else:
+                self.static_pattern_total = seq_len
+        return key_states[:, valid_start:, :, :], value_states[:, valid_start:, :, :]
+
+    def sync(self, layer_idx, start_bdx):
+        return None
+
+    def capture_cuda_graph(self):
+        return None
+
+    def ensure_layer_ready(self, layer_idx: int) -> None:
+        """The device build is stream-ordered before decode; only metadata checks remain."""
+        if self.layer_ready[layer_idx] or not self.build_index_when_prefilling:
+            return
+        if not self.layer_started[layer_idx]:
+            raise RuntimeError(f"IMI layer {layer_idx} not started")
+        self.layer_ready[layer_idx] = True
+
+    # ------------------------------------------------------------------------
+    # decode buffers (runtime.py:11-377)
+    # ------------------------------------------------------------------------
+    def prepare_cache(self, skip_prefetch: bool = False):
+        if not self.build_index_when_prefilling:
+            return
+        if self.cache_prepared:
+            return
+        bg, G = self.batch_groups, self.group_size
+        for dev in self.device_list:
+            rows = torch.zeros((bg, self.execution_stride), dtype=torch.int32, device=dev)
+            rc = torch.zeros((bg,), dtype=torch.int32, device=dev)
+            self._dec[dev] = dict(
+                rows=rows, row_count=rc,
+                sel=torch.zeros((bg, self.nprobe), dtype=torch.int32, device=dev),
+                sel_count=torch.zeros((bg,), dtype=torch.int32, device=dev),
+                kept=torch.zeros((bg,), dtype=torch.int32, device=dev),
+                part_o=torch.empty((bg, self.splits, G, self.head_dim), dtype=torch.float32, device=dev),
+                part_ml=torch.empty((bg, self.splits, G, 2), dtype=torch.float32, device=dev),
+            )
+            self.execution_buffer_keys_dict[dev] = rows
+            self.execution_buffer_values_dict[dev] = rows
+            self.valid_lengths_dict[dev] = rc
+        for ldx in range(self.layer_num):
+            self.ensure_layer_ready(ldx)
+            if self.async_update_enabled:
+                self._init_async(ldx)
+        self.attn_func = self.sparse_attention
+        self.cache_prepared = True
+
+    def _init_async(self, ldx: int) -> None:
+        idx = self.index[ldx]
+        if idx is None:
+            return
+        dev = idx.centroids.device
+        bg, ns, D, R = self.batch_groups, idx.n_slots, self.head_dim, self.async_update_delta_tokens
+        self._async[ldx] = dict(
+            live=idx.centroids, shadow=idx.centroids.clone(),
+            shadow_dirty=torch.zeros((bg, ns), dtype=torch.uint8, device=dev),
+            pending=torch.zeros((bg, ns), dtype=torch.uint8, device=dev),
+            live_dirty=torch.zeros((bg, ns), dtype=torch.uint8, device=dev),
+            counts=idx.cell_sizes.clone(),
+            delta_counts=torch.zeros((bg, ns), dtype=torch.int32, device=dev),
+            delta_sums=torch.zeros((bg, ns, D), dtype=torch.float32, device=dev),
+            batch_keys=torch.zeros((bg, self.async_update_batch, D), dtype=self.dtype, device=dev),
+            batch_values=torch.zeros((bg, self.async_update_batch, D), dtype=self.dtype, device=dev),
+            ring_keys=torch.zeros((bg, R, D), dtype=self.dtype, device=dev),
+            ring_values=torch.zeros((bg, R, D), dtype=self.dtype, device=dev),
+            ring_ids=torch.full((bg, R), self.padding_cluster_id, dtype=torch.int32, device=dev),
+            ring_pos=torch.zeros((bg,), dtype=torch.int32, device=dev),
+            ring_count=torch.zeros((bg,), dtype=torch.int32, device=dev),
+            count=0, pending_flag=False,
+        )
+
+    # ------------------------------------------------------------------------
+    # decode (runtime.py:378-392, async_update.py:77-162)
+    # ------------------------------------------------------------------------
+    def decode_update_kv_cache(self, key_states, value_states, layer_idx):
+        """key_states/value_states: [B, 1, kv_heads, D]."""
+        st = self._async[layer_idx] if self.async_update_enabled else None
+        nk = key_states[:, 0].reshape(self.batch_groups, self.head_dim)
+        nv = value_states[:, 0].reshape(self.batch_groups, self.head_dim)
+        zk = self.steady_zone_keys[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        zv = self.steady_zone_values[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        if st is not None:
+            ops.decode_append(new_keys=nk, new_values=nv, zone_keys=zk, zone_values=zv, pos=self.static_pattern_total,
+                              batch_keys=st["batch_keys"], batch_values=st["batch_values"], batch_slot=st["count"])
+            st["count"] += 1
+            if st["count"] >= self.async_update_batch:
+                ops.async_assign(index=self.index[layer_idx], batch=st["count"], batch_keys=st["batch_keys"],
+                                 batch_values=st["batch_values"], shadow=st["shadow"],
+                                 shadow_dirty=st["shadow_dirty"], pending=st["pending"], counts=st["counts"],
+                                 delta_counts=st["delta_counts"], delta_sums=st["delta_sums"],
+                                 ring_keys=st["ring_keys"], ring_values=st["ring_values"],
+                                 ring_cell_ids=st["ring_ids"], ring_write_pos=st["ring_pos"],
+                                 ring_count=st["ring_count"], threshold=self.async_update_threshold)
+                st["count"] = 0
+                st["pending_flag"] = "scheduled"
+        else:
+            ops.decode_append(new_keys=nk, new_values=nv, zone_keys=zk, zone_values=zv, pos=self.static_pattern_total)
+        if layer_idx == self.layer_num - 1:
+            self.context += 1
+            self.static_pattern_total += 1
+        return None, None
+
+    def _apply_async_centroid_updates(self, layer_idx: int) -> None:
+        """Publish the shadow centroids updated by an earlier decode step
+        (async_update.py:7-19).  An update scheduled at step t becomes visible at
+        the layer's next visit after that step's attention."""
+        st = self._async[layer_idx]
+        if st is None:
+            return
+        if st["pending_flag"] == "ready":
+            ops.apply_updates(shadow=st["shadow"], live=st["live"], pending=st["pending"],
+                              live_dirty=st["live_dirty"])
+            st["pending_flag"] = False
+
+    def sparse_attention(self, queries, layer_idx, static_len):
+        self.ensure_layer_ready(layer_idx)
+        dev = self.layer_mapping[str(layer_idx)]
+        if self.async_update_enabled:
+            self._apply_async_centroid_updates(layer_idx)
+        idx = self.index[layer_idx]
+        buf = self._dec[dev]
+        q = queries.reshape(self.batch_groups, self.group_size, self.head_dim)
+        if not q.is_contiguous():
+            q = q.contiguous()
+        st = self._async[layer_idx] if self.async_update_enabled else None
+        rc = buf["row_count"]
+        if self.row_count_log is not None and self._log_pos < self.row_count_log.shape[0]:
+            rc = self.row_count_log[self._log_pos]
+            self._log_pos += 1
+        ops.select_cells(q=q, index=idx, nprobe=self.nprobe, max_tokens=self.max_retrieval_tokens,
+                         buffer_pages=self.buffer_size, page_size=self.page_size, padding_id=self.padding_cluster_id,
+                         static_len=int(static_len), exec_capacity=self.execution_stride, sel_cells=buf["sel"],
+                         sel_count=buf["sel_count"], row_index=buf["rows"], row_count=rc,
+                         kept_count=buf["kept"],
+                         centroids=st["live"] if st is not None else None,
+                         cell_dirty=st["live_dirty"] if st is not None else None,
+                         delta_cell_ids=st["ring_ids"] if st is not None else None,
+                         delta_count=st["ring_count"] if st is not None else None)
+        out = torch.empty((self.batch_groups, self.group_size, self.head_dim), dtype=self.dtype, device=q.device)
+        zk = self.steady_zone_keys[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        zv = self.steady_zone_values[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        ev = None
+        if self.attn_event_log is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        ops.sparse_attention(q=q, row_index=buf["rows"], row_count=rc, list_keys=idx.list_keys,
+                             list_values=idx.list_values, static_keys=zk, static_values=zv, out=out,
+                             part_o=buf["part_o"], part_ml=buf["part_ml"], splits=self.splits,
+                             delta_keys=st["ring_keys"] if st is not None else None,
+                             delta_values=st["ring_values"] if st is not None else None)
+        if ev is not None:
+            ev[1].record()
+            self.attn_event_log.append(ev)
+        if st is not None and st["pending_flag"] == "scheduled":
+            st["pending_flag"] = "ready"
+        return out.view(self.batch_size, 1, self.num_heads, self.head_dim)
+
+    def dense_attention(self, queries, layer_idx, static_len):
+        """Attention over the first ``static_len`` steady-zone rows (runtime.py:393-403)."""
+        dev = queries.device
+        bg, G, D = self.batch_groups, self.group_size, self.head_dim
+        n = int(static_len) if not torch.is_tensor(static_len) else int(static_len.max())
+        rows = torch.arange(n, dtype=torch.int32, device=dev).bitwise_or_(1 << 30).expand(bg, n).contiguous()
+        rc = torch.full((bg,), n, dtype=torch.int32, device=dev)
+        q = queries.reshape(bg, G, D).contiguous()
+        out = torch.empty((bg, G, D), dtype=self.dtype, device=dev)
+        splits = ops.default_splits(bg, n)
+        zk = self.steady_zone_keys[layer_idx].view(bg, self.static_capacity, D)
+        zv = self.steady_zone_values[layer_idx].view(bg, self.static_capacity, D)
+        ops.sparse_attention(q=q, row_index=rows, row_count=rc, list_keys=zk, list_values=zv, static_keys=zk,
+                             static_values=zv, out=out,
+                             part_o=torch.empty((bg, splits, G, D), dtype=torch.float32, device=dev),
+                             part_ml=torch.empty((bg, splits, G, 2), dtype=torch.float32, device=dev), splits=splits)
+        return out.view(self.batch_size, 1, self.num_heads, self.head_dim)
+
+    # ------------------------------------------------------------------------
+    # lifecycle (cache.py:380-454, indexing.py:453-542)
+    # ------------------------------------------------------------------------
+    def can_reuse_for_next_sequence(self, valid_start, max_new_length: int, input_length: int) -> bool:
+        new_list_stride = max(int(input_length) - self.static_pattern_start - self.static_pattern_end, 0)
+        if new_list_stride > self.list_capacity:
+            return False
+        new_static = self.static_pattern_start + self.static_pattern_end + int(max_new_length) - 1
+        if new_static > self.static_capacity:
+            return False
+        return len(valid_start) == len(self.valid_start_list)
+
+    def reset_for_next_sequence(self, valid_start, max_new_length: int, input_length: int) -> None:
+        if not self.can_reuse_for_next_sequence(valid_start, max_new_length, input_length):
+            raise ValueError("AdaptiveIMI cache shape mismatch; cannot reuse across samples")
+        self.valid_start_list = valid_start
+        self.input_length = int(input_length)
+        self.actual_gen_len = int(max_new_length) - 1
+        self.list_stride = max(self.input_length - self.static_pattern_start - self.static_pattern_end, 0)
+        self.static_pattern_total = self.static_pattern_start + self.static_pattern_end
+        self.context = 0
+        self.attn_func = self.dense_attention
+        self.layer_ready = [False] * self.layer_num
+        self.layer_started = [False] * self.layer_num
+        self.cache_prepared = False
+        self._async = [None] * self.layer_num
+
+    def cleanup(self) -> None:
+        for p in self.imi_pipelines:
+            if p is not None:
+                p.close()
+        self.index = [None] * self.layer_num
+        self.list_keys = [None] * self.layer_num
+        self.list_values = [None] * self.layer_num
+        self._async = [None] * self.layer_num
+        self._dec.clear()

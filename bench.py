@@ -1,0 +1,486 @@
+"""Benchmark of the IMI KV-cache path on B200.
+
+Workload (Llama-3-8B attention geometry, synthetic): 32 layers, 32 query / 8 KV
+heads, head_dim 128, bf16, batch 1, 131072-token context.  Keys per layer and
+head come from a 64-component Gaussian mixture (std 0.3) with RoPE
+(theta 500000); values N(0, 1).  IMI with subspace_parts=2 (adaptive k = 90),
+retrieval_budget 0.1, k-means settings of the reference's Llama config
+(max_iters 20, early stop min iter 20, tol / rel tol 5e-4), decode-time cell
+assignment on (batch 16, threshold 16, 512 delta tokens).
+
+A step is one decode step through all layers: per layer the new token is
+appended (``decode_update_kv_cache``) and attention runs through
+``imi_decode_attn`` (cell scoring, selection, gather attention).  The metric is
+microseconds per layer per step (lower is better).  ``value`` runs with the
+step inputs resident in HBM; ``e2e`` runs the same API with the inputs in
+pinned host memory, copied in every step, and every layer's attention output
+copied back.  The working set per step (about 1.7 GB of K/V rows) is larger
+than L2, so no explicit flush is needed.
+
+Under torchrun (N > 1) the KV heads are sharded over the ranks (no collective
+on the data path); the reported time is the max over ranks.
+
+``--impl reference`` times the reference's own CPU code for the path on the
+host cores: the index build (imi::kmeans_execute + reorganize_from_kmeans,
+compiled from the reference sources into oracle/_ref) and the decode selection
+(the reference's torch top-k rule + AdpIMI_Index.batch_access) with a CPU
+restatement of the scorer and attention, on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "sparse_decode_us_per_layer_step@128K"
+UNIT = "us/layer/step"
+CFG = dict(model="Llama-3-8B-geometry", layers=32, q_heads=32, kv_heads=8, head_dim=128, context=131072,
+           subspace_parts=2, retrieval_budget=0.1, static_start=32, static_end=64, buffer_cluster_num=32,
+           max_new_length=257, theta=500000.0, components=64)
+KMEANS = {"max_iters": 20, "tol": 0.0005, "early_stop_min_iter": 20, "early_stop_rel_tol": 0.0005}
+ASYNC = {"enabled": True, "batch": 16, "threshold": 16, "delta_tokens": 512}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap,utilization.gpu",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[2:6], float(parts[6])))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        loaded = [r for r in rows if r[3] > 0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[2]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ----------------------------------------------------------------------------
+# our implementation
+# ----------------------------------------------------------------------------
+def make_inputs(layers, heads_local, head0, G, ctx, steps, dev, seed=0):
+    """Per-layer prefill K/V generator and per-step decode inputs (device)."""
+    from adaptiveimi_b200.synthetic import mixture_keys, rope
+
+    D = CFG["head_dim"]
+    kvh = CFG["kv_heads"]
+
+    def layer_kv(l):
+        k, means = mixture_keys(kvh, ctx, D, CFG["components"], seed + 1000 * l, CFG["theta"], device=dev)
+        g = torch.Generator(device=dev).manual_seed(seed + 1000 * l + 7)
+        v = torch.randn(kvh, ctx, D, generator=g, device=dev)
+        sl = slice(head0, head0 + heads_local)
+        return k[sl].to(torch.bfloat16), v[sl].to(torch.bfloat16), means[sl]
+
+    return layer_kv
+
+
+def decode_inputs(means_per_layer, G, ctx, steps, dev, seed=0):
+    """q [steps, L, 1, 1, H, D], k/v [steps, L, 1, 1, kv, D] (bf16, device)."""
+    from adaptiveimi_b200.synthetic import rope
+
+    L = len(means_per_layer)
+    kvh, D = means_per_layer[0].shape[0], means_per_layer[0].shape[2]
+    g = torch.Generator(device=dev).manual_seed(seed + 99)
+    qs, ks, vs = [], [], []
+    for l in range(L):
+        m = means_per_layer[l]
+        C = m.shape[1]
+        comp = torch.randint(0, C, (steps, kvh, G + 1), generator=g, device=dev)
+        x = torch.gather(m.unsqueeze(0).expand(steps, -1, -1, -1), 2,
+                         comp[..., None].expand(-1, -1, -1, D)) + 0.3 * torch.randn(steps, kvh, G + 1, D,
+                                                                                   generator=g, device=dev)
+        pos = torch.arange(ctx, ctx + steps, device=dev)
+        x = rope(x.permute(1, 2, 0, 3), pos, CFG["theta"]).permute(2, 0, 1, 3)  # [steps, kv, G+1, D]
+        qs.append(x[:, :, :G].reshape(steps, 1, 1, kvh * G, D))
+        ks.append(x[:, :, G].reshape(steps, 1, 1, kvh, D))
+        vs.append(torch.randn(steps, 1, 1, kvh, D, generator=g, device=dev))
+    st = lambda a: torch.stack(a, 1).to(torch.bfloat16).contiguous()  # noqa: E731
+    return st(qs), st(ks), st(vs)
+
+
+def run_ours(args):
+    from adaptiveimi_b200.attn import imi_decode_attn
+    from adaptiveimi_b200.cache import adpimi_cache
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", init_method="env://")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L, ctx, kvh, G = args.layers, args.context, CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"]
+    if kvh % ws != 0:
+        raise SystemExit(f"{kvh} KV heads do not shard over {ws} GPUs")
+    hl = kvh // ws
+    head0 = rank * hl
+    steps_total = args.steps + args.warmup
+    cache = adpimi_cache(
+        valid_start=[0], layer_num=L, batch_size=1, max_length=ctx + CFG["max_new_length"], num_key_value_heads=hl,
+        num_heads=hl * G, head_dim=CFG["head_dim"], dtype=torch.bfloat16,
+        layer_mapping={str(i): f"cuda:{local}" for i in range(L)}, max_new_length=CFG["max_new_length"],
+        input_length=ctx, static_pattern_start=CFG["static_start"], static_pattern_end=CFG["static_end"],
+        core=os.cpu_count() or 1, pages_per_cluster=2, retrieval_budget=CFG["retrieval_budget"], cache_ratio=0.05,
+        buffer_cluster_num=CFG["buffer_cluster_num"], prefill_bsz=1, num_gpus=1, model_size=8,
+        subspace_parts=CFG["subspace_parts"], runtime_config={"kmeans": KMEANS, "async_update": ASYNC})
+    # ---- prefill: device index build of every layer (timed for the build metric)
+    layer_kv = make_inputs(L, hl, head0, G, ctx, steps_total, dev)
+    means = []
+    build_ms = 0.0
+    for l in range(L):
+        k, v, m = layer_kv(l)
+        means.append(m)
+        ks = k.transpose(0, 1).unsqueeze(0)  # [1, ctx, kv, D] strided view (model layout)
+        vs = v.transpose(0, 1).unsqueeze(0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        cache.prefill_update_kv_cache(None, ks, vs, l, 0)
+        e1.record()
+        torch.cuda.synchronize()
+        build_ms += e0.elapsed_time(e1)
+        del k, v, ks, vs
+    torch.cuda.empty_cache()
+    cache.prepare_cache()
+    n_mid = cache.list_stride
+    n_active = [int(cache.index[l].n_active.max()) for l in range(L)]
+    qd, kd, vd = decode_inputs(means, G, ctx, steps_total, dev)
+
+    def step(t, q_src, k_src, v_src, out_sink=None):
+        for l in range(L):
+            cache.decode_update_kv_cache(k_src[l], v_src[l], l)
+            o = imi_decode_attn(q_src[l], None, None, l, cache)
+            if out_sink is not None:
+                out_sink[l].copy_(o, non_blocking=True)
+
+    # ---- warmup (device inputs)
+    for t in range(args.warmup):
+        step(t, qd[t], kd[t], vd[t])
+    torch.cuda.synchronize()
+    # ---- timed region: device-resident inputs
+    cache.row_count_log = torch.zeros((args.steps * L, hl), dtype=torch.int32, device=dev)
+    cache._log_pos = 0
+    cache.attn_event_log = []
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for t in range(args.steps):
+            step(args.warmup + t, qd[args.warmup + t], kd[args.warmup + t], vd[args.warmup + t])
+        e1.record()
+        torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    dev_ms = e0.elapsed_time(e1)
+    attn_ms = [a.elapsed_time(b) for a, b in cache.attn_event_log]
+    rows = cache.row_count_log.to(torch.int64).sum().item()
+    cache.row_count_log = None
+    cache.attn_event_log = None
+    # ---- e2e: pinned host inputs copied in, outputs copied out, every step
+    # (the cache has capacity for warmup + steps appended tokens; e2e reuses the
+    # last `e2e_steps` positions after a reset of the appended-token counter)
+    e2e_steps = min(args.steps, 8)
+    qh = qd[:e2e_steps].cpu().pin_memory()
+    kh = kd[:e2e_steps].cpu().pin_memory()
+    vh = vd[:e2e_steps].cpu().pin_memory()
+    outs_h = torch.empty((e2e_steps, L, 1, 1, hl * G, CFG["head_dim"]), dtype=torch.bfloat16).pin_memory()
+    qb, kb, vb = torch.empty_like(qd[0]), torch.empty_like(kd[0]), torch.empty_like(vd[0])
+    cache.static_pattern_total -= e2e_steps  # re-use appended positions (same shapes, same work)
+    cache.context -= e2e_steps
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for t in range(e2e_steps):
+        qb.copy_(qh[t], non_blocking=True)
+        kb.copy_(kh[t], non_blocking=True)
+        vb.copy_(vh[t], non_blocking=True)
+        step(t, qb, kb, vb, out_sink=outs_h[t])
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    # ---- max over ranks
+    vals = torch.tensor([dev_ms, e2e_ms, sum(attn_ms), build_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, e2e_ms, attn_total_ms, build_ms_max = vals.tolist()
+    if rank != 0:
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return None
+    us_per_layer_step = dev_ms * 1e3 / (args.steps * L)
+    e2e_us = e2e_ms * 1e3 / (e2e_steps * L)
+    hbm, src = peaks()
+    # algorithmic bytes of the attention launches (this rank): K and V rows
+    # (512 B each), their row indices (4 B), q and out, the split partials
+    # written and read back by the combine kernel.
+    n_launch = max(1, len(attn_ms))
+    part_bytes = hl * cache.splits * G * (128 + 2) * 4 * 2
+    algo = rows * (512 + 4) + n_launch * (hl * G * 128 * 2 * 2 + part_bytes)
+    attn_avg_s = (sum(attn_ms) / n_launch) * 1e-3
+    achieved = (algo / n_launch) / attn_avg_s / 1e9 if attn_avg_s > 0 else 0.0
+    keys_built = L * kvh * n_mid
+    res = {
+        "metric": METRIC, "value": round(us_per_layer_step, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (Gaussian-mixture keys + RoPE, N(0,1) values; seeded)",
+        "config": {"workload": "BASELINE configs[1]: Llama-3-8B geometry, 128K context, 32 layers, IMI S=2, "
+                               "budget 0.1, async cell assignment on", "context": ctx, "layers": L,
+                   "kv_heads": kvh, "q_heads": CFG["q_heads"], "head_dim": 128, "global_batch": 1,
+                   "parallelism": f"kv-head shard x{ws}" if ws > 1 else "single GPU",
+                   "l2": "working set per step > L2 (no flush needed)",
+                   "n_slots": cache.n_centroids, "nprobe": cache.nprobe, "budget_tokens": cache.max_retrieval_tokens,
+                   "max_active_cells": max(n_active), "splits": cache.splits},
+        "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": int(L * (qh[0, 0].numel() +
+                                                                                        2 * kh[0, 0].numel()) * 2),
+                "d2h_bytes_per_step": int(L * outs_h[0, 0].numel() * 2), "steps": e2e_steps},
+        "roofline": {"kernel": "imi_attn_kernel + imi_combine_kernel", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "traffic": None,
+                     "algorithmic_bytes_per_launch": int(algo / n_launch),
+                     "avg_launch_us": round(attn_avg_s * 1e6, 3)},
+        "build": {"metric": "IMI build Mkeys/s", "value": round(keys_built / (build_ms_max * 1e-3) / 1e6, 3),
+                  "unit": "Mkeys/s", "build_ms_total": round(build_ms_max, 2), "keys": keys_built,
+                  "kmeans": KMEANS},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+    # our kernels per layer-step: append + select + attention + combine, plus
+    # the async assignment every 16 steps and the centroid publish after it
+    res["gpu_launches"] = int(args.steps * L * 4 + (args.steps // ASYNC["batch"]) * L * 2)
+    if ws == 1 and not args.no_cpu_baseline:
+        try:
+            res["cpu_baseline"] = cpu_baseline(args, sample_layers=1, sample_steps=2)
+        except Exception as exc:  # reported, not fatal
+            res["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    return res
+
+
+# ----------------------------------------------------------------------------
+# reference CPU path (bounded sample)
+# ----------------------------------------------------------------------------
+def _ref_modules():
+    ref_dir = ROOT / "oracle" / "_ref"
+    if not any(ref_dir.glob("imi_ref*.so")):
+        return None
+    sys.path.insert(0, str(ref_dir))
+    import AdpIMI_Index  # noqa: E402
+    import imi_ref  # noqa: E402
+    return imi_ref, AdpIMI_Index
+
+
+def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
+    """The reference's CPU path on a bounded sample: build of `build_heads` heads
+    of one 128K layer with every host thread, and `sample_steps` decode steps of
+    `sample_layers` layers (8 KV heads)."""
+    import numpy as np
+
+    from adaptiveimi_b200.sizing import RetrievalSizes, adaptive_k
+    from adaptiveimi_b200.synthetic import mixture_keys
+    from oracle import oracle as O
+
+    mods = _ref_modules()
+    kind = "reference" if mods is not None else "port"
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    ctx = args.context
+    D = 128
+    kvh, G = CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"]
+    k, means = mixture_keys(kvh, ctx, D, CFG["components"], 0, CFG["theta"])
+    g = torch.Generator().manual_seed(7)
+    v = torch.randn(kvh, ctx, D, generator=g)
+    k, v = k.to(torch.bfloat16), v.to(torch.bfloat16)
+    mid_k = k[:, 32:ctx - 64].contiguous()
+    mid_v = v[:, 32:ctx - 64].contiguous()
+    n = mid_k.shape[1]
+    ks = adaptive_k(n, 2)
+    # ---- build sample
+    t0 = time.perf_counter()
+    if mods is not None:
+        r = mods[0].build(mid_k[:build_heads].contiguous(), mid_v[:build_heads].contiguous(), 2, list(ks),
+                          KMEANS["max_iters"], KMEANS["tol"], KMEANS["early_stop_min_iter"],
+                          KMEANS["early_stop_rel_tol"], cores)
+    else:
+        kb, vb = O.bf16_bits(mid_k), O.bf16_bits(mid_v)
+        for h in range(build_heads):
+            O.build_head(kb[h], vb[h], 2, ks, KMEANS["max_iters"], KMEANS["tol"], KMEANS["early_stop_min_iter"],
+                         KMEANS["early_stop_rel_tol"])
+    build_s = time.perf_counter() - t0
+    build_mkeys = build_heads * n / build_s / 1e6
+    # ---- decode sample: one layer's index for all heads, built on the GPU
+    # box's CPU would take minutes; the sample uses the GPU-independent oracle
+    # index of `build_heads` heads tiled to 8 groups (selection work per group is
+    # what is timed, and it does not depend on which head's index it scans)
+    sizes = RetrievalSizes.from_capacity(n, 2, CFG["retrieval_budget"], CFG["buffer_cluster_num"], 96 + 256)
+    if mods is not None:
+        sizes_t = torch.zeros(kvh, sizes.n_centroids, dtype=torch.int32)
+        offs_t = torch.zeros(kvh, sizes.n_centroids + 1, dtype=torch.int32)
+        cents = torch.zeros(kvh, sizes.n_centroids, D)
+        lk = torch.zeros(kvh, n, D, dtype=torch.bfloat16)
+        lv = torch.zeros_like(lk)
+        for h in range(kvh):
+            src = h % build_heads
+            c = int(r["cluster_counts"][src])
+            sizes_t[h, :c] = r["cluster_sizes"][src, :c]
+            offs_t[h, :c + 1] = r["cluster_offsets"][src, :c + 1]
+            offs_t[h, c + 1:] = r["cluster_offsets"][src, c]
+            cents[h, :c] = r["centroids"][src, :c]
+            lk[h] = r["list_keys"][src]
+            lv[h] = r["list_values"][src]
+    else:
+        raise RuntimeError("decode CPU baseline needs oracle/_ref")
+    mask = (sizes_t == 0)
+    pool = mods[1].AdpIMI_ThreadPool(cores)
+    z = lambda *s: torch.zeros(*s, dtype=torch.int32)  # noqa: E731
+    bp = sizes.buffer_size
+    q = torch.randn(kvh, G, D).to(torch.bfloat16)
+    qb = O.bf16_bits(q)
+    t0 = time.perf_counter()
+    for _ in range(sample_steps * sample_layers):
+        # scorer (compute_impl.cu:62-103 restated in C)
+        sims = torch.from_numpy(np.stack([O.scores(qb[h], cents[h].numpy(), mask[h].numpy().astype(np.uint8))
+                                          for h in range(kvh)]))
+        # the reference's selection (retrieval.py:295-303)
+        topk = torch.topk(sims, sizes.nprobe, dim=-1, largest=True, sorted=True)
+        szs = torch.gather(sizes_t, 1, topk.indices)
+        cum = torch.cumsum(szs, dim=-1, dtype=torch.int32)
+        keep = (szs > 0) & ((cum - szs) < sizes.max_retrieval_tokens)
+        sel = topk.indices.masked_fill(~keep, sizes.padding_cluster_id)
+        # the reference's page truncation (AdpIMI_Index.batch_access)
+        bufs = [z(kvh, bp) for _ in range(3)] + [z(kvh)] + [z(kvh, bp) for _ in range(3)] + [z(kvh)] + \
+               [z(kvh, bp) for _ in range(3)] + [z(kvh)]
+        idx = mods[1].AdpIMI_Index(1, kvh, D, sizes.nprobe, 0, 8, sizes.n_centroids, bp, 1, cores, pool.get())
+        idx.set_indices(*bufs, sel.clone())
+        ph = torch.empty(kvh, 0, D, dtype=torch.bfloat16)
+        idx.set_kv(ph.unsqueeze(0), ph.unsqueeze(0), ph, ph)
+        idx.set_cluster_metadata(sizes_t, offs_t, 0)
+        idx.batch_access()
+        idx.sync()
+        # gather + attention on the CPU (fp32)
+        miss_ids, miss_sizes, miss_num = bufs[4], bufs[5], bufs[7]
+        for h in range(kvh):
+            segs = [torch.arange(int(miss_ids[h, j]), int(miss_ids[h, j]) + int(miss_sizes[h, j]))
+                    for j in range(int(miss_num[h]))]
+            ridx = torch.cat(segs) if segs else torch.zeros(0, dtype=torch.int64)
+            kr = lk[h, ridx].float()
+            vr = lv[h, ridx].float()
+            s = (q[h].float() @ kr.T) / math.sqrt(D)
+            torch.softmax(s, -1) @ vr
+    dec_s = time.perf_counter() - t0
+    us = dec_s * 1e6 / (sample_steps * sample_layers)
+    return {"value": round(us, 1), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"decode: {sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, 128K context; "
+                      f"build: {build_heads} heads x {n} keys, k={ks[0]}x{ks[1]}, {KMEANS['max_iters']} iters",
+            "build": {"value": round(build_mkeys, 4), "unit": "Mkeys/s", "seconds": round(build_s, 2)}}
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    warm = max(0, min(args.warmup, 1))
+    steps = max(1, min(args.steps, 3))
+    cb = cpu_baseline(args, sample_layers=1, sample_steps=steps + warm)
+    res = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": ws,
+        "steps": steps, "warmup": warm, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (same generator)",
+        "config": {"workload": "BASELINE configs[1] (bounded CPU sample)", "context": args.context},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "build": cb["build"],
+    }
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=CFG["layers"])
+    ap.add_argument("--context", type=int, default=CFG["context"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.steps + args.warmup + 8 > CFG["max_new_length"] - 1:
+        raise SystemExit("steps + warmup exceed the decode capacity (256 tokens)")
+    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -226,11 +226,13 @@ def test_attention_matches_oracle(splits):
 
 
 def test_attention_dense_equivalence_full_budget():
-    """budget 1.0 -> every token is attended: equals dense softmax attention."""
+    """budget 1.0 and a page buffer large enough that the reference's page
+    truncation (ceil(size/8) pages per cell against buffer_size) drops nothing:
+    every token is attended, so the result equals dense softmax attention."""
     K, V, Q, k, v = _build_cfg0(heads=2, ctx=2048)
     heads, G = 2, 4
     n = k.shape[1]
-    sizes = RetrievalSizes.from_capacity(n, 2, 1.0, 32, static_capacity=96 + 1)
+    sizes = RetrievalSizes.from_capacity(n, 2, 1.0, 4096, static_capacity=96 + 1)
     idx = _gpu_build(k, v, 2, (16, 16), 4, sizes.n_centroids)
     static_len = 96
     zk, zv = _zone(K, V, heads, static_len, 97)
