@@ -58,7 +58,7 @@ class AttnDesc(ctypes.Structure):
         ("list_keys", P), ("list_values", P), ("list_rows", i64),
         ("static_keys", P), ("static_values", P), ("static_rows", i64),
         ("delta_keys", P), ("delta_values", P), ("delta_rows", i64),
-        ("part_o", P), ("part_ml", P), ("out", P),
+        ("part_o", P), ("part_ml", P), ("out", P), ("counters", P),
     ]
 
 
@@ -81,7 +81,7 @@ class AsyncDesc(ctypes.Structure):
         ("batch_keys", P), ("batch_values", P), ("sub_centroids", P), ("cell_code", P),
         ("shadow", P), ("shadow_dirty", P), ("pending", P), ("counts", P), ("delta_counts", P), ("delta_sums", P),
         ("ring_keys", P), ("ring_values", P), ("ring_cell_ids", P), ("ring_write_pos", P), ("ring_count", P),
-        ("ids_out", P),
+        ("ids_out", P), ("part_best", P), ("part_chunks", i32),
     ]
 
 
@@ -95,7 +95,7 @@ class ApplyDesc(ctypes.Structure):
 EXPORTS = (
     "imi_abi_version", "imi_last_error", "imi_build_workspace_size", "imi_build_index",
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
-    "imi_async_assign", "imi_apply_updates",
+    "imi_async_assign", "imi_apply_updates", "imi_decode_attend",
 )
 
 _lib = None
@@ -128,6 +128,8 @@ def load():
         L.imi_decode_append.argtypes = [ctypes.POINTER(AppendDesc), P]
         L.imi_async_assign.argtypes = [ctypes.POINTER(AsyncDesc), P]
         L.imi_apply_updates.argtypes = [ctypes.POINTER(ApplyDesc), P]
+        L.imi_decode_attend.argtypes = [ctypes.POINTER(SelectDesc), ctypes.POINTER(AttnDesc),
+                                        ctypes.POINTER(ApplyDesc), P]
         if L.imi_abi_version() != 1:
             raise ImportError("libimi_b200.so ABI version mismatch")
         _lib = L

@@ -233,6 +233,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                 kept=torch.zeros((bg,), dtype=torch.int32, device=dev),
                 part_o=torch.empty((bg, self.splits, G, self.head_dim), dtype=torch.float32, device=dev),
                 part_ml=torch.empty((bg, self.splits, G, 2), dtype=torch.float32, device=dev),
+                counters=torch.zeros((bg,), dtype=torch.int32, device=dev),
             )
             self.execution_buffer_keys_dict[dev] = rows
             self.execution_buffer_values_dict[dev] = rows
@@ -241,8 +242,63 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             self.ensure_layer_ready(ldx)
             if self.async_update_enabled:
                 self._init_async(ldx)
+        self._descs = [self._make_descs(ldx) for ldx in range(self.layer_num)]
         self.attn_func = self.sparse_attention
         self.cache_prepared = True
+
+    def _make_descs(self, ldx: int):
+        """Per-layer C-ABI descriptors with every constant field filled in; the
+        hot path only writes the per-call pointers and lengths."""
+        idx = self.index[ldx]
+        dev = self.layer_mapping[str(ldx)]
+        buf = self._dec[dev]
+        st = self._async[ldx] if self.async_update_enabled else None
+        bg, G, D = self.batch_groups, self.group_size, self.head_dim
+        sel = _lib.SelectDesc()
+        sel.bg, sel.G, sel.dim, sel.n_slots, sel.parts, sel.kmax = bg, G, D, idx.n_slots, idx.parts, idx.kmax
+        sel.ks = ops._ks4(idx.ks)
+        sel.sub_centroids = idx.sub_centroids.data_ptr()
+        sel.cell_code, sel.cell_sizes = idx.cell_code.data_ptr(), idx.cell_sizes.data_ptr()
+        sel.cell_offsets, sel.cell_mask = idx.cell_offsets.data_ptr(), idx.cell_mask.data_ptr()
+        sel.centroids = (st["live"] if st is not None else idx.centroids).data_ptr()
+        sel.cell_dirty = st["live_dirty"].data_ptr() if st is not None else None
+        sel.nprobe, sel.max_tokens, sel.buffer_pages = self.nprobe, self.max_retrieval_tokens, self.buffer_size
+        sel.page_size, sel.padding_id = self.page_size, self.padding_cluster_id
+        sel.delta_cell_ids = st["ring_ids"].data_ptr() if st is not None else None
+        sel.delta_count = st["ring_count"].data_ptr() if st is not None else None
+        sel.delta_capacity = self.async_update_delta_tokens if st is not None else 0
+        sel.exec_capacity = self.execution_stride
+        sel.sel_cells, sel.sel_count, sel.kept_count = buf["sel"].data_ptr(), buf["sel_count"].data_ptr(), \
+            buf["kept"].data_ptr()
+        sel.row_index = buf["rows"].data_ptr()
+        att = _lib.AttnDesc()
+        att.bg, att.G, att.splits, att.exec_capacity = bg, G, self.splits, self.execution_stride
+        att.scale = 1.0 / math.sqrt(D)
+        att.row_index = buf["rows"].data_ptr()
+        att.list_keys, att.list_values, att.list_rows = idx.list_keys.data_ptr(), idx.list_values.data_ptr(), \
+            idx.list_keys.shape[1]
+        zk = self.steady_zone_keys[ldx]
+        att.static_keys, att.static_values = zk.data_ptr(), self.steady_zone_values[ldx].data_ptr()
+        att.static_rows = self.static_capacity
+        if st is not None:
+            att.delta_keys, att.delta_values = st["ring_keys"].data_ptr(), st["ring_values"].data_ptr()
+            att.delta_rows = self.async_update_delta_tokens
+        att.part_o, att.part_ml = buf["part_o"].data_ptr(), buf["part_ml"].data_ptr()
+        att.counters = buf["counters"].data_ptr()
+        app = None
+        if st is not None:
+            app = _lib.ApplyDesc()
+            app.bg, app.n_slots, app.dim = bg, idx.n_slots, D
+            app.shadow, app.live = st["shadow"].data_ptr(), st["live"].data_ptr()
+            app.pending, app.live_dirty = st["pending"].data_ptr(), st["live_dirty"].data_ptr()
+        ap = _lib.AppendDesc()
+        ap.bg, ap.dim = bg, D
+        ap.zone_keys, ap.zone_values, ap.zone_rows = zk.data_ptr(), self.steady_zone_values[ldx].data_ptr(), \
+            self.static_capacity
+        if st is not None:
+            ap.batch_keys, ap.batch_values = st["batch_keys"].data_ptr(), st["batch_values"].data_ptr()
+            ap.batch_cap = self.async_update_batch
+        return dict(sel=sel, att=att, app=app, append=ap)
 
     def _init_async(self, ldx: int) -> None:
         idx = self.index[ldx]
@@ -265,6 +321,8 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             ring_ids=torch.full((bg, R), self.padding_cluster_id, dtype=torch.int32, device=dev),
             ring_pos=torch.zeros((bg,), dtype=torch.int32, device=dev),
             ring_count=torch.zeros((bg,), dtype=torch.int32, device=dev),
+            part_best=torch.empty((bg, ops.async_chunks(ns), self.async_update_batch), dtype=torch.int64,
+                                  device=dev),
             count=0, pending_flag=False,
         )
 
@@ -276,11 +334,25 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         st = self._async[layer_idx] if self.async_update_enabled else None
         nk = key_states[:, 0].reshape(self.batch_groups, self.head_dim)
         nv = value_states[:, 0].reshape(self.batch_groups, self.head_dim)
-        zk = self.steady_zone_keys[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
-        zv = self.steady_zone_values[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        if nk.stride(-1) != 1 or nv.stride(-1) != 1 or nk.stride(0) != nv.stride(0):
+            nk, nv = nk.contiguous(), nv.contiguous()
+        dev = nk.device
+        L = _lib.load()
+        if self.cache_prepared:
+            ap = self._descs[layer_idx]["append"]
+        else:
+            ap = _lib.AppendDesc()
+            ap.bg, ap.dim = self.batch_groups, self.head_dim
+            ap.zone_keys = self.steady_zone_keys[layer_idx].data_ptr()
+            ap.zone_values = self.steady_zone_values[layer_idx].data_ptr()
+            ap.zone_rows = self.static_capacity
+        ap.new_keys, ap.new_values, ap.src_head_stride = nk.data_ptr(), nv.data_ptr(), nk.stride(0)
+        ap.pos = self.static_pattern_total
         if st is not None:
-            ops.decode_append(new_keys=nk, new_values=nv, zone_keys=zk, zone_values=zv, pos=self.static_pattern_total,
-                              batch_keys=st["batch_keys"], batch_values=st["batch_values"], batch_slot=st["count"])
+            ap.batch_slot = st["count"]
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(L.imi_decode_append(ctypes.byref(ap), stream), "imi_decode_append")
+        if st is not None:
             st["count"] += 1
             if st["count"] >= self.async_update_batch:
                 ops.async_assign(index=self.index[layer_idx], batch=st["count"], batch_keys=st["batch_keys"],
@@ -289,11 +361,10 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                                  delta_counts=st["delta_counts"], delta_sums=st["delta_sums"],
                                  ring_keys=st["ring_keys"], ring_values=st["ring_values"],
                                  ring_cell_ids=st["ring_ids"], ring_write_pos=st["ring_pos"],
-                                 ring_count=st["ring_count"], threshold=self.async_update_threshold)
+                                 ring_count=st["ring_count"], threshold=self.async_update_threshold,
+                                 part_best=st["part_best"])
                 st["count"] = 0
                 st["pending_flag"] = "scheduled"
-        else:
-            ops.decode_append(new_keys=nk, new_values=nv, zone_keys=zk, zone_values=zv, pos=self.static_pattern_total)
         if layer_idx == self.layer_num - 1:
             self.context += 1
             self.static_pattern_total += 1
@@ -312,41 +383,39 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             st["pending_flag"] = False
 
     def sparse_attention(self, queries, layer_idx, static_len):
-        self.ensure_layer_ready(layer_idx)
+        """retrieval.py:320-602: cell scores, selection under the token budget and
+        page truncation, and attention over [steady zone | selected rows | delta
+        rows], as one C-ABI call (imi_decode_attend)."""
+        if not self.layer_ready[layer_idx]:
+            self.ensure_layer_ready(layer_idx)
         dev = self.layer_mapping[str(layer_idx)]
-        if self.async_update_enabled:
-            self._apply_async_centroid_updates(layer_idx)
-        idx = self.index[layer_idx]
-        buf = self._dec[dev]
         q = queries.reshape(self.batch_groups, self.group_size, self.head_dim)
         if not q.is_contiguous():
             q = q.contiguous()
+        d = self._descs[layer_idx]
+        sel, att = d["sel"], d["att"]
         st = self._async[layer_idx] if self.async_update_enabled else None
-        rc = buf["row_count"]
+        apply = None
+        if st is not None and st["pending_flag"] == "ready":
+            apply = ctypes.byref(d["app"])
+            st["pending_flag"] = False
+        rc = self._dec[dev]["row_count"]
         if self.row_count_log is not None and self._log_pos < self.row_count_log.shape[0]:
             rc = self.row_count_log[self._log_pos]
             self._log_pos += 1
-        ops.select_cells(q=q, index=idx, nprobe=self.nprobe, max_tokens=self.max_retrieval_tokens,
-                         buffer_pages=self.buffer_size, page_size=self.page_size, padding_id=self.padding_cluster_id,
-                         static_len=int(static_len), exec_capacity=self.execution_stride, sel_cells=buf["sel"],
-                         sel_count=buf["sel_count"], row_index=buf["rows"], row_count=rc,
-                         kept_count=buf["kept"],
-                         centroids=st["live"] if st is not None else None,
-                         cell_dirty=st["live_dirty"] if st is not None else None,
-                         delta_cell_ids=st["ring_ids"] if st is not None else None,
-                         delta_count=st["ring_count"] if st is not None else None)
         out = torch.empty((self.batch_groups, self.group_size, self.head_dim), dtype=self.dtype, device=q.device)
-        zk = self.steady_zone_keys[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
-        zv = self.steady_zone_values[layer_idx].view(self.batch_groups, self.static_capacity, self.head_dim)
+        qp, rcp = q.data_ptr(), rc.data_ptr()
+        sel.q = att.q = qp
+        sel.row_count = att.row_count = rcp
+        sel.static_len = int(static_len)
+        att.out = out.data_ptr()
         ev = None
         if self.attn_event_log is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        ops.sparse_attention(q=q, row_index=buf["rows"], row_count=rc, list_keys=idx.list_keys,
-                             list_values=idx.list_values, static_keys=zk, static_values=zv, out=out,
-                             part_o=buf["part_o"], part_ml=buf["part_ml"], splits=self.splits,
-                             delta_keys=st["ring_keys"] if st is not None else None,
-                             delta_values=st["ring_values"] if st is not None else None)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
+        _lib.check(_lib.load().imi_decode_attend(ctypes.byref(sel), ctypes.byref(att), apply, stream),
+                   "imi_decode_attend")
         if ev is not None:
             ev[1].record()
             self.attn_event_log.append(ev)

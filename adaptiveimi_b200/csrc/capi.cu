@@ -65,7 +65,7 @@ int imi_query_group_similarities(const uint16_t* q, const float* centroids, floa
                        "imi_query_group_similarities");
 }
 
-int imi_select_cells(const imi_select_desc* d, void* stream) {
+static int check_select(const imi_select_desc* d) {
     if (!d) return fail(IMI_ERR_INVALID, "imi_select_cells: null descriptor");
     const int Sp = d->parts == 0 ? 1 : d->parts;
     if (!(d->parts == 0 || d->parts == 2 || d->parts == 4) || d->dim != 128)
@@ -87,14 +87,16 @@ int imi_select_cells(const imi_select_desc* d, void* stream) {
     if (table > 8192) return fail(IMI_ERR_INVALID, "imi_select_cells: prefix table (product of the first S-1 k) > 8192");
     if (d->delta_count && (!d->delta_cell_ids || d->delta_capacity <= 0))
         return fail(IMI_ERR_INVALID, "imi_select_cells: delta ring needs ids and capacity");
+    if (d->n_slots > imi::select_max_slots())
+        return fail(IMI_ERR_INVALID, "imi_select_cells: n_slots > " + std::to_string(imi::select_max_slots()));
     const size_t sm = imi::select_smem_bytes(*d);
     if (sm > 227 * 1024)
         return fail(IMI_ERR_INVALID, "imi_select_cells: n_slots too large for the on-chip selection (" +
                                          std::to_string(sm) + " bytes of shared memory)");
-    return cuda_status(imi::launch_select(*d, S(stream)), "imi_select_cells");
+    return IMI_OK;
 }
 
-int imi_sparse_attention(const imi_attn_desc* d, void* stream) {
+static int check_attention(const imi_attn_desc* d) {
     if (!d) return fail(IMI_ERR_INVALID, "imi_sparse_attention: null descriptor");
     if (d->bg <= 0 || d->G <= 0 || d->G > 8 || d->splits <= 0 || d->splits > 4096)
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: need 1 <= G <= 8 and 1 <= splits <= 4096");
@@ -104,7 +106,42 @@ int imi_sparse_attention(const imi_attn_desc* d, void* stream) {
     if (!aligned16(d->list_keys) || !aligned16(d->list_values) || !aligned16(d->static_keys) ||
         !aligned16(d->static_values) || !aligned16(d->q))
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: K/V/q buffers must be 16-byte aligned");
+    if (d->exec_capacity <= 0) return fail(IMI_ERR_INVALID, "imi_sparse_attention: exec_capacity must be positive");
+    if (imi::attn_smem_bytes(*d) > 227 * 1024)
+        return fail(IMI_ERR_INVALID, "imi_sparse_attention: too few splits for the row capacity (raise splits)");
+    return IMI_OK;
+}
+
+int imi_select_cells(const imi_select_desc* d, void* stream) {
+    const int st = check_select(d);
+    if (st != IMI_OK) return st;
+    return cuda_status(imi::launch_select(*d, S(stream)), "imi_select_cells");
+}
+
+int imi_sparse_attention(const imi_attn_desc* d, void* stream) {
+    const int st = check_attention(d);
+    if (st != IMI_OK) return st;
     return cuda_status(imi::launch_attention(*d, S(stream)), "imi_sparse_attention");
+}
+
+int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
+                      void* stream) {
+    int st = check_select(sel);
+    if (st != IMI_OK) return st;
+    st = check_attention(attn);
+    if (st != IMI_OK) return st;
+    if (sel->bg != attn->bg || sel->G != attn->G || sel->row_index != attn->row_index ||
+        sel->row_count != attn->row_count || sel->q != attn->q || sel->exec_capacity != attn->exec_capacity)
+        return fail(IMI_ERR_INVALID, "imi_decode_attend: select and attention descriptors disagree");
+    if (apply) {
+        if (!apply->shadow || !apply->live || !apply->pending || !apply->live_dirty)
+            return fail(IMI_ERR_INVALID, "imi_decode_attend: null pointer in apply descriptor");
+        cudaError_t e = imi::launch_apply(*apply, S(stream));
+        if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
+    }
+    cudaError_t e = imi::launch_select(*sel, S(stream));
+    if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
+    return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");
 }
 
 int imi_decode_append(const imi_append_desc* d, void* stream) {
@@ -126,12 +163,14 @@ int imi_async_assign(const imi_async_desc* d, void* stream) {
         return fail(IMI_ERR_INVALID, "imi_async_assign: null pointer");
     if (d->batch <= 0 || d->batch > d->batch_cap || d->batch > 64 || d->ring_cap <= 0 || d->dim != 128)
         return fail(IMI_ERR_INVALID, "imi_async_assign: bad batch / ring sizes");
+    if (!d->part_best || d->part_chunks != imi::async_chunks(d->n_slots))
+        return fail(IMI_ERR_INVALID, "imi_async_assign: part_best scratch with part_chunks = ceil(n_slots/512) required");
     if (imi::async_smem_bytes(*d) > 227 * 1024) return fail(IMI_ERR_INVALID, "imi_async_assign: batch too large");
     {
         const int Sp = d->parts == 0 ? 1 : d->parts;
         long long table = 1;
         for (int s = 0; s < Sp - 1; ++s) table *= d->ks[s];
-        if (table * d->batch > 16384)
+        if (table * d->batch > 16384 || table * d->batch > 32 * 512)
             return fail(IMI_ERR_INVALID, "imi_async_assign: batch * prefix table > 16384");
     }
     return cuda_status(imi::launch_async_assign(*d, S(stream)), "imi_async_assign");

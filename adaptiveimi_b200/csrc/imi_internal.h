@@ -19,12 +19,14 @@ using BuildArgs = imi_build_desc;
 cudaError_t launch_similarity(const uint16_t* q, const float* cent, float* out, int bg, int G, int n_cells, int dim,
                               long long out_stride, cudaStream_t st);
 size_t select_smem_bytes(const SelectArgs& a);
+int select_max_slots();
 cudaError_t launch_select(const SelectArgs& a, cudaStream_t st);
-size_t attn_smem_bytes();
+size_t attn_smem_bytes(const AttnArgs& a);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t st);
 size_t async_smem_bytes(const AsyncArgs& a);
 cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st);
+int async_chunks(int n_slots);
 cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st);
 
 size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks);

@@ -215,18 +215,23 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
 
 
 def default_splits(bg: int, rows_per_group: int, sms: int = 148) -> int:
-    """CTAs per KV group for the split-K attention: about two waves of CTAs
-    over the SMs, and at least 64 rows per CTA."""
-    want = max(1, (2 * sms + bg - 1) // bg)
-    return int(max(1, min(want, (rows_per_group + 63) // 64, 512)))
+    """CTAs per KV group for the split-K attention: one wave (one CTA per SM,
+    the kernel's shared-memory ring allows one), at least 64 rows per CTA, and
+    at most 16K rows per CTA (the staged row indices)."""
+    want = max(1, sms // bg)
+    s = max(1, min(want, (rows_per_group + 63) // 64, 512))
+    return int(max(s, (rows_per_group + 16383) // 16384))
 
 
 def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: torch.Tensor,
                      list_keys: torch.Tensor, list_values: torch.Tensor, static_keys: torch.Tensor,
                      static_values: torch.Tensor, out: torch.Tensor, part_o: torch.Tensor, part_ml: torch.Tensor,
                      splits: int, scale: Optional[float] = None, delta_keys: Optional[torch.Tensor] = None,
-                     delta_values: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Attention of q [bg, G, 128] over the rows named by row_index."""
+                     delta_values: Optional[torch.Tensor] = None,
+                     counters: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of q [bg, G, 128] over the rows named by row_index.
+    counters: int32 [bg] zeroed scratch; when given the split merge happens in
+    the attention kernel itself (its last CTA per group)."""
     bg, G, D = q.shape
     if D != 128:
         raise ValueError("sparse attention supports head_dim 128")
@@ -241,6 +246,7 @@ def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: tor
         d.delta_keys, d.delta_values, d.delta_rows = delta_keys.data_ptr(), delta_values.data_ptr(), \
             delta_keys.shape[-2]
     d.part_o, d.part_ml, d.out = part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr()
+    d.counters = counters.data_ptr() if counters is not None else None
     L = _lib.load()
     _lib.check(L.imi_sparse_attention(ctypes.byref(d), _stream(q.device)), "imi_sparse_attention")
     return out
@@ -268,7 +274,10 @@ def async_assign(*, index: IMIIndex, batch: int, batch_keys: torch.Tensor, batch
                  shadow: torch.Tensor, shadow_dirty: torch.Tensor, pending: torch.Tensor, counts: torch.Tensor,
                  delta_counts: torch.Tensor, delta_sums: torch.Tensor, ring_keys: torch.Tensor,
                  ring_values: torch.Tensor, ring_cell_ids: torch.Tensor, ring_write_pos: torch.Tensor,
-                 ring_count: torch.Tensor, threshold: int, ids_out: Optional[torch.Tensor] = None) -> None:
+                 ring_count: torch.Tensor, threshold: int, ids_out: Optional[torch.Tensor] = None,
+                 part_best: Optional[torch.Tensor] = None) -> None:
+    """One batched decode-time cell assignment (async_update.py:122-161).
+    part_best: int64 scratch [bg, ceil(n_slots / 512), batch] (allocated when absent)."""
     bg = batch_keys.shape[0]
     d = _lib.AsyncDesc()
     d.bg, d.dim, d.n_slots, d.parts, d.kmax = bg, batch_keys.shape[-1], index.n_slots, index.parts, index.kmax
@@ -282,8 +291,16 @@ def async_assign(*, index: IMIIndex, batch: int, batch_keys: torch.Tensor, batch
         ring_cell_ids.data_ptr()
     d.ring_write_pos, d.ring_count = ring_write_pos.data_ptr(), ring_count.data_ptr()
     d.ids_out = ids_out.data_ptr() if ids_out is not None else None
+    chunks = async_chunks(index.n_slots)
+    if part_best is None or part_best.numel() < bg * chunks * batch:
+        part_best = torch.empty((bg, chunks, batch), dtype=torch.int64, device=batch_keys.device)
+    d.part_best, d.part_chunks = part_best.data_ptr(), chunks
     L = _lib.load()
     _lib.check(L.imi_async_assign(ctypes.byref(d), _stream(batch_keys.device)), "imi_async_assign")
+
+
+def async_chunks(n_slots: int) -> int:
+    return (n_slots + 511) // 512
 
 
 def apply_updates(*, shadow: torch.Tensor, live: torch.Tensor, pending: torch.Tensor,

@@ -23,8 +23,8 @@ on the data path); the reported time is the max over ranks.
 ``--impl reference`` times the reference's own CPU code for the path on the
 host cores: the index build (imi::kmeans_execute + reorganize_from_kmeans,
 compiled from the reference sources into oracle/_ref) and the decode selection
-(the reference's torch top-k rule + AdpIMI_Index.batch_access) with a CPU
-restatement of the scorer and attention, on a bounded sample.
+(the C port in oracle/ of the scorer, the top-k + token budget rule and the
+batch_access page truncation, with torch fp32 attention), on a bounded sample.
 """
 from __future__ import annotations
 
@@ -223,24 +223,26 @@ def run_ours(args):
     # ---- timed region: device-resident inputs
     cache.row_count_log = torch.zeros((args.steps * L, hl), dtype=torch.int32, device=dev)
     cache._log_pos = 0
-    cache.attn_event_log = []
+    cache.attn_event_log = None  # the roofline pass below times the attention kernel alone
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         e0.record()
+        h0 = time.perf_counter()
         for t in range(args.steps):
             step(args.warmup + t, qd[args.warmup + t], kd[args.warmup + t], vd[args.warmup + t])
+        host_s = time.perf_counter() - h0
         e1.record()
         torch.cuda.synchronize()
     if ws > 1:
         torch.distributed.barrier()
     dev_ms = e0.elapsed_time(e1)
-    attn_ms = [a.elapsed_time(b) for a, b in cache.attn_event_log]
-    rows = cache.row_count_log.to(torch.int64).sum().item()
+    rows_timed = cache.row_count_log.to(torch.int64).sum().item()
     cache.row_count_log = None
     cache.attn_event_log = None
+    attn = attention_kernel_pass(cache, qd[args.warmup + args.steps - 1], L, hl, G, dev)
     # ---- e2e: pinned host inputs copied in, outputs copied out, every step
     # (the cache has capacity for warmup + steps appended tokens; e2e reuses the
     # last `e2e_steps` positions after a reset of the appended-token counter)
@@ -266,10 +268,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
     # ---- max over ranks
-    vals = torch.tensor([dev_ms, e2e_ms, sum(attn_ms), build_ms], dtype=torch.float64, device=dev)
+    vals = torch.tensor([dev_ms, e2e_ms, attn["avg_us"], build_ms], dtype=torch.float64, device=dev)
     if ws > 1:
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
-    dev_ms, e2e_ms, attn_total_ms, build_ms_max = vals.tolist()
+    dev_ms, e2e_ms, attn_avg_us, build_ms_max = vals.tolist()
     if rank != 0:
         if ws > 1:
             torch.distributed.destroy_process_group()
@@ -277,14 +279,7 @@ def run_ours(args):
     us_per_layer_step = dev_ms * 1e3 / (args.steps * L)
     e2e_us = e2e_ms * 1e3 / (e2e_steps * L)
     hbm, src = peaks()
-    # algorithmic bytes of the attention launches (this rank): K and V rows
-    # (512 B each), their row indices (4 B), q and out, the split partials
-    # written and read back by the combine kernel.
-    n_launch = max(1, len(attn_ms))
-    part_bytes = hl * cache.splits * G * (128 + 2) * 4 * 2
-    algo = rows * (512 + 4) + n_launch * (hl * G * 128 * 2 * 2 + part_bytes)
-    attn_avg_s = (sum(attn_ms) / n_launch) * 1e-3
-    achieved = (algo / n_launch) / attn_avg_s / 1e9 if attn_avg_s > 0 else 0.0
+    achieved = attn["algo_bytes"] / (attn_avg_us * 1e-6) / 1e9 if attn_avg_us > 0 else 0.0
     keys_built = L * kvh * n_mid
     res = {
         "metric": METRIC, "value": round(us_per_layer_step, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -301,21 +296,23 @@ def run_ours(args):
         "e2e": {"value": round(e2e_us, 3), "unit": UNIT, "h2d_bytes_per_step": int(L * (qh[0, 0].numel() +
                                                                                         2 * kh[0, 0].numel()) * 2),
                 "d2h_bytes_per_step": int(L * outs_h[0, 0].numel() * 2), "steps": e2e_steps},
-        "roofline": {"kernel": "imi_attn_kernel + imi_combine_kernel", "bound": "hbm",
+        "roofline": {"kernel": "imi_attn_kernel (gather attention with in-kernel split merge)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "frac": round(achieved / hbm, 4), "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": None,
-                     "algorithmic_bytes_per_launch": int(algo / n_launch),
-                     "avg_launch_us": round(attn_avg_s * 1e6, 3)},
+                     "algorithmic_bytes_per_launch": int(attn["algo_bytes"]),
+                     "avg_launch_us": round(attn_avg_us, 3), "launches_timed": attn["launches"],
+                     "rows_per_launch": attn["rows_per_launch"]},
         "build": {"metric": "IMI build Mkeys/s", "value": round(keys_built / (build_ms_max * 1e-3) / 1e6, 3),
                   "unit": "Mkeys/s", "build_ms_total": round(build_ms_max, 2), "keys": keys_built,
                   "kmeans": KMEANS},
         "gpu_launches": None,
+        "host_launch_us_per_layer_step": round(host_s * 1e6 / (args.steps * L), 2),
         "clocks": clk.summary(),
     }
     # our kernels per layer-step: append + select + attention + combine, plus
     # the async assignment every 16 steps and the centroid publish after it
-    res["gpu_launches"] = int(args.steps * L * 4 + (args.steps // ASYNC["batch"]) * L * 2)
+    res["gpu_launches"] = int(args.steps * L * 4 + (args.steps // ASYNC["batch"]) * L * 3)
     if ws == 1 and not args.no_cpu_baseline:
         try:
             res["cpu_baseline"] = cpu_baseline(args, sample_layers=1, sample_steps=2)
@@ -324,6 +321,57 @@ def run_ours(args):
     if ws > 1:
         torch.distributed.destroy_process_group()
     return res
+
+
+def attention_kernel_pass(cache, q_last, L, hl, G, dev, repeats=6):
+    """Live CUDA-event timing of the attention kernel alone (imi_sparse_attention:
+    gather attention + split combine) on every layer's row list of the last
+    decode step, cycling through the 32 layers so that each launch streams its
+    rows from HBM (the layers' rows together exceed L2).
+
+    Algorithmic bytes per launch = rows * (256 B key + 256 B value + 4 B row
+    index) + q and out (bf16) + the split partials written and read back."""
+    from adaptiveimi_b200 import ops
+
+    bg = hl
+    rows, rcs = [], []
+    for l in range(L):
+        r = torch.empty((bg, cache.execution_stride), dtype=torch.int32, device=dev)
+        rc = torch.empty((bg,), dtype=torch.int32, device=dev)
+        q = q_last[l].reshape(bg, G, 128).contiguous()
+        ops.select_cells(q=q, index=cache.index[l], nprobe=cache.nprobe, max_tokens=cache.max_retrieval_tokens,
+                         buffer_pages=cache.buffer_size, page_size=8, padding_id=cache.padding_cluster_id,
+                         static_len=cache.static_pattern_total, exec_capacity=cache.execution_stride,
+                         sel_cells=torch.empty((bg, cache.nprobe), dtype=torch.int32, device=dev),
+                         sel_count=torch.empty((bg,), dtype=torch.int32, device=dev), row_index=r, row_count=rc)
+        rows.append((q, r))
+        rcs.append(rc)
+    out = torch.empty((bg, G, 128), dtype=torch.bfloat16, device=dev)
+    part_o = torch.empty((bg, cache.splits, G, 128), dtype=torch.float32, device=dev)
+    part_ml = torch.empty((bg, cache.splits, G, 2), dtype=torch.float32, device=dev)
+    counters = torch.zeros((bg,), dtype=torch.int32, device=dev)
+    evs = []
+    torch.cuda.synchronize()
+    for rep in range(repeats + 1):
+        for l in range(L):
+            q, r = rows[l]
+            zk = cache.steady_zone_keys[l].view(bg, cache.static_capacity, 128)
+            zv = cache.steady_zone_values[l].view(bg, cache.static_capacity, 128)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            ops.sparse_attention(q=q, row_index=r, row_count=rcs[l], list_keys=cache.index[l].list_keys,
+                                 list_values=cache.index[l].list_values, static_keys=zk, static_values=zv, out=out,
+                                 part_o=part_o, part_ml=part_ml, splits=cache.splits, counters=counters)
+            b.record()
+            if rep > 0:  # the first sweep is warmup
+                evs.append((a, b))
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) * 1e3 for a, b in evs]
+    total_rows = sum(int(rc.to(torch.int64).sum()) for rc in rcs)
+    rows_per_launch = total_rows / L
+    algo = rows_per_launch * (512 + 4) + bg * G * 128 * 2 * 2 + bg * cache.splits * G * (128 + 2) * 4 * 2
+    return {"avg_us": sum(times) / len(times), "algo_bytes": algo, "launches": len(times),
+            "rows_per_launch": rows_per_launch}
 
 
 # ----------------------------------------------------------------------------
@@ -377,69 +425,52 @@ def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
                          KMEANS["early_stop_rel_tol"])
     build_s = time.perf_counter() - t0
     build_mkeys = build_heads * n / build_s / 1e6
-    # ---- decode sample: one layer's index for all heads, built on the GPU
-    # box's CPU would take minutes; the sample uses the GPU-independent oracle
-    # index of `build_heads` heads tiled to 8 groups (selection work per group is
-    # what is timed, and it does not depend on which head's index it scans)
+    # ---- decode sample: the index of `build_heads` heads tiled over the 8 KV
+    # groups (the selection and gather work per group does not depend on which
+    # head's index it scans).  Scorer (compute_impl.cu:62-103), top-k + token
+    # budget (retrieval.py:295-303) and page truncation
+    # (wave_buffer_cpu_hotcold.cpp:303-371) are the C port in oracle/; the
+    # attention over the gathered rows is torch fp32 on the host cores.
     sizes = RetrievalSizes.from_capacity(n, 2, CFG["retrieval_budget"], CFG["buffer_cluster_num"], 96 + 256)
-    if mods is not None:
-        sizes_t = torch.zeros(kvh, sizes.n_centroids, dtype=torch.int32)
-        offs_t = torch.zeros(kvh, sizes.n_centroids + 1, dtype=torch.int32)
-        cents = torch.zeros(kvh, sizes.n_centroids, D)
-        lk = torch.zeros(kvh, n, D, dtype=torch.bfloat16)
-        lv = torch.zeros_like(lk)
-        for h in range(kvh):
-            src = h % build_heads
-            c = int(r["cluster_counts"][src])
-            sizes_t[h, :c] = r["cluster_sizes"][src, :c]
-            offs_t[h, :c + 1] = r["cluster_offsets"][src, :c + 1]
-            offs_t[h, c + 1:] = r["cluster_offsets"][src, c]
-            cents[h, :c] = r["centroids"][src, :c]
-            lk[h] = r["list_keys"][src]
-            lv[h] = r["list_values"][src]
-    else:
-        raise RuntimeError("decode CPU baseline needs oracle/_ref")
-    mask = (sizes_t == 0)
-    pool = mods[1].AdpIMI_ThreadPool(cores)
-    z = lambda *s: torch.zeros(*s, dtype=torch.int32)  # noqa: E731
-    bp = sizes.buffer_size
+    if mods is None:
+        raise RuntimeError("decode CPU baseline needs the reference build (oracle/_ref)")
+    ns = sizes.n_centroids
+    sizes_np = np.zeros((kvh, ns), np.int32)
+    offs_np = np.zeros((kvh, ns + 1), np.int32)
+    cents = np.zeros((kvh, ns, D), np.float32)
+    mask = np.ones((kvh, ns), np.uint8)
+    lk = [None] * kvh
+    lv = [None] * kvh
+    for h in range(kvh):
+        src = h % build_heads
+        c = int(r["cluster_counts"][src])
+        sizes_np[h, :c] = r["cluster_sizes"][src, :c].numpy()
+        offs_np[h, :c + 1] = r["cluster_offsets"][src, :c + 1].numpy()
+        offs_np[h, c + 1:] = offs_np[h, c]
+        cents[h, :c] = r["centroids"][src, :c].numpy()
+        mask[h, :c] = 0
+        lk[h] = r["list_keys"][src]
+        lv[h] = r["list_values"][src]
     q = torch.randn(kvh, G, D).to(torch.bfloat16)
     qb = O.bf16_bits(q)
     t0 = time.perf_counter()
     for _ in range(sample_steps * sample_layers):
-        # scorer (compute_impl.cu:62-103 restated in C)
-        sims = torch.from_numpy(np.stack([O.scores(qb[h], cents[h].numpy(), mask[h].numpy().astype(np.uint8))
-                                          for h in range(kvh)]))
-        # the reference's selection (retrieval.py:295-303)
-        topk = torch.topk(sims, sizes.nprobe, dim=-1, largest=True, sorted=True)
-        szs = torch.gather(sizes_t, 1, topk.indices)
-        cum = torch.cumsum(szs, dim=-1, dtype=torch.int32)
-        keep = (szs > 0) & ((cum - szs) < sizes.max_retrieval_tokens)
-        sel = topk.indices.masked_fill(~keep, sizes.padding_cluster_id)
-        # the reference's page truncation (AdpIMI_Index.batch_access)
-        bufs = [z(kvh, bp) for _ in range(3)] + [z(kvh)] + [z(kvh, bp) for _ in range(3)] + [z(kvh)] + \
-               [z(kvh, bp) for _ in range(3)] + [z(kvh)]
-        idx = mods[1].AdpIMI_Index(1, kvh, D, sizes.nprobe, 0, 8, sizes.n_centroids, bp, 1, cores, pool.get())
-        idx.set_indices(*bufs, sel.clone())
-        ph = torch.empty(kvh, 0, D, dtype=torch.bfloat16)
-        idx.set_kv(ph.unsqueeze(0), ph.unsqueeze(0), ph, ph)
-        idx.set_cluster_metadata(sizes_t, offs_t, 0)
-        idx.batch_access()
-        idx.sync()
-        # gather + attention on the CPU (fp32)
-        miss_ids, miss_sizes, miss_num = bufs[4], bufs[5], bufs[7]
         for h in range(kvh):
-            segs = [torch.arange(int(miss_ids[h, j]), int(miss_ids[h, j]) + int(miss_sizes[h, j]))
-                    for j in range(int(miss_num[h]))]
-            ridx = torch.cat(segs) if segs else torch.zeros(0, dtype=torch.int64)
-            kr = lk[h, ridx].float()
-            vr = lv[h, ridx].float()
+            sc = O.scores(qb[h], cents[h], mask[h])
+            sel, _ = O.select(sc, sizes_np[h], sizes.nprobe, sizes.max_retrieval_tokens, sizes.buffer_size, 8,
+                              sizes.padding_cluster_id)
+            ridx = torch.cat([torch.arange(int(offs_np[h, c]), int(offs_np[h, c]) + int(sizes_np[h, c]))
+                              for c in sel]) if len(sel) else torch.zeros(0, dtype=torch.int64)
+            kr = lk[h][ridx].float()
+            vr = lv[h][ridx].float()
             s = (q[h].float() @ kr.T) / math.sqrt(D)
             torch.softmax(s, -1) @ vr
     dec_s = time.perf_counter() - t0
     us = dec_s * 1e6 / (sample_steps * sample_layers)
     return {"value": round(us, 1), "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"decode: {sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, 128K context; "
+            "sample": f"decode (C port of the scorer/selection/truncation + torch fp32 attention): "
+                      f"{sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, {ctx}-token context; "
+                      f"build (the reference's own kmeans_execute + reorganize_from_kmeans): "
                       f"build: {build_heads} heads x {n} keys, k={ks[0]}x{ks[1]}, {KMEANS['max_iters']} iters",
             "build": {"value": round(build_mkeys, 4), "unit": "Mkeys/s", "seconds": round(build_s, 2)}}
 

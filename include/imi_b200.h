@@ -32,6 +32,9 @@
  *                          (async_update.py:20-76)
  *   imi_sparse_attention   the gather of gather_copy_and_concat fused with
  *                          weighted_flash_decoding (retrieval.py:439-447)
+ *   imi_decode_attend      the whole decode attention of one layer,
+ *                          AdaptiveIMIRetrievalMixin.sparse_attention
+ *                          (retrieval.py:320-602): apply + select + attention
  *   imi_decode_append      decode_update_kv_cache (runtime.py:378-392) and the
  *                          async-update batch buffer (async_update.py:112-117)
  *   imi_async_assign       _schedule_async_update batch step (async_update.py:118-161)
@@ -60,7 +63,10 @@ extern "C" {
 #define IMI_ERR_CUDA 2
 
 /* Row-list entries written by imi_select_cells: (source << 30) | row, where
- * source 0 = IMI list row, 1 = steady-zone row, 2 = delta-ring row. */
+ * source 0 = IMI list row, 1 = steady-zone row, 2 = delta-ring row (the value is
+ * then negative as int32; -1 is never a valid entry).  The list holds the
+ * steady-zone rows, then the selected cells' rows (cells in slot order), then
+ * the matching delta rows. */
 #define IMI_ROW_SOURCE_SHIFT 30
 
 typedef struct imi_build_desc {
@@ -105,7 +111,7 @@ typedef struct imi_select_desc {
     const int32_t* delta_count;            /* [bg] or NULL */
     int32_t delta_capacity;
     int32_t exec_capacity;                 /* row-list capacity (>= static_len + buffer_pages*page_size) */
-    int32_t* sel_cells;                    /* [bg, nprobe] out: selected cells in score order */
+    int32_t* sel_cells;                    /* [bg, nprobe] out: selected cells, ascending slot order */
     int32_t* sel_count;                    /* [bg] out */
     int32_t* kept_count;                   /* [bg] out or NULL: cells kept before page truncation */
     int32_t* row_index;                    /* [bg, exec_capacity] out */
@@ -131,6 +137,10 @@ typedef struct imi_attn_desc {
     float* part_o;                         /* scratch [bg, splits, G, 128] */
     float* part_ml;                        /* scratch [bg, splits, G, 2] */
     void* out;                             /* [bg, G, 128] bf16 out */
+    int32_t* counters;                     /* scratch [bg], zero before the first call, or NULL:
+                                              with it the last CTA of a group merges the
+                                              splits (and re-zeroes its counter); without it a
+                                              separate merge kernel runs */
 } imi_attn_desc;
 
 typedef struct imi_append_desc {
@@ -166,6 +176,8 @@ typedef struct imi_async_desc {
     int32_t* ring_write_pos;               /* [bg] */
     int32_t* ring_count;                   /* [bg] */
     int32_t* ids_out;                      /* [bg, batch] or NULL */
+    unsigned long long* part_best;         /* scratch [bg, part_chunks, batch] */
+    int32_t part_chunks;                   /* = ceil(n_slots / 512) */
 } imi_async_desc;
 
 typedef struct imi_apply_desc {
@@ -186,6 +198,11 @@ IMI_API int imi_query_group_similarities(const uint16_t* q, const float* centroi
                                  int32_t groups, int32_t n_clusters, int32_t dim, int64_t out_stride, void* stream);
 IMI_API int imi_select_cells(const imi_select_desc* desc, void* stream);
 IMI_API int imi_sparse_attention(const imi_attn_desc* desc, void* stream);
+/* apply (optional, NULL to skip) + select + attention in one call: the per-layer
+ * decode attention of the cache (retrieval.py:320-602).  sel and attn must name
+ * the same q, row_index, row_count and exec_capacity. */
+IMI_API int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
+                              void* stream);
 IMI_API int imi_decode_append(const imi_append_desc* desc, void* stream);
 IMI_API int imi_async_assign(const imi_async_desc* desc, void* stream);
 IMI_API int imi_apply_updates(const imi_apply_desc* desc, void* stream);
