@@ -46,7 +46,7 @@ class SelectDesc(ctypes.Structure):
         ("delta_cell_ids", P), ("delta_count", P),
         ("delta_capacity", i32), ("exec_capacity", i32),
         ("sel_cells", P), ("sel_count", P), ("kept_count", P), ("row_index", P), ("row_count", P),
-        ("scores_out", P),
+        ("scores_out", P), ("phase_ns", P),
     ]
 
 

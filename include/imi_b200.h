@@ -117,6 +117,8 @@ typedef struct imi_select_desc {
     int32_t* row_index;                    /* [bg, exec_capacity] out */
     int32_t* row_count;                    /* [bg] out */
     float* scores_out;                     /* [bg, n_slots] out or NULL */
+    unsigned long long* phase_ns;          /* [bg, 8] out or NULL: device timestamps (ns) of the
+                                              selection's phases, a profiling aid */
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
