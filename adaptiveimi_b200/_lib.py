@@ -95,7 +95,7 @@ class ApplyDesc(ctypes.Structure):
 EXPORTS = (
     "imi_abi_version", "imi_last_error", "imi_build_workspace_size", "imi_build_index",
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
-    "imi_async_assign", "imi_apply_updates", "imi_decode_attend",
+    "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_sparse_attention_noalloc",
 )
 
 _lib = None
@@ -128,6 +128,7 @@ def load():
         L.imi_decode_append.argtypes = [ctypes.POINTER(AppendDesc), P]
         L.imi_async_assign.argtypes = [ctypes.POINTER(AsyncDesc), P]
         L.imi_apply_updates.argtypes = [ctypes.POINTER(ApplyDesc), P]
+        L.imi_sparse_attention_noalloc.argtypes = [ctypes.POINTER(AttnDesc), P]
         L.imi_decode_attend.argtypes = [ctypes.POINTER(SelectDesc), ctypes.POINTER(AttnDesc),
                                         ctypes.POINTER(ApplyDesc), P]
         if L.imi_abi_version() != 1:

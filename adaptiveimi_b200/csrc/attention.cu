@@ -20,6 +20,9 @@
 // product has M <= 8 against tcgen05's minimum M of 64, and the kernel moves
 // 512 bytes per row for 4 * 128 * 2 multiply-adds -- it is bound by HBM, and
 // the tensor instruction only has to keep the instruction count per byte low.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "imi_internal.h"
 
@@ -330,3 +333,83 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
 }
 
 }  // namespace imi
+
+// ---------------------------------------------------------------------------
+// imi_sparse_attention_noalloc: the same attention, with its scratch (split
+// partials and merge counters) in a fixed array that the library owns.
+//
+// For callers that cannot call cudaMalloc at all -- for example code running
+// under an allocator that must not be re-entered, inside a host callback, or
+// in a runtime that forbids device allocation once set up -- and so cannot
+// provide part_o / part_ml / counters.  The array below is created when the
+// library is loaded on a device and lives until the process exits (every GPU
+// that loads the library holds IMI_NOALLOC_SCRATCH_BYTES of it).
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_attn_scratch[IMI_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[128] = {};
+
+// Device address of g_attn_scratch for the current device.  The name is only
+// a host-side stand-in, so the address is asked of the runtime, once per
+// device, with that device current.
+cudaError_t scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (e != cudaSuccess) return e;
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return cudaSuccess;
+}
+
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" IMI_API int imi_sparse_attention_noalloc(const imi_attn_desc* desc, void* stream) {
+    if (!desc) {
+        imi::set_last_error("imi_sparse_attention_noalloc: null descriptor");
+        return IMI_ERR_INVALID;
+    }
+    if (desc->bg <= 0 || desc->G <= 0 || desc->splits <= 0) {
+        imi::set_last_error("imi_sparse_attention_noalloc: bg, G and splits must be positive");
+        return IMI_ERR_INVALID;
+    }
+    const size_t groups = (size_t)desc->bg * desc->splits * desc->G;
+    const size_t need = round256((size_t)desc->bg * 4) + round256(groups * 2 * 4) + groups * 128 * 4;
+    if (need > IMI_NOALLOC_SCRATCH_BYTES) {
+        imi::set_last_error("imi_sparse_attention_noalloc: bg * splits * G needs " + std::to_string(need) +
+                            " bytes of scratch; the fixed array holds " +
+                            std::to_string((size_t)IMI_NOALLOC_SCRATCH_BYTES) +
+                            " (lower splits or use imi_sparse_attention)");
+        return IMI_ERR_INVALID;
+    }
+    void* base = nullptr;
+    cudaError_t e = scratch_address(&base);
+    if (e != cudaSuccess) {
+        imi::set_last_error(std::string("imi_sparse_attention_noalloc: cudaGetSymbolAddress: ") +
+                            cudaGetErrorString(e));
+        return IMI_ERR_CUDA;
+    }
+    unsigned char* p = static_cast<unsigned char*>(base);
+    imi_attn_desc d = *desc;
+    d.counters = reinterpret_cast<int32_t*>(p);
+    d.part_ml = reinterpret_cast<float*>(p + round256((size_t)desc->bg * 4));
+    d.part_o = reinterpret_cast<float*>(p + round256((size_t)desc->bg * 4) + round256(groups * 2 * 4));
+    // the merge counters must start at zero; the array keeps the last call's contents
+    e = cudaMemsetAsync(d.counters, 0, (size_t)desc->bg * 4, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        imi::set_last_error(std::string("imi_sparse_attention_noalloc: ") + cudaGetErrorString(e));
+        return IMI_ERR_CUDA;
+    }
+    return imi_sparse_attention(&d, stream);
+}

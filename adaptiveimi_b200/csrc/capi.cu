@@ -28,6 +28,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 }  // namespace
 
+namespace imi {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace imi
+
 extern "C" {
 
 int imi_abi_version(void) { return IMI_ABI_VERSION; }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "../../include/imi_b200.h"
 
 namespace imi {
@@ -30,6 +32,7 @@ int async_chunks(int n_slots);
 cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st);
 
 size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks);
+void set_last_error(const std::string& msg);
 cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why);
 
 }  // namespace imi

@@ -69,6 +69,9 @@ extern "C" {
  * the matching delta rows. */
 #define IMI_ROW_SOURCE_SHIFT 30
 
+/* Size of the library-owned scratch array used by imi_sparse_attention_noalloc. */
+#define IMI_NOALLOC_SCRATCH_BYTES (1u << 20)
+
 typedef struct imi_build_desc {
     int32_t heads, n_tokens, dim, parts;   /* parts: 0 (IVF), 2 or 4 */
     int32_t ks[4];                         /* k per subspace (ks[0] for IVF) */
@@ -200,6 +203,20 @@ IMI_API int imi_query_group_similarities(const uint16_t* q, const float* centroi
                                  int32_t groups, int32_t n_clusters, int32_t dim, int64_t out_stride, void* stream);
 IMI_API int imi_select_cells(const imi_select_desc* desc, void* stream);
 IMI_API int imi_sparse_attention(const imi_attn_desc* desc, void* stream);
+/* imi_sparse_attention without caller-provided scratch.  This entry point has
+ * no counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory at all (code running inside another allocator, a host callback,
+ * or a runtime that forbids cudaMalloc after start-up) and therefore cannot pass
+ * part_o / part_ml / counters: those fields of the descriptor are ignored and a
+ * fixed array owned by the library (IMI_NOALLOC_SCRATCH_BYTES, 1 MiB per GPU
+ * that loads the library, held until the process exits) is used instead.
+ * Limit: bg * splits * G * 520 bytes plus alignment must fit in that array;
+ * larger requests fail with IMI_ERR_INVALID and a message.  The first call on
+ * a device looks the array's address up (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls share the one array, so calls that
+ * can overlap on the GPU (other streams, other host threads) race: serialise
+ * them.  It allocates nothing (no cudaMalloc/cudaFree). */
+IMI_API int imi_sparse_attention_noalloc(const imi_attn_desc* desc, void* stream);
 /* apply (optional, NULL to skip) + select + attention in one call: the per-layer
  * decode attention of the cache (retrieval.py:320-602).  sel and attn must name
  * the same q, row_index, row_count and exec_capacity. */
