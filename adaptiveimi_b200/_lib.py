@@ -58,7 +58,7 @@ class AttnDesc(ctypes.Structure):
         ("list_keys", P), ("list_values", P), ("list_rows", i64),
         ("static_keys", P), ("static_values", P), ("static_rows", i64),
         ("delta_keys", P), ("delta_values", P), ("delta_rows", i64),
-        ("part_o", P), ("part_ml", P), ("out", P), ("counters", P),
+        ("part_o", P), ("part_ml", P), ("out", P), ("counters", P), ("status", P),
     ]
 
 

@@ -152,7 +152,8 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.execution_buffer_values_dict: Dict[str, torch.Tensor] = {}
         self.valid_lengths_dict: Dict[str, torch.Tensor] = {}
         self._dec: Dict[str, Dict[str, torch.Tensor]] = {}
-        self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity)
+        self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity,
+                                          exec_capacity=self.execution_stride)
         # optional measurement hooks (bench.py): per-call row counts and CUDA
         # events around the attention launch, both on the launching stream
         self.row_count_log: Optional[torch.Tensor] = None
@@ -234,6 +235,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                 part_o=torch.empty((bg, self.splits, G, self.head_dim), dtype=torch.float32, device=dev),
                 part_ml=torch.empty((bg, self.splits, G, 2), dtype=torch.float32, device=dev),
                 counters=torch.zeros((bg,), dtype=torch.int32, device=dev),
+                status=torch.zeros((1,), dtype=torch.int32, device=dev),
             )
             self.execution_buffer_keys_dict[dev] = rows
             self.execution_buffer_values_dict[dev] = rows
@@ -285,6 +287,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             att.delta_rows = self.async_update_delta_tokens
         att.part_o, att.part_ml = buf["part_o"].data_ptr(), buf["part_ml"].data_ptr()
         att.counters = buf["counters"].data_ptr()
+        att.status = buf["status"].data_ptr()
         app = None
         if st is not None:
             app = _lib.ApplyDesc()

@@ -6,15 +6,23 @@
 // selected rows are read once, straight from the HBM-resident lists.
 //
 // Grid (splits, groups); 8 warps per CTA, one CTA per SM.  A CTA owns a
-// contiguous range of the group's rows.  It first resolves every row's source
-// address into shared memory, then each warp streams 16-row tiles through a
-// 3-deep cp.async ring (16-byte chunks XOR-swizzled by row so ldmatrix is
-// conflict-free), computes S = Q K^T and O += P V with mma.sync m16n8k16
-// (query heads on M: G <= 8 of the 16 rows are live), and keeps an online
-// softmax in exp2 space.  The warps merge through shared memory; the CTA
-// writes one (m, l, o) partial; the last CTA of a group (an atomic counter
-// that it re-zeroes) merges the partials into the bf16 output, or a separate
-// merge kernel does when no counter buffer is given.
+// contiguous range of the group's rows and stages their row-list entries in
+// shared memory.  Each warp streams 16-row tiles through a 3-deep ring: one
+// lane per row issues a 256-byte cp.async.bulk (K rows from lanes 0-15, V rows
+// from lanes 16-31) that completes on the stage's mbarrier, so one warp
+// instruction moves a whole tile.  Rows sit at a 272-byte pitch so the eight
+// rows of an ldmatrix fall on distinct banks.  The warp computes S = Q K^T and
+// O += P V with mma.sync m16n8k16 (query heads on M: G <= 8 of the 16 rows are
+// live) and keeps an online softmax in exp2 space.  The warps merge through
+// shared memory; the CTA writes one (m, l, o) partial; the last CTA of a group
+// (an atomic counter that it re-zeroes) merges the partials into the bf16
+// output, or a separate merge kernel does when no counter buffer is given.
+// Every mbarrier wait is bounded: a wait that gives up sets bit 0 of
+// `status` and the kernel finishes without hanging.
+//
+// The kernel is launched as a programmatic dependent (PDL) of the kernel
+// before it in the stream: its CTAs set up their barriers while that kernel
+// (normally the selection) drains, and wait for it before reading memory.
 //
 // Why mma.sync and not tcgen05: with G = 4..8 query heads per KV group the
 // product has M <= 8 against tcgen05's minimum M of 64, and the kernel moves
@@ -30,20 +38,44 @@ namespace imi {
 
 constexpr int AT_WARPS = 8;
 constexpr int AT_STAGES = 3;
-constexpr int AT_TILE = 16;                            // rows per tile
-constexpr int AT_ROWB = 256;                           // bytes per row (dim 128, bf16)
-constexpr int AT_STAGE_BYTES = 2 * AT_TILE * AT_ROWB;  // K + V
+constexpr int AT_TILE = 16;                              // rows per tile
+constexpr int AT_ROWB = 256;                             // bytes per row in HBM (dim 128, bf16)
+constexpr int AT_PITCH = 272;                            // bytes per row in shared memory: the 16-byte pad
+                                                         // puts the 8 rows of an ldmatrix on distinct banks
+constexpr int AT_STAGE_BYTES = 2 * AT_TILE * AT_PITCH;   // K tile + V tile
 constexpr int AT_RING_BYTES = AT_WARPS * AT_STAGES * AT_STAGE_BYTES;
+constexpr int AT_BAR_BYTES = AT_WARPS * AT_STAGES * 8;   // one mbarrier per stage per warp
+constexpr int AT_WAIT_LIMIT = 1 << 20;                   // polls of an mbarrier before the kernel gives up
 
 IMI_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
-IMI_DEV void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+IMI_DEV void mbar_init(uint32_t bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
 }
-IMI_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-IMI_DEV void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+IMI_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+IMI_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// The whole warp polls until every lane sees the phase complete, at most
+// AT_WAIT_LIMIT times; false when it gave up.
+IMI_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < AT_WAIT_LIMIT; ++i)
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    return false;
+}
+// One row, global -> shared, completing on `bar` (no multicast).
+IMI_DEV void bulk_row(uint32_t dst, const void* src, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"((uint32_t)AT_ROWB), "r"(bar)
+                 : "memory");
 }
 IMI_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
@@ -67,26 +99,28 @@ IMI_DEV uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Source of a row-list entry: the key row's address with the source (0 list,
-// 1 steady zone, 2 delta ring) in the low two bits (rows are 16-byte aligned);
-// 0 when the entry has no backing buffer.
-IMI_DEV unsigned long long row_key_addr(const AttnArgs& a, int h, int idx) {
+// Address of a row-list entry's key (kv = 0) or value (kv = 1) row; the top
+// two bits of the entry name the source (0 list, 1 steady zone, 2 delta ring).
+// NULL when that source has no buffer.
+IMI_DEV const unsigned char* row_src(const AttnArgs& a, int h, int idx, int kv) {
     const unsigned src = (unsigned)idx >> 30;
     const long long row = idx & 0x3fffffff;
-    const unsigned char* b;
+    const void* b;
     long long stride;
     if (src == 0) {
-        b = reinterpret_cast<const unsigned char*>(a.list_keys);
+        b = kv ? a.list_values : a.list_keys;
         stride = a.list_rows;
     } else if (src == 1) {
-        b = reinterpret_cast<const unsigned char*>(a.static_keys);
+        b = kv ? a.static_values : a.static_keys;
         stride = a.static_rows;
-    } else {
-        b = reinterpret_cast<const unsigned char*>(a.delta_keys);
+    } else if (src == 2) {
+        b = kv ? a.delta_values : a.delta_keys;
         stride = a.delta_rows;
+    } else {
+        return nullptr;
     }
-    if (!b) return 0ull;
-    return reinterpret_cast<unsigned long long>(b + ((long long)h * stride + row) * AT_ROWB) | src;
+    if (!b) return nullptr;
+    return reinterpret_cast<const unsigned char*>(b) + ((long long)h * stride + row) * AT_ROWB;
 }
 
 __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) {
@@ -95,6 +129,15 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const int split = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
+    const uint32_t ring = smem_u32(att_smem);
+    const uint32_t bars = ring + AT_RING_BYTES;
+    int32_t* ridx_s = reinterpret_cast<int32_t*>(att_smem + AT_RING_BYTES + AT_BAR_BYTES);
+    if (threadIdx.x < AT_WARPS * AT_STAGES) mbar_init(bars + 8 * threadIdx.x, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    // Launched as a programmatic dependent of the select kernel: everything
+    // above overlaps its tail; every global read comes after this wait.
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+
     const int rows_total = a.row_count[h];
     int chunk = (rows_total + a.splits - 1) / a.splits;
     chunk = (chunk + AT_TILE - 1) & ~(AT_TILE - 1);
@@ -102,24 +145,10 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const int r1 = min(rows_total, r0 + chunk);
     const int nrows = max(0, r1 - r0);
     const int ntiles = (nrows + AT_TILE - 1) / AT_TILE;
-
-    // row sources for the whole range, resolved once
-    unsigned long long* rptr = reinterpret_cast<unsigned long long*>(att_smem + AT_RING_BYTES);
     {
         const int32_t* ridx = a.row_index + (size_t)h * a.exec_capacity + r0;
-        for (int r = threadIdx.x; r < ntiles * AT_TILE; r += blockDim.x)
-            rptr[r] = r < nrows ? row_key_addr(a, h, ridx[r]) : 0ull;
+        for (int r = threadIdx.x; r < nrows; r += blockDim.x) ridx_s[r] = ridx[r];
     }
-    const long long vdiff0 = reinterpret_cast<const unsigned char*>(a.list_values) -
-                             reinterpret_cast<const unsigned char*>(a.list_keys);
-    const long long vdiff1 = reinterpret_cast<const unsigned char*>(a.static_values) -
-                             reinterpret_cast<const unsigned char*>(a.static_keys);
-    const long long vdiff2 = a.delta_keys ? reinterpret_cast<const unsigned char*>(a.delta_values) -
-                                                reinterpret_cast<const unsigned char*>(a.delta_keys)
-                                          : 0ll;
-    __syncthreads();
-
-    const uint32_t wbuf = smem_u32(att_smem) + warp * AT_STAGES * AT_STAGE_BYTES;
     uint32_t qa[8][2];
     {
         const uint16_t* qh = a.q + (size_t)h * a.G * 128;
@@ -135,55 +164,64 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             }
         }
     }
+    __syncthreads();
+
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY, l_run = 0.0f;
     float o[16][4];
 #pragma unroll
     for (int u = 0; u < 16; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
     const int my_tiles = ntiles > warp ? (ntiles - warp + AT_WARPS - 1) / AT_WARPS : 0;
-    const int ch = lane & 15;
-    const int half = lane >> 4;
+    const uint32_t wring = ring + warp * AT_STAGES * AT_STAGE_BYTES;
+    const uint32_t wbars = bars + warp * AT_STAGES * 8;
 
-    // copy tile `it` of this warp: lane copies chunk `ch` of rows 2j+half (K and V)
+    // Tile `it` of this warp: lane l brings row (l & 15) of the tile's K
+    // (l < 16) or V (l >= 16) with one bulk copy.  Rows past the range or
+    // without a source buffer are zero-filled instead (a past-the-range row is
+    // also masked out of the softmax; a sourceless one counts as a zero row).
     auto issue = [&](int it) {
         const int t = warp + it * AT_WARPS;
-        const uint32_t sb = wbuf + (it % AT_STAGES) * AT_STAGE_BYTES;
+        const int st = it % AT_STAGES;
+        const uint32_t bar = wbars + 8 * st;
+        const int i = lane & 15, kv = lane >> 4;
+        const int r = t * AT_TILE + i;
+        const unsigned char* src = r < nrows ? row_src(a, h, ridx_s[r], kv) : nullptr;
+        const unsigned live = __ballot_sync(0xffffffffu, src != nullptr);
+        if (lane == 0) mbar_expect_tx(bar, (uint32_t)__popc(live) * AT_ROWB);
+        __syncwarp();
+        const uint32_t dst = wring + st * AT_STAGE_BYTES + (kv * AT_TILE + i) * AT_PITCH;
+        if (src) {
+            bulk_row(dst, src, bar);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int i = 2 * j + half;
-            const unsigned long long e = rptr[t * AT_TILE + i];
-            const unsigned src = (unsigned)(e & 3ull);
-            const unsigned char* kp = reinterpret_cast<const unsigned char*>(e & ~3ull);
-            const long long vd = src == 0 ? vdiff0 : (src == 1 ? vdiff1 : vdiff2);
-            const int nb = e ? 16 : 0;
-            const unsigned char* ks = e ? kp + ch * 16 : reinterpret_cast<const unsigned char*>(a.q);
-            const unsigned char* vs = e ? kp + vd + ch * 16 : reinterpret_cast<const unsigned char*>(a.q);
-            const uint32_t dst = sb + i * AT_ROWB + ((ch ^ (i & 7)) << 4);
-            cp_async16(dst, ks, nb);
-            cp_async16(dst + AT_TILE * AT_ROWB, vs, nb);
+            for (int q = 0; q < AT_ROWB / 16; ++q)
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst + 16 * q), "r"(0u) : "memory");
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         }
     };
 
-#pragma unroll
-    for (int it = 0; it < AT_STAGES - 1; ++it) {
-        if (it < my_tiles) issue(it);
-        cp_async_commit();
-    }
+    int issued = 0, waited = 0;
+    bool failed = false;
+    for (; issued < AT_STAGES - 1 && issued < my_tiles; ++issued) issue(issued);
     for (int it = 0; it < my_tiles; ++it) {
-        if (it + AT_STAGES - 1 < my_tiles) issue(it + AT_STAGES - 1);
-        cp_async_commit();
-        cp_async_wait<AT_STAGES - 1>();
+        if (issued < my_tiles) issue(issued++);
+        const int st = it % AT_STAGES;
+        if (!mbar_wait_warp(wbars + 8 * st, (uint32_t)((it / AT_STAGES) & 1))) {
+            failed = true;
+            break;
+        }
+        ++waited;
         __syncwarp();
         const int t = warp + it * AT_WARPS;
-        const uint32_t kb = wbuf + (it % AT_STAGES) * AT_STAGE_BYTES;
-        const uint32_t vb = kb + AT_TILE * AT_ROWB;
+        const uint32_t kb = wring + st * AT_STAGE_BYTES;
+        const uint32_t vb = kb + AT_TILE * AT_PITCH;
         float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int row = (lane & 7) + ((lane >> 4) << 3);
             const int cc = 2 * j + ((lane >> 3) & 1);
             uint32_t b0, b1, b2, b3;
-            ldsm_x4(kb + row * AT_ROWB + ((cc ^ (row & 7)) << 4), b0, b1, b2, b3);
+            ldsm_x4(kb + row * AT_PITCH + (cc << 4), b0, b1, b2, b3);
             mma_bf16(s0, qa[j][0], 0u, qa[j][1], 0u, b0, b1);
             mma_bf16(s1, qa[j][0], 0u, qa[j][1], 0u, b2, b3);
         }
@@ -221,13 +259,19 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             const int row = (lane & 7) + (((lane >> 3) & 1) << 3);
             const int cc = u + (lane >> 4);
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vb + row * AT_ROWB + ((cc ^ (row & 7)) << 4), b0, b1, b2, b3);
+            ldsm_x4_t(vb + row * AT_PITCH + (cc << 4), b0, b1, b2, b3);
             mma_bf16(o[u], pa0, 0u, pa2, 0u, b0, b1);
             mma_bf16(o[u + 1], pa0, 0u, pa2, 0u, b2, b3);
         }
         __syncwarp();
     }
-    cp_async_wait<0>();
+    if (failed) {
+        // a wait gave up: report it, then let the copies still in flight land
+        // (bounded again) before the ring is reused by the merge below
+        if (lane == 0 && a.status) atomicOr(a.status, 1);
+        for (int it = waited; it < issued; ++it)
+            (void)mbar_wait_warp(wbars + 8 * (it % AT_STAGES), (uint32_t)((it / AT_STAGES) & 1));
+    }
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     __syncthreads();
@@ -275,22 +319,69 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // Parallel merge.  Warp g reduces query head g's (m, l) over the splits
+    // (lanes stride the splits, loads independent) and leaves one weight
+    // 2^(m_q - M) per split in shared memory; then every thread sums float4
+    // columns of the partial outputs over a share of the splits, so the loads
+    // of different splits are in flight together instead of one L2 round trip
+    // per split.  The ring is free by now: red[] / sL[] / wsm[] reuse it.
     const size_t hb = (size_t)h * a.splits * a.G;
-    for (int e = threadIdx.x; e < a.G * 128; e += blockDim.x) {
-        const int gg = e >> 7, d = e & 127;
+    float4* red = reinterpret_cast<float4*>(att_smem);                   // [P][G*32]
+    float* sL = reinterpret_cast<float*>(att_smem + 256 * sizeof(float4));  // [8]
+    float* wsm = sL + 8;                                                    // [splits][G]
+    if (warp < a.G) {
         float M = -INFINITY;
-        for (int q = 0; q < a.splits; ++q) M = fmaxf(M, __ldcg(&a.part_ml[(hb + (size_t)q * a.G + gg) * 2]));
-        float acc = 0.0f, L = 0.0f;
-        if (M != -INFINITY) {
-            for (int q = 0; q < a.splits; ++q) {
-                const size_t pb = hb + (size_t)q * a.G + gg;
-                const float f = exp2f(__ldcg(&a.part_ml[pb * 2]) - M);
-                acc += __ldcg(&a.part_o[pb * 128 + d]) * f;
-                L += __ldcg(&a.part_ml[pb * 2 + 1]) * f;
-            }
+        for (int q = lane; q < a.splits; q += 32) M = fmaxf(M, __ldcg(&a.part_ml[(hb + (size_t)q * a.G + warp) * 2]));
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+        float L = 0.0f;
+        for (int q = lane; q < a.splits; q += 32) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(&a.part_ml[(hb + (size_t)q * a.G + warp) * 2]));
+            const float f = M == -INFINITY ? 0.0f : exp2f(ml.x - M);
+            wsm[q * a.G + warp] = f;
+            L += ml.y * f;
         }
-        const float r = L > 0.0f ? acc / L : 0.0f;
-        reinterpret_cast<__nv_bfloat16*>(a.out)[((size_t)h * a.G + gg) * 128 + d] = __float2bfloat16_rn(r);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        if (lane == 0) sL[warp] = L;
+    }
+    __syncthreads();
+    const int cols = a.G * 32;  // float4 columns of the [G][128] output
+    const int P = (AT_WARPS * 32) / cols;
+    if ((int)threadIdx.x < P * cols) {
+        const int col = threadIdx.x % cols, ph = threadIdx.x / cols;
+        const int gg = col >> 5, d4 = col & 31;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+        for (int q = ph; q < a.splits; q += P) {
+            const size_t pb = hb + (size_t)q * a.G + gg;
+            const float f = wsm[q * a.G + gg];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + pb * 128) + d4);
+            acc.x += v.x * f;
+            acc.y += v.y * f;
+            acc.z += v.z * f;
+            acc.w += v.w * f;
+        }
+        red[ph * cols + col] = acc;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < cols) {
+        const int col = threadIdx.x, gg = col >> 5, d4 = col & 31;
+        float4 acc = red[col];
+        for (int ph = 1; ph < P; ++ph) {
+            const float4 v = red[ph * cols + col];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float L = sL[gg];
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        uint2 packed;
+        packed.x = pack_bf16(acc.x * inv, acc.y * inv);
+        packed.y = pack_bf16(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + ((size_t)h * a.G + gg) * 128 + 4 * d4) =
+            packed;
     }
     if (threadIdx.x == 0) a.counters[h] = 0;
 }
@@ -318,14 +409,28 @@ __global__ void imi_combine_kernel(AttnArgs a) {
 size_t attn_smem_bytes(const AttnArgs& a) {
     int chunk = (a.exec_capacity + a.splits - 1) / a.splits;
     chunk = (chunk + AT_TILE - 1) & ~(AT_TILE - 1);
-    return (size_t)AT_RING_BYTES + (size_t)chunk * 8;
+    return (size_t)AT_RING_BYTES + AT_BAR_BYTES + (size_t)chunk * 4;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     const size_t sm = attn_smem_bytes(a);
     cudaError_t e = cudaFuncSetAttribute(imi_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return e;
-    imi_attn_kernel<<<dim3(a.splits, a.bg), AT_WARPS * 32, sm, st>>>(a);
+    // programmatic dependent launch: the CTAs may start (barrier set-up) while
+    // the kernel before them in the stream finishes; they wait for it with
+    // griddepcontrol.wait before their first global read
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.splits, a.bg);
+    cfg.blockDim = dim3(AT_WARPS * 32);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, imi_attn_kernel, a);
+    if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess || a.counters) return e;
     imi_combine_kernel<<<a.bg, 512, 0, st>>>(a);

@@ -110,6 +110,9 @@ static int check_attention(const imi_attn_desc* d) {
     if (!aligned16(d->list_keys) || !aligned16(d->list_values) || !aligned16(d->static_keys) ||
         !aligned16(d->static_values) || !aligned16(d->q))
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: K/V/q buffers must be 16-byte aligned");
+    if (!aligned16(d->part_o) || (reinterpret_cast<uintptr_t>(d->part_ml) & 7u) != 0 ||
+        (reinterpret_cast<uintptr_t>(d->out) & 7u) != 0)
+        return fail(IMI_ERR_INVALID, "imi_sparse_attention: part_o must be 16-byte and part_ml/out 8-byte aligned");
     if (d->exec_capacity <= 0) return fail(IMI_ERR_INVALID, "imi_sparse_attention: exec_capacity must be positive");
     if (imi::attn_smem_bytes(*d) > 227 * 1024)
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: too few splits for the row capacity (raise splits)");

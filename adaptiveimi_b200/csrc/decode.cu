@@ -4,8 +4,8 @@
 //                           centroids (compute_impl.cu:62-103)
 //   (cell selection: select.cu; gather attention: attention.cu)
 //   imi_append_kernel       steady-zone append (runtime.py:378-392)
-//   imi_async_assign_kernel batched decode-time cell assignment and running
-//                           mean update (async_update.py:77-162)
+//   imi_async_score_kernel  batched decode-time cell assignment (argmax) and
+//   imi_async_finish_kernel running-mean update (async_update.py:77-162)
 //   imi_apply_kernel        publish updated cell centroids (async_update.py:7-19)
 #include "common.cuh"
 #include "imi_internal.h"
@@ -79,55 +79,111 @@ __global__ void imi_append_kernel(AppendArgs a) {
 //                           delta ring
 // ----------------------------------------------------------------------------
 constexpr int ASYNC_CHUNK = 512;
+constexpr int ASYNC_BMAX = 64;  // batch limit (checked by the C ABI)
+
+// Leading dimension of a transposed [sub][k] centroid table (odd: a warp
+// reading one row at scattered columns spreads over the banks).
+__host__ __device__ inline int as_ld(int k) { return (k & 1) ? k + 2 : k + 1; }
+__host__ __device__ inline int as_bpad(int B) { return (B + 3) & ~3; }
+
+// Shared-memory plan of the score kernel, in floats: keys transposed
+// [dim][bpad], prefix values [B][table], the transposed subspace tables, then
+// the per-warp winners (8-byte aligned).
+struct AsyncPlan {
+    int S, sub, table, bpad;
+    size_t kf, tab, tables, total_floats;
+    __host__ __device__ AsyncPlan(const AsyncArgs& a) {
+        S = a.parts == 0 ? 1 : a.parts;
+        sub = a.dim / S;
+        table = 1;
+        for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
+        bpad = as_bpad(a.batch);
+        kf = (size_t)a.dim * bpad;
+        tab = (size_t)a.batch * table;
+        tables = 0;
+        if (S > 1)
+            for (int s = 0; s < S; ++s) tables += (size_t)sub * as_ld(a.ks[s]);
+        total_floats = kf + tab + tables;
+    }
+};
+
+IMI_DEV void as_cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
 
 __global__ void __launch_bounds__(ASYNC_CHUNK) imi_async_score_kernel(AsyncArgs a) {
     extern __shared__ __align__(16) unsigned char as_smem[];
     const int h = blockIdx.y;
     const int tid = threadIdx.x;
-    const int S = a.parts == 0 ? 1 : a.parts;
-    const int sub = a.dim / S;
+    const AsyncPlan pl(a);
+    const int S = pl.S, sub = pl.sub, table = pl.table, bp = pl.bpad;
     const int B = a.batch;
     const size_t hs = h;
-    int table = 1;
-    for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
     const int k_last = a.ks[S - 1];
-    float* kf = reinterpret_cast<float*>(as_smem);                  // [B][dim]
-    float* tab = kf + (size_t)B * a.dim;                            // [B][table]
-    float* cT = tab + (size_t)B * table;                            // [sub][k_last+1] (S > 1)
+    float* kfT = reinterpret_cast<float*>(as_smem);  // [dim][bp]
+    float* tab = kfT + pl.kf;                         // [B][table]
+    float* cT = tab + pl.tab;                         // last subspace [sub][ld(k_last)]
+    const int ldT = as_ld(k_last);
+    float* cP = cT + (S > 1 ? (size_t)sub * ldT : 0);  // prefix subspaces back to back
     unsigned long long* wbest = reinterpret_cast<unsigned long long*>(
-        (reinterpret_cast<uintptr_t>(cT + (S > 1 ? (size_t)sub * (k_last + 1) : 0)) + 15) & ~uintptr_t(15));
-    for (int e = tid; e < B * a.dim; e += blockDim.x) {
-        const int b = e / a.dim, d = e - b * a.dim;
-        kf[e] = bf16_bits_to_f32(a.batch_keys[(hs * a.batch_cap + b) * a.dim + d]);
-    }
+        (reinterpret_cast<uintptr_t>(kfT + pl.total_floats) + 15) & ~uintptr_t(15));
+
+    // every load up front: the subspace tables by cp.async (transposed), the
+    // batch keys and this thread's slot metadata into registers
     const float* subc = a.sub_centroids + hs * (size_t)S * a.kmax * sub;
+    int poff[4] = {0, 0, 0, 0};
     if (S > 1) {
-        const float* cl = subc + (size_t)(S - 1) * a.kmax * sub;
-        for (int e = tid; e < k_last * sub; e += blockDim.x) {
-            const int i = e / sub, d = e - i * sub;
-            cT[d * (k_last + 1) + i] = cl[(size_t)i * sub + d];
+        int off = 0;
+        for (int s = 0; s < S - 1; ++s) {
+            poff[s] = off;
+            off += sub * as_ld(a.ks[s]);
         }
-        for (int b = tid; b < B; b += blockDim.x) tab[(size_t)b * table] = 0.0f;
+        for (int s = 0; s < S; ++s) {
+            const int k = a.ks[s], ld = as_ld(k);
+            float* dst = s == S - 1 ? cT : cP + poff[s];
+            const float* src = subc + (size_t)s * a.kmax * sub;
+            for (int e = tid; e < k * sub; e += ASYNC_CHUNK) {
+                const int i = e / sub, d = e - i * sub;
+                as_cp_async4(dst + d * ld + i, src + e);
+            }
+        }
     }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    const int c = blockIdx.x * ASYNC_CHUNK + tid;
+    int cc = -1;
+    bool dirty = false;
+    if (c < a.n_slots) {
+        cc = a.cell_code[hs * a.n_slots + c];
+        dirty = a.shadow_dirty && a.shadow_dirty[hs * a.n_slots + c];
+    }
+    for (int e = tid; e < B * a.dim; e += ASYNC_CHUNK) {
+        const int b = e / a.dim, d = e - b * a.dim;
+        kfT[d * bp + b] = bf16_bits_to_f32(a.batch_keys[(hs * a.batch_cap + b) * a.dim + d]);
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
     __syncthreads();
+
+    // prefix values over the first S-1 subspaces, per key (level by level)
     if (S > 1) {
         int width = 1;
         for (int s = 0; s < S - 1; ++s) {
-            const int ks = a.ks[s];
+            const int ks = a.ks[s], ld = as_ld(ks);
             const int total = width * ks;
-            const float* cs = subc + (size_t)s * a.kmax * sub;
+            const float* cs = cP + poff[s];
             float vals[32];
             int cnt = 0;
-            for (int e = tid; e < B * total && cnt < 32; e += blockDim.x, ++cnt) {
+            for (int e = tid; e < B * total && cnt < 32; e += ASYNC_CHUNK, ++cnt) {
                 const int b = e / total, r = e - b * total;
                 const int pi = r / ks, i = r - pi * ks;
-                float acc = tab[(size_t)b * table + pi];
-                for (int d = 0; d < sub; ++d) acc = __fmaf_rn(kf[b * a.dim + s * sub + d], cs[(size_t)i * sub + d], acc);
+                float acc = s == 0 ? 0.0f : tab[(size_t)b * table + pi];
+                for (int d = 0; d < sub; ++d) acc = __fmaf_rn(kfT[(s * sub + d) * bp + b], cs[d * ld + i], acc);
                 vals[cnt] = acc;
             }
-            __syncthreads();
+            if (s > 0) __syncthreads();
             cnt = 0;
-            for (int e = tid; e < B * total && cnt < 32; e += blockDim.x, ++cnt) {
+            for (int e = tid; e < B * total && cnt < 32; e += ASYNC_CHUNK, ++cnt) {
                 const int b = e / total, r = e - b * total;
                 tab[(size_t)b * table + r] = vals[cnt];
             }
@@ -135,41 +191,68 @@ __global__ void __launch_bounds__(ASYNC_CHUNK) imi_async_score_kernel(AsyncArgs 
             width = total;
         }
     }
-    // one slot per thread, every key of the batch
-    const int c = blockIdx.x * ASYNC_CHUNK + tid;
+
+    // One slot per thread, every key of the batch, 16 keys at a time (each
+    // centroid column is loaded once for all of them).  A padding slot whose
+    // shadow row was never updated holds zeros, and its d-ordered fma chain
+    // from +0 stays exactly +0: it scores 0 without a load.  Updated slots (and
+    // every slot of a flat index) run the full chain over their shadow row.
     const int lane = tid & 31, w = tid >> 5;
-    const float* shadow = a.shadow + hs * a.n_slots * (size_t)a.dim;
-    int cc = -1, pidx = 0, il = 0;
-    bool full = true;
-    if (c < a.n_slots) {
-        cc = a.cell_code[hs * a.n_slots + c];
-        full = (S == 1 || cc < 0 || (a.shadow_dirty && a.shadow_dirty[hs * a.n_slots + c]));
-        if (!full) {
-            for (int t = 0; t < S - 1; ++t) pidx = pidx * a.ks[t] + ((cc >> (8 * t)) & 0xff);
-            il = (cc >> (8 * (S - 1))) & 0xff;
-        }
+    const bool valid = c < a.n_slots;
+    const bool pad = valid && cc < 0 && !dirty;
+    const bool full = valid && !pad && (S == 1 || dirty);
+    int pidx = 0, il = 0;
+    if (valid && !pad && !full) {
+        for (int t = 0; t < S - 1; ++t) pidx = pidx * a.ks[t] + ((cc >> (8 * t)) & 0xff);
+        il = (cc >> (8 * (S - 1))) & 0xff;
     }
-    for (int b = 0; b < B; ++b) {
-        unsigned long long key = 0ull;
-        if (c < a.n_slots) {
-            float s;
-            if (full) {
-                const float* row = shadow + (size_t)c * a.dim;
-                s = 0.0f;
-                for (int d = 0; d < a.dim; ++d) s = __fmaf_rn(kf[b * a.dim + d], row[d], s);
-            } else {
-                s = tab[(size_t)b * table + pidx];
-                const float* kq = kf + b * a.dim + (S - 1) * sub;
-#pragma unroll 8
-                for (int d = 0; d < sub; ++d) s = __fmaf_rn(kq[d], cT[d * (k_last + 1) + il], s);
+    const float* row = a.shadow + (hs * a.n_slots + (valid ? c : 0)) * (size_t)a.dim;
+    for (int b0 = 0; b0 < B; b0 += 16) {
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+        if (full) {
+            for (int d = 0; d < a.dim; ++d) {
+                const float r = row[d];
+                const float4* kv = reinterpret_cast<const float4*>(kfT + d * bp + b0);
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 k4 = kv[j4];
+                    acc[4 * j4 + 0] = __fmaf_rn(k4.x, r, acc[4 * j4 + 0]);
+                    acc[4 * j4 + 1] = __fmaf_rn(k4.y, r, acc[4 * j4 + 1]);
+                    acc[4 * j4 + 2] = __fmaf_rn(k4.z, r, acc[4 * j4 + 2]);
+                    acc[4 * j4 + 3] = __fmaf_rn(k4.w, r, acc[4 * j4 + 3]);
+                }
             }
-            key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)c);
+        } else if (valid && !pad) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = b0 + j < B ? tab[(size_t)(b0 + j) * table + pidx] : 0.0f;
+            const int dk = (S - 1) * sub;
+            for (int d = 0; d < sub; ++d) {
+                const float r = cT[d * ldT + il];
+                const float4* kv = reinterpret_cast<const float4*>(kfT + (dk + d) * bp + b0);
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 k4 = kv[j4];
+                    acc[4 * j4 + 0] = __fmaf_rn(k4.x, r, acc[4 * j4 + 0]);
+                    acc[4 * j4 + 1] = __fmaf_rn(k4.y, r, acc[4 * j4 + 1]);
+                    acc[4 * j4 + 2] = __fmaf_rn(k4.z, r, acc[4 * j4 + 2]);
+                    acc[4 * j4 + 3] = __fmaf_rn(k4.w, r, acc[4 * j4 + 3]);
+                }
+            }
         }
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other > key ? other : key;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (b0 + j >= B) break;  // uniform over the block
+            unsigned long long key =
+                valid ? ((unsigned long long)ord_f32(acc[j]) << 32) | (0xffffffffu - (uint32_t)c) : 0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            if (lane == 0) wbest[w * B + b0 + j] = key;
         }
-        if (lane == 0) wbest[w * B + b] = key;
     }
     __syncthreads();
     for (int b = tid; b < B; b += blockDim.x) {
@@ -179,13 +262,19 @@ __global__ void __launch_bounds__(ASYNC_CHUNK) imi_async_score_kernel(AsyncArgs 
     }
 }
 
+// One CTA per group.  The batch keys' winning cells; then, per distinct cell
+// (first occurrence in token order), its delta sum gains the cell's keys in
+// token order and, once its delta count reaches the threshold, the running
+// mean replaces its shadow row -- one thread per (cell, d), no sequential walk
+// over the batch; then the delta ring.
 __global__ void __launch_bounds__(256) imi_async_finish_kernel(AsyncArgs a) {
     const int h = blockIdx.x;
     const int tid = threadIdx.x;
     const int B = a.batch;
     const size_t hs = h;
-    __shared__ int ids[64];
-    __shared__ float kf[64 * 128];
+    __shared__ int ids[ASYNC_BMAX];
+    __shared__ int first[ASYNC_BMAX], ucnt[ASYNC_BMAX], dcold[ASYNC_BMAX], cold[ASYNC_BMAX];
+    __shared__ float kf[ASYNC_BMAX * 128];
     for (int e = tid; e < B * a.dim; e += blockDim.x) {
         const int b = e / a.dim, d = e - b * a.dim;
         kf[e] = bf16_bits_to_f32(a.batch_keys[(hs * a.batch_cap + b) * a.dim + d]);
@@ -196,47 +285,52 @@ __global__ void __launch_bounds__(256) imi_async_finish_kernel(AsyncArgs a) {
         ids[tid] = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
     }
     __syncthreads();
-    // delta counts / sums in token order (one warp walks the batch)
-    if (tid < 32) {
-        for (int b = 0; b < B; ++b) {
-            const int cid = ids[b];
-            float* ds = a.delta_sums + (hs * a.n_slots + cid) * (size_t)a.dim;
-            for (int d = tid; d < a.dim; d += 32) ds[d] = __fadd_rn(ds[d], kf[b * a.dim + d]);
-            if (tid == 0) a.delta_counts[hs * a.n_slots + cid] += 1;
-            __syncwarp();
+    if (tid < B) {
+        const int cid = ids[tid];
+        bool f = true;
+        for (int e = 0; e < tid; ++e)
+            if (ids[e] == cid) f = false;
+        int cnt = 0;
+        for (int e = tid; e < B; ++e) cnt += ids[e] == cid;
+        first[tid] = f;
+        ucnt[tid] = cnt;
+        if (f) {
+            const size_t cs = hs * a.n_slots + cid;
+            dcold[tid] = a.delta_counts[cs];
+            cold[tid] = a.counts[cs];
         }
     }
     __syncthreads();
-    // running mean for cells that reached the threshold; each touched cell once
-    for (int b = 0; b < B; ++b) {
+    for (int e = tid; e < B * a.dim; e += blockDim.x) {
+        const int b = e / a.dim, d = e - b * a.dim;
+        if (!first[b]) continue;
         const int cid = ids[b];
-        bool first = true;
-        for (int e = 0; e < b; ++e)
-            if (ids[e] == cid) first = false;
-        if (!first) continue;
         const size_t cs = hs * a.n_slots + cid;
-        const int dc = a.delta_counts[cs];
-        __syncthreads();
+        float* dsp = a.delta_sums + cs * a.dim + d;
+        float ds = *dsp;
+        for (int bb = b; bb < B; ++bb)
+            if (ids[bb] == cid) ds = __fadd_rn(ds, kf[bb * a.dim + d]);
+        const int dc = dcold[b] + ucnt[b];
         if (dc >= a.threshold) {
-            const int cnt = a.counts[cs];
-            const int nc = cnt + dc;
+            const int nc = cold[b] + dc;
             const float denom = (float)max(nc, 1);
-            const float fc = (float)cnt;
-            float* row = a.shadow + cs * a.dim;
-            float* ds = a.delta_sums + cs * a.dim;
-            for (int d = tid; d < a.dim; d += blockDim.x) {
-                row[d] = __fdiv_rn(__fadd_rn(__fmul_rn(row[d], fc), ds[d]), denom);
-                ds[d] = 0.0f;
-            }
-            __syncthreads();
-            if (tid == 0) {
-                a.counts[cs] = nc;
-                a.delta_counts[cs] = 0;
-                if (a.shadow_dirty) a.shadow_dirty[cs] = 1;
-                if (a.pending) a.pending[cs] = 1;
-            }
+            float* rp = a.shadow + cs * a.dim + d;
+            *rp = __fdiv_rn(__fadd_rn(__fmul_rn(*rp, (float)cold[b]), ds), denom);
+            ds = 0.0f;
         }
-        __syncthreads();
+        *dsp = ds;
+    }
+    if (tid < B && first[tid]) {
+        const size_t cs = hs * a.n_slots + ids[tid];
+        const int dc = dcold[tid] + ucnt[tid];
+        if (dc >= a.threshold) {
+            a.counts[cs] = cold[tid] + dc;
+            a.delta_counts[cs] = 0;
+            if (a.shadow_dirty) a.shadow_dirty[cs] = 1;
+            if (a.pending) a.pending[cs] = 1;
+        } else {
+            a.delta_counts[cs] = dc;
+        }
     }
     // delta ring (async_update.py:146-161)
     const int wp = a.ring_write_pos[h];
@@ -259,18 +353,25 @@ __global__ void __launch_bounds__(256) imi_async_finish_kernel(AsyncArgs a) {
 
 // Publish the updated cells: live[c] = shadow[c] for slots flagged pending
 // (async_update.py:7-19 copies the whole shadow; only changed rows differ).
+// Each warp checks 32 slots with one ballot and copies the flagged rows.
 __global__ void imi_apply_kernel(ApplyArgs a) {
     const int h = blockIdx.y;
     const size_t hs = h;
-    for (int c = blockIdx.x; c < a.n_slots; c += gridDim.x) {
-        const size_t cs = hs * a.n_slots + c;
-        if (!a.pending[cs]) continue;
-        for (int d = threadIdx.x; d < a.dim; d += blockDim.x) a.live[cs * a.dim + d] = a.shadow[cs * a.dim + d];
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            a.pending[cs] = 0;
-            a.live_dirty[cs] = 1;
-        }
+    const int lane = threadIdx.x & 31;
+    const int c0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
+    if (c0 >= a.n_slots) return;
+    const int c = c0 + lane;
+    const bool pend = c < a.n_slots && a.pending[hs * a.n_slots + c];
+    unsigned m = __ballot_sync(0xffffffffu, pend);
+    while (m) {
+        const int q = __ffs(m) - 1;
+        m &= m - 1;
+        const size_t cs = hs * a.n_slots + c0 + q;
+        for (int d = lane; d < a.dim; d += 32) a.live[cs * a.dim + d] = a.shadow[cs * a.dim + d];
+    }
+    if (pend) {
+        a.pending[hs * a.n_slots + c] = 0;
+        a.live_dirty[hs * a.n_slots + c] = 1;
     }
 }
 
@@ -290,12 +391,8 @@ cudaError_t launch_append(const AppendArgs& a, cudaStream_t st) {
 }
 
 size_t async_smem_bytes(const AsyncArgs& a) {
-    const int S = a.parts == 0 ? 1 : a.parts;
-    int table = 1;
-    for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
-    const size_t ct = S > 1 ? (size_t)(a.dim / S) * (a.ks[S - 1] + 1) : 0;
-    return sizeof(float) * ((size_t)a.batch * a.dim + (size_t)a.batch * table + ct) + 16 +
-           8 * (size_t)(ASYNC_CHUNK / 32) * a.batch + 64;
+    const AsyncPlan pl(a);
+    return sizeof(float) * pl.total_floats + 16 + 8 * (size_t)(ASYNC_CHUNK / 32) * a.batch;
 }
 
 int async_chunks(int n_slots) { return (n_slots + ASYNC_CHUNK - 1) / ASYNC_CHUNK; }
@@ -311,7 +408,8 @@ cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st) {
-    imi_apply_kernel<<<dim3(min(a.n_slots, 256), a.bg), 128, 0, st>>>(a);
+    const int warps = (a.n_slots + 31) / 32;  // 4 warps (128 slots) per CTA
+    imi_apply_kernel<<<dim3((warps + 3) / 4, a.bg), 128, 0, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -18,24 +18,33 @@
 //
 // Each rule is monotone in rank, so the selected set is the rank prefix that
 // ends before the first element A violating a rule.  A is found by histogram
-// refinement over the 64-bit key range (key = score bits, then the complement
-// of the slot, so keys are unique): a round histograms the candidates into
-// 2048 power-of-two buckets of the key range weighted by (1, tokens, pages), a
-// block-wide descending scan finds the first bucket where a rule can fire, and
-// once that bucket holds at most 32 elements one warp ranks them and walks the
-// rules exactly.  The boundary with all three rules (the selected cells) and
-// the boundary without the page rule (the kept list that delta rows match
-// against) come out of the same pass.  Attention does not depend on row order,
-// so the selected cells are emitted in slot order without a sort.
+// refinement: a round histograms the candidates into 2048 buckets weighted by
+// (count, pages) packed in one 64-bit word and by tokens, a block-wide
+// descending scan finds the first bucket where a rule can fire, and once that
+// bucket holds at most 32 elements one warp ranks them and walks the rules
+// exactly.  The first round uses buckets linear in the score; the rare
+// fallback refines power-of-two ranges of the 64-bit key (score bits, then the
+// complement of the slot, so keys are unique).  The boundary with all three
+// rules (the selected cells) and the boundary without the page rule (the kept
+// list that delta rows match against) come out of the same pass.  Attention
+// does not depend on row order, so the selected cells are emitted in slot
+// order without a sort.
 //
 // The kernel sits on the decode critical path (attention waits on it), so it
-// is written for latency: a cluster of 8 CTAs per KV group scores the cells
-// (subspace centroids staged transposed in shared memory, two interleaved fma
-// chains per thread) and stores every key and size straight into the leader
-// CTA's shared memory through DSMEM; the leader alone then runs the boundary
-// search and emits the rows (warp-contiguous slot ranges, ballot ranks).  Two
-// cluster barriers in all.
+// is written for latency.  A cluster of 8 CTAs serves one KV group.  Every
+// CTA issues all of its global loads at once -- the subspace centroids
+// (4-byte cp.async straight into a transposed shared-memory layout), its
+// slice of the cell codes, masks and sizes, and the query -- and waits once.
+// It then scores its slice (two to four interleaved fma chains per thread)
+// and stores every key and size straight into the leader CTA's shared memory
+// through DSMEM.  The first cluster barrier is split (arrive at entry, wait
+// just before the first DSMEM store) so it costs nothing.  The leader alone
+// runs the boundary search, ranks the selected cells by warp ballots in slot
+// order, computes their row offsets with one block scan and writes the rows
+// with every warp.
 #include <cooperative_groups.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "imi_internal.h"
@@ -50,11 +59,16 @@ constexpr int SL_WARPS = SL_THREADS / 32;
 constexpr int SL_NB = 2048;             // histogram buckets per refinement round (2^11)
 constexpr int SL_NB_BITS = 11;
 constexpr int SL_MAX_SLOTS = 16384;     // keys and sizes live in the leader's shared memory
+constexpr int SL_CPT = SL_MAX_SLOTS / SL_CL / SL_THREADS;  // cells per thread when scoring (<= 4)
+constexpr int SL_SEL_MAX = 2048;        // selected cells at most (nprobe <= 2048)
 
 struct SelHdr {
     unsigned long long kmin, kmax;
-    int hist[3][SL_NB];
-    int red[64];
+    unsigned long long hcp[SL_NB];  // per bucket: (count << 32) | pages
+    unsigned int hsz[SL_NB];        // per bucket: tokens
+    unsigned long long red64[SL_WARPS];
+    unsigned int red32[SL_WARPS];
+    int redi[SL_WARPS];
     // boundary with all three rules
     unsigned long long bkeys[32];
     int bsz[32];
@@ -67,9 +81,21 @@ struct SelHdr {
     int nb2, first2, bucket2, bcnt2;
     long long pre2[3];
     unsigned long long T2;
-    int wsel[SL_WARPS], wrows[SL_WARPS], wkept[SL_WARPS];
+    int wsel[SL_WARPS], wkept[SL_WARPS];
+    unsigned long long rscr[2][48];  // resolve scratch per warp: 32 keys, then 32 sizes
 };
 
+// Leading dimension of a transposed [sub][k] centroid table: odd, so that a
+// warp reading one row at scattered columns spreads over the banks.
+__host__ __device__ inline int sl_ld(int k) { return (k & 1) ? k + 2 : k + 1; }
+
+IMI_DEV void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+
+// Block-wide inclusive scan of one int (all SL_THREADS threads call it).
 __device__ __forceinline__ int sl_scan(int v, int* red, int* total) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     int x = v;
@@ -78,7 +104,6 @@ __device__ __forceinline__ int sl_scan(int v, int* red, int* total) {
         const int t = __shfl_up_sync(0xffffffffu, x, o);
         if (l >= o) x += t;
     }
-    __syncthreads();
     if (l == 31) red[w] = x;
     __syncthreads();
     if (w == 0) {
@@ -97,14 +122,46 @@ __device__ __forceinline__ int sl_scan(int v, int* red, int* total) {
     return x + base;
 }
 
-__device__ __forceinline__ int warp_incl_scan(int x) {
-    const int l = threadIdx.x & 31;
+// Block-wide inclusive scan of a (64-bit, 32-bit) pair under one set of barriers.
+__device__ __forceinline__ void sl_scan_pair(unsigned long long& x, unsigned int& y, SelHdr& sm) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, x, o);
-        if (l >= o) x += t;
+        const unsigned long long tx = __shfl_up_sync(0xffffffffu, x, o);
+        const unsigned int ty = __shfl_up_sync(0xffffffffu, y, o);
+        if (l >= o) {
+            x += tx;
+            y += ty;
+        }
     }
-    return x;
+    if (l == 31) {
+        sm.red64[w] = x;
+        sm.red32[w] = y;
+    }
+    __syncthreads();
+    if (w == 0) {
+        unsigned long long xx = l < SL_WARPS ? sm.red64[l] : 0ull;
+        unsigned int yy = l < SL_WARPS ? sm.red32[l] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long tx = __shfl_up_sync(0xffffffffu, xx, o);
+            const unsigned int ty = __shfl_up_sync(0xffffffffu, yy, o);
+            if (l >= o) {
+                xx += tx;
+                yy += ty;
+            }
+        }
+        if (l < SL_WARPS) {
+            sm.red64[l] = xx;
+            sm.red32[l] = yy;
+        }
+    }
+    __syncthreads();
+    if (w > 0) {
+        x += sm.red64[w - 1];
+        y += sm.red32[w - 1];
+    }
+    __syncthreads();
 }
 
 __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
@@ -118,11 +175,10 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const int wid = tid >> 5, lid = tid & 31;
     const int S = a.parts == 0 ? 1 : a.parts;
     const int sub = a.dim / S;
+    const int sub_shift = __ffs(sub) - 1;  // sub is a power of two (128 / S)
     const int k_last = a.ks[S - 1];
     int table = 1;
     for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
-    int kpre = 1;  // largest k among the first S-1 subspaces
-    for (int s = 0; s < S - 1; ++s) kpre = max(kpre, a.ks[s]);
     const int n = a.n_slots;
     const int npad = (n + 1) & ~1;
     const bool pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
@@ -142,11 +198,15 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     p += sizeof(float) * a.dim;
     float* tab = reinterpret_cast<float*>(p);
     p += sizeof(float) * (table + 4);
-    float* cT = reinterpret_cast<float*>(p);  // last subspace, [sub][k_last + 1]
-    p += sizeof(float) * (S > 1 ? (size_t)sub * (k_last + 1) : 0);
-    float* cP = reinterpret_cast<float*>(p);  // one prefix subspace at a time, [sub][kpre + 1]
-    int* sel_slot = reinterpret_cast<int*>(cP);  // leader, reused after scoring
-    int* sel_start = sel_slot + 2048;
+    // transposed centroid tables: the last subspace [sub][ld(k_last)], then
+    // the prefix subspaces back to back; the leader reuses the region for the
+    // selected-cell lists once scoring is over
+    float* cT = reinterpret_cast<float*>(p);
+    const int ldT = sl_ld(k_last);
+    float* cP = cT + (S > 1 ? sub * ldT : 0);
+    int* sel_slot = reinterpret_cast<int*>(p);
+    int* sel_start = sel_slot + SL_SEL_MAX;
+    int* sel_off = sel_start + SL_SEL_MAX;
 
     const size_t hs = (size_t)h;
     auto stamp = [&](int k) {
@@ -157,6 +217,17 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         }
     };
     stamp(0);
+    // let the attention kernel that follows (a programmatic dependent launch)
+    // start setting up on the SMs this kernel leaves free
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    if (rank == 0 && tid == 0) {
+        sm.kmin = ~0ull;
+        sm.kmax = 0ull;
+    }
+    // first half of the cluster barrier that guards the DSMEM stores: every
+    // CTA is running and the leader's header is set
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+
     const int32_t* sizes = a.cell_sizes + hs * n;
     const uint8_t* mask = a.cell_mask + hs * n;
     const int32_t* code = a.cell_code + hs * n;
@@ -164,9 +235,41 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const float* merged = a.centroids + hs * n * (size_t)a.dim;
     const float* subc = a.sub_centroids + hs * (size_t)S * a.kmax * sub;
 
-    // ---------------- every CTA: q_sum, last subspace, prefix sums ----------------
-    // all staging loads are issued before the first barrier
-    // q_sum: every load of a thread is issued before the adds
+    // ---------------- every CTA: all global loads at once ----------------
+    int poff[4] = {0, 0, 0, 0};  // offsets of the prefix tables within cP
+    if (S > 1) {
+        int off = 0;
+        for (int s = 0; s < S - 1; ++s) {
+            poff[s] = off;
+            off += sub * sl_ld(a.ks[s]);
+        }
+        for (int s = 0; s < S; ++s) {
+            const int k = a.ks[s];
+            float* dst = s == S - 1 ? cT : cP + poff[s];
+            const int ld = sl_ld(k);
+            const float* src = subc + (size_t)s * a.kmax * sub;
+            const int total = k * sub;
+            for (int e = tid; e < total; e += SL_THREADS) {
+                const int i = e >> sub_shift, d = e & (sub - 1);
+                cp_async4(dst + d * ld + i, src + e);
+            }
+        }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    const int chunk = (n + SL_CL - 1) / SL_CL;
+    const int c0 = rank * chunk;
+    const int c1 = min(n, c0 + chunk);
+    int ccv[SL_CPT], szv[SL_CPT];
+    bool mkv[SL_CPT], dkv[SL_CPT];
+#pragma unroll
+    for (int j = 0; j < SL_CPT; ++j) {
+        const int c = c0 + tid + j * SL_THREADS;
+        const bool in = c < c1;
+        ccv[j] = in ? code[c] : -1;
+        mkv[j] = in ? mask[c] != 0 : true;
+        szv[j] = in ? sizes[c] : 0;
+        dkv[j] = in && dirty ? dirty[c] != 0 : false;
+    }
     if (tid < a.dim) {
         float qv[8];
 #pragma unroll
@@ -175,146 +278,121 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, qv[g]);
         qs[tid] = acc;
     }
-    // centroid staging: batches of 16 loads in registers, then the stores
-    auto stage_T = [&](const float* src, int k, float* dst, int ld) {
-        const int total = k * sub;
-        for (int base = 0; base < total; base += 16 * SL_THREADS) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int e = base + j * SL_THREADS + tid;
-                v[j] = e < total ? src[e] : 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int e = base + j * SL_THREADS + tid;
-                if (e < total) {
-                    const int i = e / sub, d = e - i * sub;
-                    dst[d * ld + i] = v[j];
-                }
-            }
-        }
-    };
-    if (S > 1) {
-        stage_T(subc + (size_t)(S - 1) * a.kmax * sub, k_last, cT, k_last + 1);
-        stage_T(subc, a.ks[0], cP, kpre + 1);
-        if (tid == 0) tab[0] = 0.0f;
-    }
-    if (rank == 0 && tid == 0) {
-        sm.kmin = ~0ull;
-        sm.kmax = 0ull;
-    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+
+    // ---------------- every CTA: prefix table over the first S-1 subspaces ----------------
     if (S > 1) {
         int width = 1;
         for (int s = 0; s < S - 1; ++s) {
             const int ks = a.ks[s];
-            if (s > 0) {
-                __syncthreads();
-                stage_T(subc + (size_t)s * a.kmax * sub, ks, cP, kpre + 1);
-            }
-            __syncthreads();
+            const float* cs = cP + poff[s];
+            const int ld = sl_ld(ks);
             const int total = width * ks;
+            const float* qq = qs + s * sub;
             float vals[16];
             int cnt = 0;
-            for (int e = tid; e < total && cnt < 16; e += blockDim.x, ++cnt) {
+            for (int e = tid; e < total && cnt < 16; e += SL_THREADS, ++cnt) {
                 const int pi = e / ks, i = e - pi * ks;
-                float acc = tab[pi];
-                const float* qq = qs + s * sub;
+                float acc = s == 0 ? 0.0f : tab[pi];
 #pragma unroll 8
-                for (int d = 0; d < sub; ++d) acc = __fmaf_rn(qq[d], cP[d * (kpre + 1) + i], acc);
+                for (int d = 0; d < sub; ++d) acc = __fmaf_rn(qq[d], cs[d * ld + i], acc);
                 vals[cnt] = acc;
             }
-            __syncthreads();
+            if (s > 0) __syncthreads();  // every read of the previous level is done
             cnt = 0;
-            for (int e = tid; e < total && cnt < 16; e += blockDim.x, ++cnt) tab[e] = vals[cnt];
+            for (int e = tid; e < total && cnt < 16; e += SL_THREADS, ++cnt) tab[e] = vals[cnt];
+            __syncthreads();
             width = total;
         }
     }
-    __syncthreads();
     stamp(1);
-    cluster.sync();  // every CTA is running (DSMEM may be used) and the leader's header is set
-    // ---------------- every CTA: score its slots, scatter into the leader ----------------
+
+    // ---------------- every CTA: score its slice ----------------
+    const float* q2 = qs + (S - 1) * sub;
+    float acc[SL_CPT];
+    int il[SL_CPT];
+    bool sep[SL_CPT], cand[SL_CPT];
+#pragma unroll
+    for (int j = 0; j < SL_CPT; ++j) {
+        acc[j] = 0.0f;
+        il[j] = 0;
+        const int cc = ccv[j];
+        cand[j] = !mkv[j] && cc >= 0;
+        sep[j] = cand[j] && S > 1 && !dkv[j];
+        if (sep[j]) {
+            int pidx = 0;
+            for (int t = 0; t < S - 1; ++t) pidx = pidx * a.ks[t] + ((cc >> (8 * t)) & 0xff);
+            il[j] = (cc >> (8 * (S - 1))) & 0xff;
+            acc[j] = tab[pidx];
+        }
+    }
+    if (S > 1) {
+        // interleaved chains over the last subspace; the number of live cells
+        // per thread is uniform over the CTA
+        // (a cell that is not separable runs the chain on column 0 and the
+        // result is discarded)
+        auto chains = [&](auto nj) {
+            constexpr int J = decltype(nj)::value;
+            float ch[J];
+#pragma unroll
+            for (int j = 0; j < J; ++j) ch[j] = acc[j];
+            for (int d0 = 0; d0 < sub; d0 += 8) {
+                float cv[8][J], qv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    qv[u] = q2[d0 + u];
+#pragma unroll
+                    for (int j = 0; j < J; ++j) cv[u][j] = cT[(d0 + u) * ldT + il[j]];
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+#pragma unroll
+                    for (int j = 0; j < J; ++j) ch[j] = __fmaf_rn(qv[u], cv[u][j], ch[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                if (sep[j]) acc[j] = ch[j];
+        };
+        const int live = (c1 - c0 + SL_THREADS - 1) / SL_THREADS;
+        if (live <= 2)
+            chains(std::integral_constant<int, 2>{});
+        else
+            chains(std::integral_constant<int, SL_CPT>{});
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
     {
         SelHdr* lead = cluster.map_shared_rank(&sm, 0);
         unsigned long long* lkey = cluster.map_shared_rank(skey, 0);
         int* lsz = cluster.map_shared_rank(ssz, 0);
-        const int chunk = (n + SL_CL - 1) / SL_CL;
-        const int c0 = rank * chunk;
-        const int c1 = min(n, c0 + chunk);
-        const float* q2 = qs + (S - 1) * sub;
         unsigned long long kmn = ~0ull, kmx = 0ull;
-        for (int cb = c0 + tid; cb < c1; cb += 2 * SL_THREADS) {
-            // two interleaved chains per thread
-            float acc[2];
-            int il[2], ccv[2], szv[2];
-            bool sep[2], cand[2], mk[2], dk[2];
-            const int cs[2] = {cb, cb + SL_THREADS};
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int c = cs[j];
-                const bool in = c < c1;
-                ccv[j] = in ? code[c] : -1;
-                mk[j] = in ? mask[c] != 0 : true;
-                szv[j] = in ? sizes[c] : 0;
-                dk[j] = in && dirty ? dirty[c] != 0 : false;
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int c = cs[j];
-                acc[j] = 0.0f;
-                il[j] = 0;
-                sep[j] = cand[j] = false;
-                if (c < c1) {
-                    const int cc = ccv[j];
-                    if (!mk[j] && cc >= 0) {
-                        cand[j] = true;
-                        if (S > 1 && !dk[j]) {
-                            int pidx = 0;
-                            for (int t = 0; t < S - 1; ++t) pidx = pidx * a.ks[t] + ((cc >> (8 * t)) & 0xff);
-                            il[j] = (cc >> (8 * (S - 1))) & 0xff;
-                            acc[j] = tab[pidx];
-                            sep[j] = true;
-                        }
+        for (int j = 0; j < SL_CPT; ++j) {
+            const int c = c0 + tid + j * SL_THREADS;
+            if (c >= c1) continue;
+            unsigned long long key = 0ull;
+            float s = -INFINITY;
+            if (cand[j]) {
+                if (sep[j]) {
+                    s = acc[j];
+                } else {
+                    const float* row = merged + (size_t)c * a.dim;
+                    s = 0.0f;
+                    for (int d = 0; d < a.dim; d += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(row + d);
+                        s = __fmaf_rn(qs[d], v.x, s);
+                        s = __fmaf_rn(qs[d + 1], v.y, s);
+                        s = __fmaf_rn(qs[d + 2], v.z, s);
+                        s = __fmaf_rn(qs[d + 3], v.w, s);
                     }
                 }
+                key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)c);
+                kmn = min(kmn, key);
+                kmx = max(kmx, key);
             }
-            if (S > 1 && (sep[0] || sep[1])) {
-#pragma unroll 8
-                for (int d = 0; d < sub; ++d) {
-                    const float qd = q2[d];
-                    const float* row = cT + d * (k_last + 1);
-                    if (sep[0]) acc[0] = __fmaf_rn(qd, row[il[0]], acc[0]);
-                    if (sep[1]) acc[1] = __fmaf_rn(qd, row[il[1]], acc[1]);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int c = cs[j];
-                if (c >= c1) continue;
-                unsigned long long key = 0ull;
-                float s = -INFINITY;
-                if (cand[j]) {
-                    if (sep[j]) {
-                        s = acc[j];
-                    } else {
-                        const float* row = merged + (size_t)c * a.dim;
-                        s = 0.0f;
-                        for (int d = 0; d < a.dim; d += 4) {
-                            const float4 v = *reinterpret_cast<const float4*>(row + d);
-                            s = __fmaf_rn(qs[d], v.x, s);
-                            s = __fmaf_rn(qs[d + 1], v.y, s);
-                            s = __fmaf_rn(qs[d + 2], v.z, s);
-                            s = __fmaf_rn(qs[d + 3], v.w, s);
-                        }
-                    }
-                    key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)c);
-                    kmn = min(kmn, key);
-                    kmx = max(kmx, key);
-                }
-                lkey[c] = key;
-                lsz[c] = key ? szv[j] : 0;
-                if (a.scores_out) a.scores_out[hs * n + c] = s;
-            }
+            lkey[c] = key;
+            lsz[c] = key ? szv[j] : 0;
+            if (a.scores_out) a.scores_out[hs * n + c] = s;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -333,78 +411,97 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const bool any_cand = key_hi0 != 0ull;
 
     // One warp resolves a boundary bucket exactly: rank its (<= 32) elements,
-    // walk them in order applying the rules from the bucket's prefix.
+    // place them in rank order (lane r holds the element of rank r), scan their
+    // tokens and pages, and let the first lane whose rule fires name the
+    // boundary.  `scratch` holds 32 keys and 32 sizes for the warp.
     auto resolve = [&](const unsigned long long* bk, const int* bs, int m, long long xc, long long xs, long long xp,
-                       bool use_pages, unsigned long long blo, unsigned long long& T, unsigned long long& fl) {
+                       bool use_pages, unsigned long long blo, unsigned long long* scratch, unsigned long long& T,
+                       unsigned long long& fl) {
         const unsigned long long mk = lid < m ? bk[lid] : 0ull;
         const int msz = lid < m ? bs[lid] : 0;
         int rk = 0;
-        for (int q = 0; q < m; ++q) rk += (__shfl_sync(0xffffffffu, mk, q) > mk) ? 1 : 0;
-        T = blo > 0 ? blo - 1 : 0ull;
-        fl = 1ull;  // nothing fires here: the token rule fires just below this bucket
-        bool found = false;
-        for (int r = 0; r < m && !found; ++r) {
-            const unsigned hm = __ballot_sync(0xffffffffu, lid < m && rk == r);
-            const int src = __ffs(hm) - 1;
-            const unsigned long long k = __shfl_sync(0xffffffffu, mk, src);
-            const int sz = __shfl_sync(0xffffffffu, msz, src);
-            const int pg = pages_of(sz);
-            const bool rc = (xc >= a.nprobe) || (xs >= a.max_tokens);
-            const bool rp = use_pages && (xp + pg > a.buffer_pages);
-            if (rc || rp) {
-                T = k;
-                fl = rc ? 1ull : 0ull;
-                found = true;
-            } else {
-                xc += 1;
-                xs += sz;
-                xp += pg;
+#pragma unroll 8
+        for (int q = 0; q < 32; ++q) {
+            const unsigned long long o = __shfl_sync(0xffffffffu, mk, q);
+            rk += (q < m && o > mk) ? 1 : 0;
+        }
+        int* ssz2 = reinterpret_cast<int*>(scratch + 32);
+        if (lid < m) {
+            scratch[rk] = mk;
+            ssz2[rk] = msz;
+        }
+        __syncwarp();
+        const unsigned long long k = lid < m ? scratch[lid] : 0ull;
+        const int sz = lid < m ? ssz2[lid] : 0;
+        const int pg = pages_of(sz);
+        int isz = sz, ipg = pg;  // inclusive scans over the ranked elements
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ts = __shfl_up_sync(0xffffffffu, isz, o);
+            const int tp = __shfl_up_sync(0xffffffffu, ipg, o);
+            if (lid >= o) {
+                isz += ts;
+                ipg += tp;
             }
         }
+        const long long bc = xc + lid, bsum = xs + (isz - sz), bpg = xp + (ipg - pg);
+        const bool rc = (bc >= a.nprobe) || (bsum >= a.max_tokens);
+        const bool rp = use_pages && (bpg + pg > a.buffer_pages);
+        const unsigned fire = __ballot_sync(0xffffffffu, lid < m && (rc || rp));
+        if (fire) {
+            const int f = __ffs(fire) - 1;
+            T = __shfl_sync(0xffffffffu, k, f);
+            fl = __shfl_sync(0xffffffffu, rc ? 1u : 0u, f) ? 1ull : 0ull;
+        } else {
+            T = blo > 0 ? blo - 1 : 0ull;
+            fl = 1ull;  // nothing fires here: the token rule fires just below this bucket
+        }
+        __syncwarp();
     };
 
-    // Histogram of the candidates with lo <= key <= hi into power-of-two
-    // buckets, and the descending block scan; returns per-thread bucket
-    // values (thread t owns buckets SL_NB-1-4t .. SL_NB-4-4t).
+    // Per-thread view of 4 buckets after a histogram round: thread t owns
+    // buckets SL_NB-1-4t .. SL_NB-4-4t (descending), with the exclusive
+    // (count, tokens, pages) prefixes of the candidates above them.
     struct Scan {
         int cv[4], sv[4], pv[4];
-        long long ec, es, ep;  // exclusive prefixes before the thread's first bucket
+        long long ec, es, ep;
     };
-    auto histogram = [&](unsigned long long lo, unsigned long long hi, int shift, long long C, long long Sz,
-                         long long Pg, Scan& sc) {
-        for (int b = tid; b < SL_NB; b += blockDim.x) sm.hist[0][b] = sm.hist[1][b] = sm.hist[2][b] = 0;
+    auto clear_hist = [&]() {
+        for (int b = tid; b < SL_NB; b += SL_THREADS) {
+            sm.hcp[b] = 0ull;
+            sm.hsz[b] = 0u;
+        }
         if (tid == 0) {
             sm.nb = sm.nb2 = 0;
             sm.first = sm.first2 = SL_NB;
         }
         __syncthreads();
-        for (int c = tid; c < n; c += blockDim.x) {
-            const unsigned long long k = skey[c];
-            if (k == 0ull || k < lo || k > hi) continue;
-            const int b = (int)((k - lo) >> shift);
-            const int sz = ssz[c];
-            atomicAdd(&sm.hist[0][b], 1);
-            atomicAdd(&sm.hist[1][b], sz);
-            atomicAdd(&sm.hist[2][b], pages_of(sz));
-        }
-        __syncthreads();
-        int c4 = 0, s4 = 0, p4 = 0;
+    };
+    auto add_hist = [&](int b, int sz) {
+        atomicAdd(&sm.hcp[b], (1ull << 32) | (unsigned long long)(unsigned)pages_of(sz));
+        atomicAdd(&sm.hsz[b], (unsigned)sz);
+    };
+    auto scan_hist = [&](long long C, long long Sz, long long Pg, Scan& sc) {
+        unsigned long long cp4 = 0ull;
+        unsigned int s4 = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int b = SL_NB - 1 - 4 * tid - q;
-            sc.cv[q] = sm.hist[0][b];
-            sc.sv[q] = sm.hist[1][b];
-            sc.pv[q] = sm.hist[2][b];
-            c4 += sc.cv[q];
-            s4 += sc.sv[q];
-            p4 += sc.pv[q];
+            const unsigned long long v = sm.hcp[b];
+            const unsigned int w = sm.hsz[b];
+            sc.cv[q] = (int)(v >> 32);
+            sc.pv[q] = (int)(v & 0xffffffffull);
+            sc.sv[q] = (int)w;
+            cp4 += v;
+            s4 += w;
         }
-        const int ic = sl_scan(c4, sm.red, nullptr);
-        const int is = sl_scan(s4, sm.red, nullptr);
-        const int ip = sl_scan(p4, sm.red, nullptr);
-        sc.ec = C + ic - c4;
-        sc.es = Sz + is - s4;
-        sc.ep = Pg + ip - p4;
+        unsigned long long icp = cp4;
+        unsigned int is = s4;
+        sl_scan_pair(icp, is, sm);
+        const unsigned long long ecp = icp - cp4;
+        sc.ec = C + (long long)(ecp >> 32);
+        sc.ep = Pg + (long long)(ecp & 0xffffffffull);
+        sc.es = Sz + (long long)(is - s4);
     };
     auto publish = [&](const Scan& sc, int fr, int& bucket, int& bcnt, long long* pre) {
         long long xc = sc.ec, xs = sc.es, xp = sc.ep;
@@ -433,8 +530,15 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         long long C = 0, Sz = 0, Pg = 0;  // totals of candidates with key > hi
         while (true) {
             const int shift = shift_of(lo, hi);
+            clear_hist();
+            for (int c = tid; c < n; c += SL_THREADS) {
+                const unsigned long long k = skey[c];
+                if (k == 0ull || k < lo || k > hi) continue;
+                add_hist((int)((k - lo) >> shift), ssz[c]);
+            }
+            __syncthreads();
             Scan sc;
-            histogram(lo, hi, shift, C, Sz, Pg, sc);
+            scan_hist(C, Sz, Pg, sc);
             {
                 long long ec = sc.ec, es = sc.es, ep = sc.ep;
 #pragma unroll
@@ -465,7 +569,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             const unsigned long long bend = blo + ((1ull << shift) - 1ull);
             const unsigned long long bhi = (bend < blo || bend > hi) ? hi : bend;
             if (cnt <= 32) {
-                for (int c = tid; c < n; c += blockDim.x) {
+                for (int c = tid; c < n; c += SL_THREADS) {
                     const unsigned long long k = skey[c];
                     if (k == 0ull || k < blo || k > bhi) continue;
                     const int at = atomicAdd(&sm.nb, 1);
@@ -477,7 +581,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
                 __syncthreads();
                 if (wid == 0) {
                     unsigned long long T, fl;
-                    resolve(sm.bkeys, sm.bsz, min(sm.nb, 32), qc, qsz, qp, use_pages, blo, T, fl);
+                    resolve(sm.bkeys, sm.bsz, min(sm.nb, 32), qc, qsz, qp, use_pages, blo, sm.rscr[0], T, fl);
                     if (lid == 0) {
                         sm.T = T;
                         sm.flags = fl;
@@ -515,42 +619,15 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             const float v = (score_of(k) - smin) * scale;
             return min(SL_NB - 1, max(0, (int)v));
         };
-        for (int b = tid; b < SL_NB; b += blockDim.x) sm.hist[0][b] = sm.hist[1][b] = sm.hist[2][b] = 0;
-        if (tid == 0) {
-            sm.nb = sm.nb2 = 0;
-            sm.first = sm.first2 = SL_NB;
-        }
-        __syncthreads();
-        for (int c = tid; c < n; c += blockDim.x) {
+        clear_hist();
+        for (int c = tid; c < n; c += SL_THREADS) {
             const unsigned long long k = skey[c];
             if (k == 0ull) continue;
-            const int b = bucket_of(k);
-            const int sz = ssz[c];
-            atomicAdd(&sm.hist[0][b], 1);
-            atomicAdd(&sm.hist[1][b], sz);
-            atomicAdd(&sm.hist[2][b], pages_of(sz));
+            add_hist(bucket_of(k), ssz[c]);
         }
         __syncthreads();
         Scan sc;
-        {
-            int c4 = 0, s4 = 0, p4 = 0;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int b = SL_NB - 1 - 4 * tid - q;
-                sc.cv[q] = sm.hist[0][b];
-                sc.sv[q] = sm.hist[1][b];
-                sc.pv[q] = sm.hist[2][b];
-                c4 += sc.cv[q];
-                s4 += sc.sv[q];
-                p4 += sc.pv[q];
-            }
-            const int ic = sl_scan(c4, sm.red, nullptr);
-            const int is = sl_scan(s4, sm.red, nullptr);
-            const int ip = sl_scan(p4, sm.red, nullptr);
-            sc.ec = ic - c4;
-            sc.es = is - s4;
-            sc.ep = ip - p4;
-        }
+        scan_hist(0, 0, 0, sc);
         {
             long long ec = sc.ec, es = sc.es, ep = sc.ep;
             bool doneA = false, doneB = false;
@@ -585,7 +662,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         const int bA = hasA ? sm.bucket : -1, bB = hasB ? sm.bucket2 : -1;
         unsigned long long minA = ~0ull, minB = ~0ull;  // lowest key of each boundary bucket
         if (hasA || hasB) {
-            for (int c = tid; c < n; c += blockDim.x) {
+            for (int c = tid; c < n; c += SL_THREADS) {
                 const unsigned long long k = skey[c];
                 if (k == 0ull) continue;
                 const int b = bucket_of(k);
@@ -612,7 +689,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
                 const int m = min(sm.nb, 32);
                 for (int q = 0; q < m; ++q) minA = min(minA, sm.bkeys[q]);
                 // "whole bucket kept" threshold = just below its lowest key
-                resolve(sm.bkeys, sm.bsz, m, sm.pre[0], sm.pre[1], sm.pre[2], true, minA, T, fl);
+                resolve(sm.bkeys, sm.bsz, m, sm.pre[0], sm.pre[1], sm.pre[2], true, minA, sm.rscr[0], T, fl);
             } else {
                 T = key_lo0 > 0 ? key_lo0 - 1 : 0ull;
             }
@@ -622,7 +699,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             if (hasB) {
                 const int m = min(sm.nb2, 32);
                 for (int q = 0; q < m; ++q) minB = min(minB, sm.bkeys2[q]);
-                resolve(sm.bkeys2, sm.bsz2, m, sm.pre2[0], sm.pre2[1], sm.pre2[2], false, minB, T, fl);
+                resolve(sm.bkeys2, sm.bsz2, m, sm.pre2[0], sm.pre2[1], sm.pre2[2], false, minB, sm.rscr[1], T, fl);
             } else {
                 T = key_lo0 > 0 ? key_lo0 - 1 : 0ull;
             }
@@ -652,82 +729,86 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 
     // ---------------- leader: emission in slot order ----------------
     // warp w owns the contiguous slot range [w*R, (w+1)*R); lanes take
-    // consecutive slots (conflict-free), warp ballots give the in-order ranks
+    // consecutive slots (conflict-free); ballots count and rank
     const int R = ((n + SL_WARPS - 1) / SL_WARPS + 31) & ~31;
     const int w0 = wid * R, w1 = min(n, w0 + R);
-    int wsel = 0, wrows = 0, wkept = 0;
-    for (int base = w0; base < w1; base += 32) {
-        const int c = base + lid;
-        const unsigned long long k = c < w1 ? skey[c] : 0ull;
-        const bool fin = k != 0ull && k > thrA;
-        const bool kept = k != 0ull && k > thrB;
-        wsel += __popc(__ballot_sync(0xffffffffu, fin));
-        wkept += __popc(__ballot_sync(0xffffffffu, kept));
-        wrows += warp_sum_i(fin ? ssz[c] : 0);
-    }
-    if (lid == 0) {
-        sm.wsel[wid] = wsel;
-        sm.wrows[wid] = wrows;
-        sm.wkept[wid] = wkept;
+    {
+        int wsel = 0, wkept = 0;
+#pragma unroll 4
+        for (int base = w0; base < w1; base += 32) {
+            const int c = base + lid;
+            const unsigned long long k = c < w1 ? skey[c] : 0ull;
+            wsel += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrA));
+            wkept += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrB));
+        }
+        if (lid == 0) {
+            sm.wsel[wid] = wsel;
+            sm.wkept[wid] = wkept;
+        }
     }
     __syncthreads();
-    int sel_base = 0, row_base = 0, nsel = 0, sel_rows = 0, nkept = 0;
+    int sel_base = 0, nsel = 0, nkept = 0;
 #pragma unroll
     for (int q = 0; q < SL_WARPS; ++q) {
-        if (q < wid) {
-            sel_base += sm.wsel[q];
-            row_base += sm.wrows[q];
-        }
+        if (q < wid) sel_base += sm.wsel[q];
         nsel += sm.wsel[q];
-        sel_rows += sm.wrows[q];
         nkept += sm.wkept[q];
     }
-    const int static_len = a.static_len;
     {
-        int si = sel_base, ri = static_len + row_base;
+        int si = sel_base;
+        const unsigned lt = (1u << lid) - 1u;
+#pragma unroll 4
         for (int base = w0; base < w1; base += 32) {
             const int c = base + lid;
             const unsigned long long k = c < w1 ? skey[c] : 0ull;
             const bool fin = k != 0ull && k > thrA;
             const unsigned fm = __ballot_sync(0xffffffffu, fin);
-            const int sz = fin ? ssz[c] : 0;
-            const int incl = warp_incl_scan(sz);
             if (fin) {
-                const int my = si + __popc(fm & ((1u << lid) - 1u));
+                const int my = si + __popc(fm & lt);
                 if (my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = c;
-                if (my < 2048) {
-                    sel_slot[my] = c;
-                    sel_start[my] = ri + incl - sz;
-                }
+                if (my < SL_SEL_MAX) sel_slot[my] = c;
             }
             si += __popc(fm);
-            ri += __shfl_sync(0xffffffffu, incl, 31);
         }
     }
     __syncthreads();
     stamp(4);
-    int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
+    // row offsets of the selected cells (slot order) by one block scan;
+    // thread t owns entries 4t .. 4t+3
+    const int ns = min(nsel, SL_SEL_MAX);
     const int32_t* offs = a.cell_offsets + hs * (n + 1);
-    for (int r = tid; r < static_len; r += blockDim.x) rows[r] = (1 << 30) | r;
+    const int static_len = a.static_len;
+    int sel_rows = 0;
     {
-        // warp w takes cells [32w', 32w'+32) for w' = w, w + SL_WARPS, ...; the
-        // lanes first load the 32 cells' list offsets together
-        const int ns = min(nsel, 2048);
-        for (int i0 = wid * 32; i0 < ns; i0 += SL_WARPS * 32) {
-            const int mi = i0 + lid;
-            const int mslot = mi < ns ? sel_slot[mi] : 0;
-            const int moff = mi < ns ? offs[mslot] : 0;
-            const int mst = mi < ns ? sel_start[mi] : 0;
-            const int msz = mi < ns ? ssz[mslot] : 0;
-            const int cnt = min(32, ns - i0);
-            for (int q = 0; q < cnt; ++q) {
-                const int off = __shfl_sync(0xffffffffu, moff, q);
-                const int s0 = __shfl_sync(0xffffffffu, mst, q);
-                const int sz = __shfl_sync(0xffffffffu, msz, q);
-                for (int jj = lid; jj < sz; jj += 32)
-                    if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
-            }
+        int szs[4], ofv[4], loc = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // the offset loads are in flight during the scan
+            const int i = 4 * tid + q;
+            const int slot = i < ns ? sel_slot[i] : 0;
+            szs[q] = i < ns ? ssz[slot] : 0;
+            ofv[q] = i < ns ? offs[slot] : 0;
+            loc += szs[q];
         }
+        int tot;
+        int run = sl_scan(loc, sm.redi, &tot) - loc + static_len;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int i = 4 * tid + q;
+            if (i < ns) {
+                sel_start[i] = run;
+                sel_off[i] = ofv[q];
+            }
+            run += szs[q];
+        }
+        sel_rows = tot;
+    }
+    __syncthreads();
+    int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
+    for (int r = tid; r < static_len; r += SL_THREADS) rows[r] = (1 << 30) | r;
+    for (int i = wid; i < ns; i += SL_WARPS) {
+        const int s0 = sel_start[i], off = sel_off[i], sz = ssz[sel_slot[i]];
+        for (int jj = lid; jj < sz; jj += 32)
+            if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
     }
     int total = min(static_len + sel_rows, a.exec_capacity);
     if (a.delta_count) {
@@ -735,7 +816,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         const bool has_pad = nkept < a.nprobe;
         const int32_t* dids = a.delta_cell_ids + hs * a.delta_capacity;
         int appended = 0;
-        for (int base = 0; base < dcount; base += blockDim.x) {
+        for (int base = 0; base < dcount; base += SL_THREADS) {
             const int pidx = base + tid;
             int f = 0;
             if (pidx < dcount) {
@@ -747,7 +828,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
                 if (cid == a.padding_id && has_pad) f = 1;
             }
             int tot;
-            const int incl = sl_scan(f, sm.red, &tot);
+            const int incl = sl_scan(f, sm.redi, &tot);
             if (f) {
                 const int at = total + appended + incl - 1;
                 if (at < a.exec_capacity) rows[at] = (2 << 30) | pidx;
@@ -767,18 +848,17 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 
 size_t select_smem_bytes(const SelectArgs& a) {
     const int S = a.parts == 0 ? 1 : a.parts;
-    int table = 1, kpre = 1;
-    for (int s = 0; s < S - 1; ++s) {
-        table *= a.ks[s];
-        kpre = a.ks[s] > kpre ? a.ks[s] : kpre;
-    }
+    int table = 1;
+    for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
     const int sub = a.dim / S;
-    const size_t ct = S > 1 ? (size_t)sub * (a.ks[S - 1] + 1) : 0;
-    size_t cp = S > 1 ? (size_t)sub * (kpre + 1) * 4 : 0;
-    if (cp < 2 * 2048 * 4) cp = 2 * 2048 * 4;  // reused for the selected-cell lists
+    size_t tables = 0;
+    if (S > 1)
+        for (int s = 0; s < S; ++s) tables += (size_t)sub * sl_ld(a.ks[s]) * sizeof(float);
+    const size_t lists = 3 * (size_t)SL_SEL_MAX * sizeof(int);  // reused for the selected-cell lists
+    const size_t region = tables > lists ? tables : lists;
     const size_t npad = ((size_t)a.n_slots + 1) & ~size_t(1);
-    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + sizeof(float) * ((size_t)a.dim + table + 4 + ct) +
-           cp + 16;
+    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + sizeof(float) * ((size_t)a.dim + table + 4) + region +
+           16;
 }
 
 int select_max_slots() { return SL_MAX_SLOTS; }

@@ -215,13 +215,18 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
     _lib.check(L.imi_select_cells(ctypes.byref(d), _stream(q.device)), "imi_select_cells")
 
 
-def default_splits(bg: int, rows_per_group: int, sms: int = 148) -> int:
+ATTN_MAX_ROWS_PER_CTA = 5632  # staged row entries per CTA that fit beside the copy ring in shared memory
+
+
+def default_splits(bg: int, rows_per_group: int, sms: int = 148, exec_capacity: Optional[int] = None) -> int:
     """CTAs per KV group for the split-K attention: one wave (one CTA per SM,
     the kernel's shared-memory ring allows one), at least 64 rows per CTA, and
-    at most 16K rows per CTA (the staged row indices)."""
+    few enough rows per CTA that its share of the row list (sized from
+    ``exec_capacity``, the row-list stride) fits in shared memory."""
     want = max(1, sms // bg)
     s = max(1, min(want, (rows_per_group + 63) // 64, 512))
-    return int(max(s, (rows_per_group + 16383) // 16384))
+    cap = max(rows_per_group, exec_capacity or 0)
+    return int(max(s, (cap + ATTN_MAX_ROWS_PER_CTA - 1) // ATTN_MAX_ROWS_PER_CTA))
 
 
 def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: torch.Tensor,
@@ -229,10 +234,12 @@ def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: tor
                      static_values: torch.Tensor, out: torch.Tensor, part_o: torch.Tensor, part_ml: torch.Tensor,
                      splits: int, scale: Optional[float] = None, delta_keys: Optional[torch.Tensor] = None,
                      delta_values: Optional[torch.Tensor] = None,
-                     counters: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     counters: Optional[torch.Tensor] = None,
+                     status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Attention of q [bg, G, 128] over the rows named by row_index.
     counters: int32 [bg] zeroed scratch; when given the split merge happens in
-    the attention kernel itself (its last CTA per group)."""
+    the attention kernel itself (its last CTA per group).
+    status: int32 [1] or None; bit 0 is set if a wait for a row copy gave up."""
     bg, G, D = q.shape
     if D != 128:
         raise ValueError("sparse attention supports head_dim 128")
@@ -248,6 +255,7 @@ def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: tor
             delta_keys.shape[-2]
     d.part_o, d.part_ml, d.out = part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr()
     d.counters = counters.data_ptr() if counters is not None else None
+    d.status = status.data_ptr() if status is not None else None
     L = _lib.load()
     _lib.check(L.imi_sparse_attention(ctypes.byref(d), _stream(q.device)), "imi_sparse_attention")
     return out

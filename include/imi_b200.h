@@ -139,13 +139,15 @@ typedef struct imi_attn_desc {
     const void* delta_keys;                /* [bg, delta_rows, 128] or NULL */
     const void* delta_values;
     int64_t delta_rows;
-    float* part_o;                         /* scratch [bg, splits, G, 128] */
-    float* part_ml;                        /* scratch [bg, splits, G, 2] */
-    void* out;                             /* [bg, G, 128] bf16 out */
+    float* part_o;                         /* scratch [bg, splits, G, 128], 16-byte aligned */
+    float* part_ml;                        /* scratch [bg, splits, G, 2], 8-byte aligned */
+    void* out;                             /* [bg, G, 128] bf16 out, 8-byte aligned */
     int32_t* counters;                     /* scratch [bg], zero before the first call, or NULL:
                                               with it the last CTA of a group merges the
                                               splits (and re-zeroes its counter); without it a
                                               separate merge kernel runs */
+    int32_t* status;                       /* [1] or NULL: bit 0 is set when a wait for a row
+                                              copy gave up (the output is then not valid) */
 } imi_attn_desc;
 
 typedef struct imi_append_desc {

@@ -207,9 +207,11 @@ def test_attention_matches_oracle(splits, fused):
         part_o = torch.empty(heads, splits, G, 128, device="cuda")
         part_ml = torch.empty(heads, splits, G, 2, device="cuda")
         counters = torch.zeros(heads, dtype=torch.int32, device="cuda") if fused else None
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
         ops.sparse_attention(q=qd, row_index=rows, row_count=rc, list_keys=idx.list_keys,
                              list_values=idx.list_values, static_keys=zkd, static_values=zvd, out=out,
-                             part_o=part_o, part_ml=part_ml, splits=splits, counters=counters)
+                             part_o=part_o, part_ml=part_ml, splits=splits, counters=counters, status=status)
+        assert int(status) == 0  # no wait for a row copy gave up
         if fused:
             assert int(counters.abs().sum()) == 0  # the merging CTA re-zeroed the counters
         torch.cuda.synchronize()
