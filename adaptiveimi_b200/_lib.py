@@ -47,6 +47,7 @@ class SelectDesc(ctypes.Structure):
         ("delta_capacity", i32), ("exec_capacity", i32),
         ("sel_cells", P), ("sel_count", P), ("kept_count", P), ("row_index", P), ("row_count", P),
         ("scores_out", P), ("phase_ns", P),
+        ("slot_bound", i32),
     ]
 
 
@@ -95,7 +96,8 @@ class ApplyDesc(ctypes.Structure):
 EXPORTS = (
     "imi_abi_version", "imi_last_error", "imi_build_workspace_size", "imi_build_index",
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
-    "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_sparse_attention_noalloc",
+    "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_decode_layer",
+    "imi_sparse_attention_noalloc",
 )
 
 _lib = None
@@ -131,6 +133,9 @@ def load():
         L.imi_sparse_attention_noalloc.argtypes = [ctypes.POINTER(AttnDesc), P]
         L.imi_decode_attend.argtypes = [ctypes.POINTER(SelectDesc), ctypes.POINTER(AttnDesc),
                                         ctypes.POINTER(ApplyDesc), P]
+        L.imi_decode_layer.argtypes = [ctypes.POINTER(AppendDesc), ctypes.POINTER(AsyncDesc),
+                                       ctypes.POINTER(ApplyDesc), ctypes.POINTER(SelectDesc),
+                                       ctypes.POINTER(AttnDesc), P]
         if L.imi_abi_version() != 1:
             raise ImportError("libimi_b200.so ABI version mismatch")
         _lib = L

@@ -156,6 +156,10 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                                           exec_capacity=self.execution_stride)
         # optional measurement hooks (bench.py): per-call row counts and CUDA
         # events around the attention launch, both on the launching stream
+        self._pending = None  # deferred append: (layer, k, v, head stride, pos, batch slot, async batch)
+        self._fused = False   # set by prepare_cache: appends ride on the layer's attention call
+        self._dev_index = [torch.device(self.layer_mapping[str(i)]).index or 0 for i in range(layer_num)]
+        self._rc: List[Optional[torch.Tensor]] = [None] * layer_num
         self.row_count_log: Optional[torch.Tensor] = None
         self.attn_event_log: Optional[list] = None
         self._log_pos = 0
@@ -202,6 +206,8 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         return key_states[:, valid_start:, :, :], value_states[:, valid_start:, :, :]
 
     def sync(self, layer_idx, start_bdx):
+        if self._pending is not None:
+            self._flush_pending()
         return None
 
     def capture_cuda_graph(self):
@@ -245,7 +251,9 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             if self.async_update_enabled:
                 self._init_async(ldx)
         self._descs = [self._make_descs(ldx) for ldx in range(self.layer_num)]
+        self._rc = [self._dec[self.layer_mapping[str(ldx)]]["row_count"] for ldx in range(self.layer_num)]
         self.attn_func = self.sparse_attention
+        self._fused = True
         self.cache_prepared = True
 
     def _make_descs(self, ldx: int):
@@ -273,6 +281,9 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         sel.sel_cells, sel.sel_count, sel.kept_count = buf["sel"].data_ptr(), buf["sel_count"].data_ptr(), \
             buf["kept"].data_ptr()
         sel.row_index = buf["rows"].data_ptr()
+        # every slot at or above the largest n_active is padding: one host read
+        # per layer, here at preparation, lets the selection skip them
+        sel.slot_bound = int(idx.n_active.max().item())
         att = _lib.AttnDesc()
         att.bg, att.G, att.splits, att.exec_capacity = bg, G, self.splits, self.execution_stride
         att.scale = 1.0 / math.sqrt(D)
@@ -301,7 +312,24 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         if st is not None:
             ap.batch_keys, ap.batch_values = st["batch_keys"].data_ptr(), st["batch_values"].data_ptr()
             ap.batch_cap = self.async_update_batch
-        return dict(sel=sel, att=att, app=app, append=ap)
+        asd = None
+        if st is not None:
+            asd = _lib.AsyncDesc()
+            asd.bg, asd.dim, asd.n_slots, asd.parts, asd.kmax = bg, D, idx.n_slots, idx.parts, idx.kmax
+            asd.batch, asd.batch_cap = self.async_update_batch, self.async_update_batch
+            asd.threshold, asd.ring_cap = self.async_update_threshold, self.async_update_delta_tokens
+            asd.ks = ops._ks4(idx.ks)
+            asd.batch_keys, asd.batch_values = st["batch_keys"].data_ptr(), st["batch_values"].data_ptr()
+            asd.sub_centroids, asd.cell_code = idx.sub_centroids.data_ptr(), idx.cell_code.data_ptr()
+            asd.shadow, asd.shadow_dirty, asd.pending = st["shadow"].data_ptr(), st["shadow_dirty"].data_ptr(), \
+                st["pending"].data_ptr()
+            asd.counts, asd.delta_counts = st["counts"].data_ptr(), st["delta_counts"].data_ptr()
+            asd.delta_sums = st["delta_sums"].data_ptr()
+            asd.ring_keys, asd.ring_values = st["ring_keys"].data_ptr(), st["ring_values"].data_ptr()
+            asd.ring_cell_ids, asd.ring_write_pos = st["ring_ids"].data_ptr(), st["ring_pos"].data_ptr()
+            asd.ring_count = st["ring_count"].data_ptr()
+            asd.part_best, asd.part_chunks = st["part_best"].data_ptr(), ops.async_chunks(idx.n_slots)
+        return dict(sel=sel, att=att, app=app, append=ap, **{"async": asd})
 
     def _init_async(self, ldx: int) -> None:
         idx = self.index[ldx]
@@ -333,45 +361,78 @@ class adpimi_cache:  # noqa: N801  (reference class name)
     # decode (runtime.py:378-392, async_update.py:77-162)
     # ------------------------------------------------------------------------
     def decode_update_kv_cache(self, key_states, value_states, layer_idx):
-        """key_states/value_states: [B, 1, kv_heads, D]."""
+        """key_states/value_states: [B, 1, kv_heads, D].
+
+        Once the cache is prepared the append is deferred: ``attn_func`` issues
+        it together with the layer's selection and attention in one
+        ``imi_decode_layer`` call (same stream order as two calls).  Any other
+        entry point issues a deferred append first."""
+        if self._pending is not None:
+            self._flush_pending()
         st = self._async[layer_idx] if self.async_update_enabled else None
-        nk = key_states[:, 0].reshape(self.batch_groups, self.head_dim)
-        nv = value_states[:, 0].reshape(self.batch_groups, self.head_dim)
-        if nk.stride(-1) != 1 or nv.stride(-1) != 1 or nk.stride(0) != nv.stride(0):
-            nk, nv = nk.contiguous(), nv.contiguous()
-        dev = nk.device
-        L = _lib.load()
-        if self.cache_prepared:
-            ap = self._descs[layer_idx]["append"]
+        nk, nv, stride = self._kv_rows(key_states, value_states)
+        pos = self.static_pattern_total
+        slot = st["count"] if st is not None else 0
+        batch = 0
+        if st is not None:
+            st["count"] += 1
+            if st["count"] >= self.async_update_batch:
+                batch = st["count"]
+                st["count"] = 0
+                st["pending_flag"] = "scheduled"
+        rec = (layer_idx, nk, nv, stride, pos, slot, batch)
+        if self._fused:
+            self._pending = rec
         else:
+            self._issue_append(rec)
+        if layer_idx == self.layer_num - 1:
+            self.context += 1
+            self.static_pattern_total += 1
+        return None, None
+
+    def _kv_rows(self, key_states, value_states):
+        """Base tensors and head stride (elements) of the new token's K/V rows;
+        a layout the kernels cannot read in place is copied first."""
+        if key_states.shape[0] != 1:
+            raise ValueError("decode_update_kv_cache: batch_size 1 only")
+        ks, vs = key_states, value_states
+        if ks.stride(-1) != 1 or vs.stride(-1) != 1 or ks.stride(2) != vs.stride(2):
+            ks, vs = ks.contiguous(), vs.contiguous()
+        return ks, vs, ks.stride(2)
+
+    def _fill_append(self, rec):
+        layer_idx, nk, nv, stride, pos, slot, batch = rec
+        ap = self._descs[layer_idx]["append"] if self.cache_prepared else None
+        if ap is None:
             ap = _lib.AppendDesc()
             ap.bg, ap.dim = self.batch_groups, self.head_dim
             ap.zone_keys = self.steady_zone_keys[layer_idx].data_ptr()
             ap.zone_values = self.steady_zone_values[layer_idx].data_ptr()
             ap.zone_rows = self.static_capacity
-        ap.new_keys, ap.new_values, ap.src_head_stride = nk.data_ptr(), nv.data_ptr(), nk.stride(0)
-        ap.pos = self.static_pattern_total
-        if st is not None:
-            ap.batch_slot = st["count"]
-        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        ap.new_keys, ap.new_values, ap.src_head_stride = nk.data_ptr(), nv.data_ptr(), stride
+        ap.pos = pos
+        ap.batch_slot = slot
+        return ap
+
+    def _issue_append(self, rec) -> None:
+        """Append (and the batched cell assignment when one is due) as their own calls."""
+        layer_idx, batch = rec[0], rec[6]
+        ap = self._fill_append(rec)
+        stream = ctypes.c_void_p(self._stream(layer_idx))
+        L = _lib.load()
         _lib.check(L.imi_decode_append(ctypes.byref(ap), stream), "imi_decode_append")
-        if st is not None:
-            st["count"] += 1
-            if st["count"] >= self.async_update_batch:
-                ops.async_assign(index=self.index[layer_idx], batch=st["count"], batch_keys=st["batch_keys"],
-                                 batch_values=st["batch_values"], shadow=st["shadow"],
-                                 shadow_dirty=st["shadow_dirty"], pending=st["pending"], counts=st["counts"],
-                                 delta_counts=st["delta_counts"], delta_sums=st["delta_sums"],
-                                 ring_keys=st["ring_keys"], ring_values=st["ring_values"],
-                                 ring_cell_ids=st["ring_ids"], ring_write_pos=st["ring_pos"],
-                                 ring_count=st["ring_count"], threshold=self.async_update_threshold,
-                                 part_best=st["part_best"])
-                st["count"] = 0
-                st["pending_flag"] = "scheduled"
-        if layer_idx == self.layer_num - 1:
-            self.context += 1
-            self.static_pattern_total += 1
-        return None, None
+        if batch:
+            asd = self._descs[layer_idx]["async"]
+            asd.batch = batch
+            _lib.check(L.imi_async_assign(ctypes.byref(asd), stream), "imi_async_assign")
+
+    def _flush_pending(self) -> None:
+        rec, self._pending = self._pending, None
+        if rec is not None:
+            self._issue_append(rec)
+
+    def _stream(self, layer_idx: int) -> int:
+        return torch._C._cuda_getCurrentRawStream(self._dev_index[layer_idx])
 
     def _apply_async_centroid_updates(self, layer_idx: int) -> None:
         """Publish the shadow centroids updated by an earlier decode step
@@ -388,25 +449,36 @@ class adpimi_cache:  # noqa: N801  (reference class name)
     def sparse_attention(self, queries, layer_idx, static_len):
         """retrieval.py:320-602: cell scores, selection under the token budget and
         page truncation, and attention over [steady zone | selected rows | delta
-        rows], as one C-ABI call (imi_decode_attend)."""
+        rows], issued with the layer's deferred append (and, when due, the
+        batched cell assignment and centroid publish) as one C-ABI call
+        (imi_decode_layer)."""
         if not self.layer_ready[layer_idx]:
             self.ensure_layer_ready(layer_idx)
-        dev = self.layer_mapping[str(layer_idx)]
-        q = queries.reshape(self.batch_groups, self.group_size, self.head_dim)
-        if not q.is_contiguous():
-            q = q.contiguous()
+        q = queries if queries.is_contiguous() else queries.contiguous()
         d = self._descs[layer_idx]
         sel, att = d["sel"], d["att"]
+        app_ref = as_ref = None
+        rec = self._pending
+        if rec is not None:
+            if rec[0] == layer_idx:
+                self._pending = None
+                app_ref = ctypes.byref(self._fill_append(rec))
+                if rec[6]:
+                    asd = d["async"]
+                    asd.batch = rec[6]
+                    as_ref = ctypes.byref(asd)
+            else:
+                self._flush_pending()
         st = self._async[layer_idx] if self.async_update_enabled else None
         apply = None
         if st is not None and st["pending_flag"] == "ready":
             apply = ctypes.byref(d["app"])
             st["pending_flag"] = False
-        rc = self._dec[dev]["row_count"]
+        rc = self._rc[layer_idx]
         if self.row_count_log is not None and self._log_pos < self.row_count_log.shape[0]:
             rc = self.row_count_log[self._log_pos]
             self._log_pos += 1
-        out = torch.empty((self.batch_groups, self.group_size, self.head_dim), dtype=self.dtype, device=q.device)
+        out = torch.empty((self.batch_size, 1, self.num_heads, self.head_dim), dtype=self.dtype, device=q.device)
         qp, rcp = q.data_ptr(), rc.data_ptr()
         sel.q = att.q = qp
         sel.row_count = att.row_count = rcp
@@ -416,18 +488,20 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         if self.attn_event_log is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        stream = ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)
-        _lib.check(_lib.load().imi_decode_attend(ctypes.byref(sel), ctypes.byref(att), apply, stream),
-                   "imi_decode_attend")
+        stream = ctypes.c_void_p(self._stream(layer_idx))
+        _lib.check(_lib.load().imi_decode_layer(app_ref, as_ref, apply, ctypes.byref(sel), ctypes.byref(att), stream),
+                   "imi_decode_layer")
         if ev is not None:
             ev[1].record()
             self.attn_event_log.append(ev)
         if st is not None and st["pending_flag"] == "scheduled":
             st["pending_flag"] = "ready"
-        return out.view(self.batch_size, 1, self.num_heads, self.head_dim)
+        return out
 
     def dense_attention(self, queries, layer_idx, static_len):
         """Attention over the first ``static_len`` steady-zone rows (runtime.py:393-403)."""
+        if self._pending is not None:
+            self._flush_pending()
         dev = queries.device
         bg, G, D = self.batch_groups, self.group_size, self.head_dim
         n = int(static_len) if not torch.is_tensor(static_len) else int(static_len.max())
@@ -459,6 +533,9 @@ class adpimi_cache:  # noqa: N801  (reference class name)
     def reset_for_next_sequence(self, valid_start, max_new_length: int, input_length: int) -> None:
         if not self.can_reuse_for_next_sequence(valid_start, max_new_length, input_length):
             raise ValueError("AdaptiveIMI cache shape mismatch; cannot reuse across samples")
+        if self._pending is not None:
+            self._flush_pending()
+        self._fused = False
         self.valid_start_list = valid_start
         self.input_length = int(input_length)
         self.actual_gen_len = int(max_new_length) - 1
@@ -472,6 +549,8 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self._async = [None] * self.layer_num
 
     def cleanup(self) -> None:
+        self._pending = None
+        self._fused = False
         for p in self.imi_pipelines:
             if p is not None:
                 p.close()

@@ -414,7 +414,8 @@ size_t attn_smem_bytes(const AttnArgs& a) {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     const size_t sm = attn_smem_bytes(a);
-    cudaError_t e = cudaFuncSetAttribute(imi_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    static int smem_set[64] = {};
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_attn_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
     // programmatic dependent launch: the CTAs may start (barrier set-up) while
     // the kernel before them in the stream finishes; they wait for it with

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "imi_internal.h"
@@ -30,6 +31,20 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 namespace imi {
 void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per device and size:
+// `cache` holds the largest size already set on each device.
+cudaError_t ensure_smem(const void* func, size_t bytes, int* cache, int cache_len) {
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < cache_len && (int)bytes <= cache[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess && dev >= 0 && dev < cache_len) cache[dev] = (int)bytes;
+    return e;
+}
 }  // namespace imi
 
 extern "C" {
@@ -119,39 +134,7 @@ static int check_attention(const imi_attn_desc* d) {
     return IMI_OK;
 }
 
-int imi_select_cells(const imi_select_desc* d, void* stream) {
-    const int st = check_select(d);
-    if (st != IMI_OK) return st;
-    return cuda_status(imi::launch_select(*d, S(stream)), "imi_select_cells");
-}
-
-int imi_sparse_attention(const imi_attn_desc* d, void* stream) {
-    const int st = check_attention(d);
-    if (st != IMI_OK) return st;
-    return cuda_status(imi::launch_attention(*d, S(stream)), "imi_sparse_attention");
-}
-
-int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
-                      void* stream) {
-    int st = check_select(sel);
-    if (st != IMI_OK) return st;
-    st = check_attention(attn);
-    if (st != IMI_OK) return st;
-    if (sel->bg != attn->bg || sel->G != attn->G || sel->row_index != attn->row_index ||
-        sel->row_count != attn->row_count || sel->q != attn->q || sel->exec_capacity != attn->exec_capacity)
-        return fail(IMI_ERR_INVALID, "imi_decode_attend: select and attention descriptors disagree");
-    if (apply) {
-        if (!apply->shadow || !apply->live || !apply->pending || !apply->live_dirty)
-            return fail(IMI_ERR_INVALID, "imi_decode_attend: null pointer in apply descriptor");
-        cudaError_t e = imi::launch_apply(*apply, S(stream));
-        if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
-    }
-    cudaError_t e = imi::launch_select(*sel, S(stream));
-    if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
-    return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");
-}
-
-int imi_decode_append(const imi_append_desc* d, void* stream) {
+static int check_append(const imi_append_desc* d) {
     if (!d || !d->new_keys || !d->new_values || !d->zone_keys || !d->zone_values)
         return fail(IMI_ERR_INVALID, "imi_decode_append: null pointer");
     if (d->bg <= 0 || d->dim <= 0 || (d->dim * 2) % 16 != 0 || d->pos < 0 || d->pos >= d->zone_rows)
@@ -160,10 +143,10 @@ int imi_decode_append(const imi_append_desc* d, void* stream) {
         return fail(IMI_ERR_INVALID, "imi_decode_append: batch slot out of range");
     if (!aligned16(d->new_keys) || !aligned16(d->new_values) || (d->src_head_stride * 2) % 16 != 0)
         return fail(IMI_ERR_INVALID, "imi_decode_append: new k/v must be 16-byte aligned");
-    return cuda_status(imi::launch_append(*d, S(stream)), "imi_decode_append");
+        return IMI_OK;
 }
 
-int imi_async_assign(const imi_async_desc* d, void* stream) {
+static int check_async(const imi_async_desc* d) {
     if (!d || !d->batch_keys || !d->batch_values || !d->sub_centroids || !d->cell_code || !d->shadow ||
         !d->counts || !d->delta_counts || !d->delta_sums || !d->ring_keys || !d->ring_values || !d->ring_cell_ids ||
         !d->ring_write_pos || !d->ring_count)
@@ -180,6 +163,86 @@ int imi_async_assign(const imi_async_desc* d, void* stream) {
         if (table * d->batch > 16384 || table * d->batch > 32 * 512)
             return fail(IMI_ERR_INVALID, "imi_async_assign: batch * prefix table > 16384");
     }
+        return IMI_OK;
+}
+
+int imi_select_cells(const imi_select_desc* d, void* stream) {
+    const int st = check_select(d);
+    if (st != IMI_OK) return st;
+    return cuda_status(imi::launch_select(*d, S(stream)), "imi_select_cells");
+}
+
+int imi_sparse_attention(const imi_attn_desc* d, void* stream) {
+    const int st = check_attention(d);
+    if (st != IMI_OK) return st;
+    return cuda_status(imi::launch_attention(*d, S(stream)), "imi_sparse_attention");
+}
+
+static int check_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply) {
+    int st = check_select(sel);
+    if (st != IMI_OK) return st;
+    st = check_attention(attn);
+    if (st != IMI_OK) return st;
+    if (sel->bg != attn->bg || sel->G != attn->G || sel->row_index != attn->row_index ||
+        sel->row_count != attn->row_count || sel->q != attn->q || sel->exec_capacity != attn->exec_capacity)
+        return fail(IMI_ERR_INVALID, "imi_decode_attend: select and attention descriptors disagree");
+    if (apply && (!apply->shadow || !apply->live || !apply->pending || !apply->live_dirty))
+        return fail(IMI_ERR_INVALID, "imi_decode_attend: null pointer in apply descriptor");
+    return IMI_OK;
+}
+
+static int launch_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
+                                void* stream) {
+    if (apply) {
+        cudaError_t e = imi::launch_apply(*apply, S(stream));
+        if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
+    }
+    cudaError_t e = imi::launch_select(*sel, S(stream));
+    if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
+    return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");
+}
+
+int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
+                      void* stream) {
+    const int st = check_decode_attend(sel, attn, apply);
+    if (st != IMI_OK) return st;
+    return launch_decode_attend(sel, attn, apply, stream);
+}
+
+int imi_decode_layer(const imi_append_desc* app, const imi_async_desc* as, const imi_apply_desc* apply,
+                     const imi_select_desc* sel, const imi_attn_desc* attn, void* stream) {
+    if (app) {
+        const int st = check_append(app);
+        if (st != IMI_OK) return st;
+    }
+    if (as) {
+        const int st = check_async(as);
+        if (st != IMI_OK) return st;
+    }
+    {
+        const int st = check_decode_attend(sel, attn, apply);
+        if (st != IMI_OK) return st;
+    }
+    if (app) {
+        cudaError_t e = imi::launch_append(*app, S(stream));
+        if (e != cudaSuccess) return cuda_status(e, "imi_decode_layer(append)");
+    }
+    if (as) {
+        cudaError_t e = imi::launch_async_assign(*as, S(stream));
+        if (e != cudaSuccess) return cuda_status(e, "imi_decode_layer(async assignment)");
+    }
+    return launch_decode_attend(sel, attn, apply, stream);
+}
+
+int imi_decode_append(const imi_append_desc* d, void* stream) {
+    const int st = check_append(d);
+    if (st != IMI_OK) return st;
+    return cuda_status(imi::launch_append(*d, S(stream)), "imi_decode_append");
+}
+
+int imi_async_assign(const imi_async_desc* d, void* stream) {
+    const int st = check_async(d);
+    if (st != IMI_OK) return st;
     return cuda_status(imi::launch_async_assign(*d, S(stream)), "imi_async_assign");
 }
 

@@ -113,7 +113,7 @@ IMI_DEV void as_cp_async4(void* dst, const void* src) {
                  : "memory");
 }
 
-__global__ void __launch_bounds__(ASYNC_CHUNK) imi_async_score_kernel(AsyncArgs a) {
+__global__ void __launch_bounds__(ASYNC_CHUNK) imi_async_score_kernel(const __grid_constant__ AsyncArgs a) {
     extern __shared__ __align__(16) unsigned char as_smem[];
     const int h = blockIdx.y;
     const int tid = threadIdx.x;
@@ -399,7 +399,8 @@ int async_chunks(int n_slots) { return (n_slots + ASYNC_CHUNK - 1) / ASYNC_CHUNK
 
 cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st) {
     const size_t sm = async_smem_bytes(a);
-    cudaError_t e = cudaFuncSetAttribute(imi_async_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    static int smem_set[64] = {};
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_async_score_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
     imi_async_score_kernel<<<dim3(a.part_chunks, a.bg), ASYNC_CHUNK, sm, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

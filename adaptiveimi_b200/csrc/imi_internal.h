@@ -33,6 +33,7 @@ cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st);
 
 size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks);
 void set_last_error(const std::string& msg);
+cudaError_t ensure_smem(const void* func, size_t bytes, int* cache, int cache_len);
 cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why);
 
 }  // namespace imi

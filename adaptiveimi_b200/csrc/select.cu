@@ -37,14 +37,19 @@
 // slice of the cell codes, masks and sizes, and the query -- and waits once.
 // It then scores its slice (two to four interleaved fma chains per thread)
 // and stores every key and size straight into the leader CTA's shared memory
-// through DSMEM.  The first cluster barrier is split (arrive at entry, wait
-// just before the first DSMEM store) so it costs nothing.  The leader alone
+// through DSMEM, with its slice's key range in a per-rank slot (plain stores:
+// no shared initial value that remote updates could race with).  The first
+// cluster barrier is split (arrive at entry, wait just before the first DSMEM
+// store) so it costs nothing.  The leader alone
 // runs the boundary search, ranks the selected cells by warp ballots in slot
 // order, computes their row offsets with one block scan and writes the rows
-// with every warp.
+// with every warp.  Only slots below `slot_bound` (the occupied compact ids)
+// are scored and scanned.
+//
+// Code shape matters here: the leader's code runs once per launch, so it is
+// kept compact -- plain functions with explicit arguments, one shared copy of
+// the boundary resolve, the rare fallback out of line, no local arrays.
 #include <cooperative_groups.h>
-
-#include <type_traits>
 
 #include "common.cuh"
 #include "imi_internal.h"
@@ -63,7 +68,7 @@ constexpr int SL_CPT = SL_MAX_SLOTS / SL_CL / SL_THREADS;  // cells per thread w
 constexpr int SL_SEL_MAX = 2048;        // selected cells at most (nprobe <= 2048)
 
 struct SelHdr {
-    unsigned long long kmin, kmax;
+    unsigned long long rmin[SL_CL], rmax[SL_CL];  // per-rank candidate key range (DSMEM stores)
     unsigned long long hcp[SL_NB];  // per bucket: (count << 32) | pages
     unsigned int hsz[SL_NB];        // per bucket: tokens
     unsigned long long red64[SL_WARPS];
@@ -80,7 +85,7 @@ struct SelHdr {
     int bsz2[32];
     int nb2, first2, bucket2, bcnt2;
     long long pre2[3];
-    unsigned long long T2;
+    unsigned long long T2, flags2;
     int wsel[SL_WARPS], wkept[SL_WARPS];
     unsigned long long rscr[2][48];  // resolve scratch per warp: 32 keys, then 32 sizes
 };
@@ -89,6 +94,20 @@ struct SelHdr {
 // warp reading one row at scattered columns spreads over the banks.
 __host__ __device__ inline int sl_ld(int k) { return (k & 1) ? k + 2 : k + 1; }
 
+struct SelRules {
+    int nprobe, max_tokens, buffer_pages, page_size, pg_shift, pg_pow2;
+};
+
+IMI_DEV int sl_pages(int sz, const SelRules& r) {
+    if (sz <= 0) return 0;
+    return r.pg_pow2 ? (sz + r.page_size - 1) >> r.pg_shift : (sz + r.page_size - 1) / r.page_size;
+}
+
+IMI_DEV float sl_key_score(unsigned long long k) {
+    const uint32_t o = (uint32_t)(k >> 32);
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
 IMI_DEV void cp_async4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
                  "l"(src)
@@ -96,7 +115,7 @@ IMI_DEV void cp_async4(void* dst, const void* src) {
 }
 
 // Block-wide inclusive scan of one int (all SL_THREADS threads call it).
-__device__ __forceinline__ int sl_scan(int v, int* red, int* total) {
+IMI_DEV int sl_scan(int v, int* red, int* total) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     int x = v;
 #pragma unroll
@@ -123,7 +142,7 @@ __device__ __forceinline__ int sl_scan(int v, int* red, int* total) {
 }
 
 // Block-wide inclusive scan of a (64-bit, 32-bit) pair under one set of barriers.
-__device__ __forceinline__ void sl_scan_pair(unsigned long long& x, unsigned int& y, SelHdr& sm) {
+IMI_DEV void sl_scan_pair(unsigned long long& x, unsigned int& y, SelHdr& sm) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -164,8 +183,343 @@ __device__ __forceinline__ void sl_scan_pair(unsigned long long& x, unsigned int
     __syncthreads();
 }
 
+// ---------------------------------------------------------------------------
+// histogram rounds (leader, all threads)
+// ---------------------------------------------------------------------------
+IMI_DEV void hist_clear(SelHdr& sm) {
+    for (int b = threadIdx.x; b < SL_NB; b += SL_THREADS) {
+        sm.hcp[b] = 0ull;
+        sm.hsz[b] = 0u;
+    }
+    if (threadIdx.x == 0) {
+        sm.nb = sm.nb2 = 0;
+        sm.first = sm.first2 = SL_NB;
+    }
+    __syncthreads();
+}
+
+IMI_DEV void hist_add(SelHdr& sm, int b, int sz, const SelRules& r) {
+    atomicAdd(&sm.hcp[b], (1ull << 32) | (unsigned long long)(unsigned)sl_pages(sz, r));
+    atomicAdd(&sm.hsz[b], (unsigned)sz);
+}
+
+// Thread t's view of buckets SL_NB-1-4t .. SL_NB-4-4t (descending) with the
+// exclusive (count, tokens, pages) prefixes of the candidates above them.
+struct BucketView {
+    int cv[4], sv[4], pv[4];
+    long long ec, es, ep;
+};
+
+IMI_DEV void hist_view(SelHdr& sm, long long C, long long Sz, long long Pg, BucketView& v) {
+    unsigned long long cp4 = 0ull;
+    unsigned int s4 = 0u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int b = SL_NB - 1 - 4 * (int)threadIdx.x - q;
+        const unsigned long long x = sm.hcp[b];
+        const unsigned int w = sm.hsz[b];
+        v.cv[q] = (int)(x >> 32);
+        v.pv[q] = (int)(x & 0xffffffffull);
+        v.sv[q] = (int)w;
+        cp4 += x;
+        s4 += w;
+    }
+    unsigned long long icp = cp4;
+    unsigned int is = s4;
+    sl_scan_pair(icp, is, sm);
+    const unsigned long long ecp = icp - cp4;
+    v.ec = C + (long long)(ecp >> 32);
+    v.ep = Pg + (long long)(ecp & 0xffffffffull);
+    v.es = Sz + (long long)(is - s4);
+}
+
+// The owner of bucket index fr (descending order) records the bucket, its
+// count and the exclusive prefixes at its start.
+IMI_DEV void view_publish(const BucketView& v, int fr, int* bucket, int* bcnt, long long* pre) {
+    const int q0 = fr & 3;
+    long long xc = v.ec, xs = v.es, xp = v.ep;
+    int cnt = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (q < q0) {
+            xc += v.cv[q];
+            xs += v.sv[q];
+            xp += v.pv[q];
+        }
+        if (q == q0) cnt = v.cv[q];
+    }
+    *bucket = SL_NB - 1 - fr;
+    *bcnt = cnt;
+    pre[0] = xc;
+    pre[1] = xs;
+    pre[2] = xp;
+}
+
+// One warp resolves a boundary bucket exactly: rank its (<= 32) elements,
+// place them in rank order (lane r holds the element of rank r), scan their
+// tokens and pages, and let the first lane whose rule fires name the
+// boundary.  T: selected = key > T; fl = 1 when the rank or token rule (not
+// only the page rule) fires.  Lane 0 writes *T_out / *fl_out.
+__device__ __noinline__ void resolve_boundary(const unsigned long long* bk, const int* bs, int m, long long xc,
+                                              long long xs, long long xp, int use_pages, unsigned long long blo,
+                                              unsigned long long* scratch, SelRules r, unsigned long long* T_out,
+                                              unsigned long long* fl_out) {
+    const int lid = threadIdx.x & 31;
+    const unsigned long long mk = lid < m ? bk[lid] : 0ull;
+    const int msz = lid < m ? bs[lid] : 0;
+    int rk = 0;
+    for (int q = 0; q < m; ++q) rk += (__shfl_sync(0xffffffffu, mk, q) > mk) ? 1 : 0;
+    int* ssz2 = reinterpret_cast<int*>(scratch + 32);
+    if (lid < m) {
+        scratch[rk] = mk;
+        ssz2[rk] = msz;
+    }
+    __syncwarp();
+    const unsigned long long k = lid < m ? scratch[lid] : 0ull;
+    const int sz = lid < m ? ssz2[lid] : 0;
+    const int pg = sl_pages(sz, r);
+    int isz = sz, ipg = pg;  // inclusive scans over the ranked elements
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ts = __shfl_up_sync(0xffffffffu, isz, o);
+        const int tp = __shfl_up_sync(0xffffffffu, ipg, o);
+        if (lid >= o) {
+            isz += ts;
+            ipg += tp;
+        }
+    }
+    const long long bc = xc + lid, bsum = xs + (isz - sz), bpg = xp + (ipg - pg);
+    const bool rc = (bc >= r.nprobe) || (bsum >= r.max_tokens);
+    const bool rp = use_pages && (bpg + pg > r.buffer_pages);
+    const unsigned fire = __ballot_sync(0xffffffffu, lid < m && (rc || rp));
+    unsigned long long T, fl;
+    if (fire) {
+        const int f = __ffs(fire) - 1;
+        T = __shfl_sync(0xffffffffu, k, f);
+        fl = __shfl_sync(0xffffffffu, rc ? 1u : 0u, f) ? 1ull : 0ull;
+    } else {
+        T = blo > 0 ? blo - 1 : 0ull;
+        fl = 1ull;  // nothing fires here: the token rule fires just below this bucket
+    }
+    if (lid == 0) {
+        *T_out = T;
+        *fl_out = fl;
+    }
+    __syncwarp();
+}
+
+// Refinement search for one boundary over power-of-two key ranges (the rare
+// path: a first-round boundary bucket with more than 32 elements).  All
+// threads call it; the result is left in sm.T / sm.flags.
+__device__ __noinline__ void search_one(SelHdr& sm, const unsigned long long* skey, const int* ssz, int ne,
+                                        unsigned long long lo, unsigned long long hi, int use_pages, SelRules r) {
+    const int tid = threadIdx.x;
+    long long C = 0, Sz = 0, Pg = 0;  // totals of candidates with key > hi
+    while (true) {
+        const unsigned long long span = hi - lo;
+        const int bits = span ? 64 - __clzll(span) : 0;
+        const int shift = bits > SL_NB_BITS ? bits - SL_NB_BITS : 0;
+        hist_clear(sm);
+        for (int c = tid; c < ne; c += SL_THREADS) {
+            const unsigned long long k = skey[c];
+            if (k == 0ull || k < lo || k > hi) continue;
+            hist_add(sm, (int)((k - lo) >> shift), ssz[c], r);
+        }
+        __syncthreads();
+        BucketView v;
+        hist_view(sm, C, Sz, Pg, v);
+        {
+            long long ec = v.ec, es = v.es, ep = v.ep;
+            bool done = false;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (!done && v.cv[q] > 0 &&
+                    ((ec + v.cv[q] > r.nprobe) || (es + v.sv[q] >= r.max_tokens) ||
+                     (use_pages && ep + v.pv[q] > r.buffer_pages))) {
+                    atomicMin(&sm.first, 4 * tid + q);
+                    done = true;
+                }
+                ec += v.cv[q];
+                es += v.sv[q];
+                ep += v.pv[q];
+            }
+        }
+        __syncthreads();
+        const int fr = sm.first;
+        if (fr == SL_NB) {
+            if (tid == 0) {
+                sm.T = lo > 0 ? lo - 1 : 0ull;  // no rule fires in [lo, hi]: all of it is selected
+                sm.flags = 0ull;
+            }
+            __syncthreads();
+            return;
+        }
+        if ((fr >> 2) == tid) view_publish(v, fr, &sm.bucket, &sm.bcnt, sm.pre);
+        __syncthreads();
+        const int cnt = sm.bcnt;
+        const long long qc = sm.pre[0], qsz = sm.pre[1], qp = sm.pre[2];
+        const unsigned long long blo = lo + ((unsigned long long)sm.bucket << shift);
+        const unsigned long long bend = blo + ((1ull << shift) - 1ull);
+        const unsigned long long bhi = (bend < blo || bend > hi) ? hi : bend;
+        if (cnt <= 32) {
+            for (int c = tid; c < ne; c += SL_THREADS) {
+                const unsigned long long k = skey[c];
+                if (k == 0ull || k < blo || k > bhi) continue;
+                const int at = atomicAdd(&sm.nb, 1);
+                if (at < 32) {
+                    sm.bkeys[at] = k;
+                    sm.bsz[at] = ssz[c];
+                }
+            }
+            __syncthreads();
+            if ((tid >> 5) == 0)
+                resolve_boundary(sm.bkeys, sm.bsz, min(sm.nb, 32), qc, qsz, qp, use_pages, blo, sm.rscr[0], r,
+                                 &sm.T, &sm.flags);
+            __syncthreads();
+            return;
+        }
+        lo = blo;
+        hi = bhi;
+        C = qc;
+        Sz = qsz;
+        Pg = qp;
+        __syncthreads();
+    }
+}
+
+// First round for both boundaries at once (the common case resolves here):
+// A = all three rules, B = rank and token rules only (the kept list before page
+// truncation), over buckets linear in the score (equal scores share a bucket
+// and are ordered by the warp rank).  Returns false when a boundary bucket
+// holds more than 32 elements.  Results in sm.T / sm.T2.
+IMI_DEV bool search_both(SelHdr& sm, const unsigned long long* skey, const int* ssz, int ne,
+                         unsigned long long key_lo0, unsigned long long key_hi0, const SelRules& r) {
+    const int tid = threadIdx.x, wid = tid >> 5;
+    const float smin = sl_key_score(key_lo0), smax = sl_key_score(key_hi0);
+    const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
+    hist_clear(sm);
+    for (int c = tid; c < ne; c += SL_THREADS) {
+        const unsigned long long k = skey[c];
+        if (k == 0ull) continue;
+        const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
+        hist_add(sm, b, ssz[c], r);
+    }
+    __syncthreads();
+    BucketView v;
+    hist_view(sm, 0, 0, 0, v);
+    {
+        long long ec = v.ec, es = v.es, ep = v.ep;
+        bool doneA = false, doneB = false;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (v.cv[q] > 0) {
+                const bool rule = (ec + v.cv[q] > r.nprobe) || (es + v.sv[q] >= r.max_tokens);
+                if (!doneA && (rule || ep + v.pv[q] > r.buffer_pages)) {
+                    atomicMin(&sm.first, 4 * tid + q);
+                    doneA = true;
+                }
+                if (!doneB && rule) {
+                    atomicMin(&sm.first2, 4 * tid + q);
+                    doneB = true;
+                }
+            }
+            ec += v.cv[q];
+            es += v.sv[q];
+            ep += v.pv[q];
+        }
+    }
+    __syncthreads();
+    const int frA = sm.first, frB = sm.first2;
+    if (frA < SL_NB && (frA >> 2) == tid) view_publish(v, frA, &sm.bucket, &sm.bcnt, sm.pre);
+    if (frB < SL_NB && (frB >> 2) == tid) view_publish(v, frB, &sm.bucket2, &sm.bcnt2, sm.pre2);
+    __syncthreads();
+    const bool hasA = frA < SL_NB, hasB = frB < SL_NB;
+    if ((hasA && sm.bcnt > 32) || (hasB && sm.bcnt2 > 32)) {
+        __syncthreads();
+        return false;
+    }
+    const int bA = hasA ? sm.bucket : -1, bB = hasB ? sm.bucket2 : -1;
+    if (hasA || hasB) {
+        for (int c = tid; c < ne; c += SL_THREADS) {
+            const unsigned long long k = skey[c];
+            if (k == 0ull) continue;
+            const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
+            if (b == bA) {
+                const int at = atomicAdd(&sm.nb, 1);
+                if (at < 32) {
+                    sm.bkeys[at] = k;
+                    sm.bsz[at] = ssz[c];
+                }
+            }
+            if (b == bB) {
+                const int at = atomicAdd(&sm.nb2, 1);
+                if (at < 32) {
+                    sm.bkeys2[at] = k;
+                    sm.bsz2[at] = ssz[c];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // warp 0 resolves A, warp 1 resolves B (one shared copy of the code); a
+    // bucket that is kept whole has its threshold just below its lowest key
+    if (wid < 2) {
+        const bool isA = wid == 0;
+        const bool has = isA ? hasA : hasB;
+        if (has) {
+            const unsigned long long* bk = isA ? sm.bkeys : sm.bkeys2;
+            const int m = min(isA ? sm.nb : sm.nb2, 32);
+            unsigned long long mn = (tid & 31) < m ? bk[tid & 31] : ~0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mn = min(mn, (unsigned long long)__shfl_xor_sync(0xffffffffu, mn, o));
+            const long long* pre = isA ? sm.pre : sm.pre2;
+            resolve_boundary(bk, isA ? sm.bsz : sm.bsz2, m, pre[0], pre[1], pre[2], isA ? 1 : 0, mn, sm.rscr[wid], r,
+                             isA ? &sm.T : &sm.T2, isA ? &sm.flags : &sm.flags2);
+        } else if ((tid & 31) == 0) {
+            *(isA ? &sm.T : &sm.T2) = key_lo0 > 0 ? key_lo0 - 1 : 0ull;
+        }
+    }
+    __syncthreads();
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// scoring helpers (every CTA)
+// ---------------------------------------------------------------------------
+// Interleaved fma chains over the last subspace for J cells per thread (a
+// cell that is not separable runs the chain on column 0 and keeps acc).
+template <int J>
+IMI_DEV void score_chains(float (&acc)[SL_CPT], const bool (&sep)[SL_CPT], const int (&il)[SL_CPT],
+                          const float* q2, const float* cT, int ldT, int sub) {
+    float ch[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) ch[j] = acc[j];
+    for (int d0 = 0; d0 < sub; d0 += 8) {
+        float cv[8][J], qv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            qv[u] = q2[d0 + u];
+#pragma unroll
+            for (int j = 0; j < J; ++j) cv[u][j] = cT[(d0 + u) * ldT + il[j]];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int j = 0; j < J; ++j) ch[j] = __fmaf_rn(qv[u], cv[u][j], ch[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+        if (sep[j]) acc[j] = ch[j];
+}
+
+IMI_DEV int prefix_table_offset(const SelectArgs& a, int s, int sub) {
+    int off = 0;
+    for (int t = 0; t < s; ++t) off += sub * sl_ld(a.ks[t]);
+    return off;
+}
+
 __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
-    imi_select_kernel(SelectArgs a) {
+    imi_select_kernel(const __grid_constant__ SelectArgs a) {
     extern __shared__ __align__(16) unsigned char dyn[];
     SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
     cg::cluster_group cluster = cg::this_cluster();
@@ -180,13 +534,17 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     int table = 1;
     for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
     const int n = a.n_slots;
+    // slots at or above the bound are padding (masked by construction): they
+    // are never candidates, so neither the scoring nor the leader visits them
+    const int ne = (a.slot_bound > 0 && a.slot_bound < n) ? a.slot_bound : n;
     const int npad = (n + 1) & ~1;
-    const bool pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
-    const int pg_shift = __ffs(a.page_size) - 1;
-    auto pages_of = [&](int sz) -> int {
-        if (sz <= 0) return 0;
-        return pg_pow2 ? (sz + a.page_size - 1) >> pg_shift : (sz + a.page_size - 1) / a.page_size;
-    };
+    SelRules rules;
+    rules.nprobe = a.nprobe;
+    rules.max_tokens = a.max_tokens;
+    rules.buffer_pages = a.buffer_pages;
+    rules.page_size = a.page_size;
+    rules.pg_shift = __ffs(a.page_size) - 1;
+    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
 
     // identical layout in every CTA (DSMEM addresses are offsets)
     unsigned char* p = dyn + ((sizeof(SelHdr) + 15) & ~size_t(15));
@@ -199,33 +557,34 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     float* tab = reinterpret_cast<float*>(p);
     p += sizeof(float) * (table + 4);
     // transposed centroid tables: the last subspace [sub][ld(k_last)], then
-    // the prefix subspaces back to back; the leader reuses the region for the
-    // selected-cell lists once scoring is over
+    // the prefix subspaces back to back, then two scratch buffers for the
+    // intermediate prefix levels (S = 4); the leader reuses the region for
+    // the selected-cell lists once scoring is over
     float* cT = reinterpret_cast<float*>(p);
     const int ldT = sl_ld(k_last);
     float* cP = cT + (S > 1 ? sub * ldT : 0);
+    float* bufA = cP + (S > 1 ? prefix_table_offset(a, S - 1, sub) : 0);
+    float* bufB = bufA + 256;
     int* sel_slot = reinterpret_cast<int*>(p);
     int* sel_start = sel_slot + SL_SEL_MAX;
     int* sel_off = sel_start + SL_SEL_MAX;
 
     const size_t hs = (size_t)h;
-    auto stamp = [&](int k) {
-        if (a.phase_ns && tid == 0 && rank == 0) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            a.phase_ns[hs * 8 + k] = t;
-        }
-    };
-    stamp(0);
+    const bool stamping = a.phase_ns != nullptr && tid == 0 && rank == 0;
+#define SL_STAMP(k)                                                \
+    do {                                                           \
+        if (stamping) {                                            \
+            unsigned long long t_;                                 \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)); \
+            a.phase_ns[hs * 8 + (k)] = t_;                         \
+        }                                                          \
+    } while (0)
+    SL_STAMP(0);
     // let the attention kernel that follows (a programmatic dependent launch)
     // start setting up on the SMs this kernel leaves free
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    if (rank == 0 && tid == 0) {
-        sm.kmin = ~0ull;
-        sm.kmax = 0ull;
-    }
     // first half of the cluster barrier that guards the DSMEM stores: every
-    // CTA is running and the leader's header is set
+    // CTA is running
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
 
     const int32_t* sizes = a.cell_sizes + hs * n;
@@ -236,29 +595,21 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const float* subc = a.sub_centroids + hs * (size_t)S * a.kmax * sub;
 
     // ---------------- every CTA: all global loads at once ----------------
-    int poff[4] = {0, 0, 0, 0};  // offsets of the prefix tables within cP
     if (S > 1) {
-        int off = 0;
-        for (int s = 0; s < S - 1; ++s) {
-            poff[s] = off;
-            off += sub * sl_ld(a.ks[s]);
-        }
         for (int s = 0; s < S; ++s) {
             const int k = a.ks[s];
-            float* dst = s == S - 1 ? cT : cP + poff[s];
+            float* dst = s == S - 1 ? cT : cP + prefix_table_offset(a, s, sub);
             const int ld = sl_ld(k);
             const float* src = subc + (size_t)s * a.kmax * sub;
             const int total = k * sub;
-            for (int e = tid; e < total; e += SL_THREADS) {
-                const int i = e >> sub_shift, d = e & (sub - 1);
-                cp_async4(dst + d * ld + i, src + e);
-            }
+            for (int e = tid; e < total; e += SL_THREADS)
+                cp_async4(dst + (e & (sub - 1)) * ld + (e >> sub_shift), src + e);
         }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    const int chunk = (n + SL_CL - 1) / SL_CL;
+    const int chunk = (ne + SL_CL - 1) / SL_CL;
     const int c0 = rank * chunk;
-    const int c1 = min(n, c0 + chunk);
+    const int c1 = min(ne, c0 + chunk);
     int ccv[SL_CPT], szv[SL_CPT];
     bool mkv[SL_CPT], dkv[SL_CPT];
 #pragma unroll
@@ -271,45 +622,38 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         dkv[j] = in && dirty ? dirty[c] != 0 : false;
     }
     if (tid < a.dim) {
-        float qv[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) qv[g] = g < a.G ? bf16_bits_to_f32(a.q[(hs * a.G + g) * a.dim + tid]) : 0.0f;
         float acc = 0.0f;
-        for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, qv[g]);
+        for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bf16_bits_to_f32(a.q[(hs * a.G + g) * a.dim + tid]));
         qs[tid] = acc;
     }
     asm volatile("cp.async.wait_all;\n" ::: "memory");
     __syncthreads();
 
     // ---------------- every CTA: prefix table over the first S-1 subspaces ----------------
+    // level s chains subspace s from level s-1; the last level lands in tab
     if (S > 1) {
         int width = 1;
         for (int s = 0; s < S - 1; ++s) {
-            const int ks = a.ks[s];
-            const float* cs = cP + poff[s];
-            const int ld = sl_ld(ks);
+            const int ks = a.ks[s], ld = sl_ld(ks);
             const int total = width * ks;
+            const float* cs = cP + prefix_table_offset(a, s, sub);
+            const float* src = s == 0 ? nullptr : (((s - 1) & 1) ? bufB : bufA);
+            float* dst = s == S - 2 ? tab : ((s & 1) ? bufB : bufA);
             const float* qq = qs + s * sub;
-            float vals[16];
-            int cnt = 0;
-            for (int e = tid; e < total && cnt < 16; e += SL_THREADS, ++cnt) {
+            for (int e = tid; e < total; e += SL_THREADS) {
                 const int pi = e / ks, i = e - pi * ks;
-                float acc = s == 0 ? 0.0f : tab[pi];
+                float acc = src ? src[pi] : 0.0f;
 #pragma unroll 8
                 for (int d = 0; d < sub; ++d) acc = __fmaf_rn(qq[d], cs[d * ld + i], acc);
-                vals[cnt] = acc;
+                dst[e] = acc;
             }
-            if (s > 0) __syncthreads();  // every read of the previous level is done
-            cnt = 0;
-            for (int e = tid; e < total && cnt < 16; e += SL_THREADS, ++cnt) tab[e] = vals[cnt];
             __syncthreads();
             width = total;
         }
     }
-    stamp(1);
+    SL_STAMP(1);
 
     // ---------------- every CTA: score its slice ----------------
-    const float* q2 = qs + (S - 1) * sub;
     float acc[SL_CPT];
     int il[SL_CPT];
     bool sep[SL_CPT], cand[SL_CPT];
@@ -328,37 +672,12 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         }
     }
     if (S > 1) {
-        // interleaved chains over the last subspace; the number of live cells
-        // per thread is uniform over the CTA
-        // (a cell that is not separable runs the chain on column 0 and the
-        // result is discarded)
-        auto chains = [&](auto nj) {
-            constexpr int J = decltype(nj)::value;
-            float ch[J];
-#pragma unroll
-            for (int j = 0; j < J; ++j) ch[j] = acc[j];
-            for (int d0 = 0; d0 < sub; d0 += 8) {
-                float cv[8][J], qv[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    qv[u] = q2[d0 + u];
-#pragma unroll
-                    for (int j = 0; j < J; ++j) cv[u][j] = cT[(d0 + u) * ldT + il[j]];
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-#pragma unroll
-                    for (int j = 0; j < J; ++j) ch[j] = __fmaf_rn(qv[u], cv[u][j], ch[j]);
-            }
-#pragma unroll
-            for (int j = 0; j < J; ++j)
-                if (sep[j]) acc[j] = ch[j];
-        };
-        const int live = (c1 - c0 + SL_THREADS - 1) / SL_THREADS;
-        if (live <= 2)
-            chains(std::integral_constant<int, 2>{});
+        // the number of live cells per thread is uniform over the CTA
+        const float* q2 = qs + (S - 1) * sub;
+        if (c1 - c0 <= 2 * SL_THREADS)
+            score_chains<2>(acc, sep, il, q2, cT, ldT, sub);
         else
-            chains(std::integral_constant<int, SL_CPT>{});
+            score_chains<SL_CPT>(acc, sep, il, q2, cT, ldT, sub);
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
     {
@@ -399,342 +718,65 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             kmn = min(kmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmn, o));
             kmx = max(kmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmx, o));
         }
-        if (lid == 0 && kmx != 0ull) {
-            atomicMin(&lead->kmin, kmn);
-            atomicMax(&lead->kmax, kmx);
+        unsigned long long* wmn = sm.rscr[0];  // [SL_WARPS] minima, then maxima (free until the resolve)
+        if (lid == 0) {
+            wmn[wid] = kmn;
+            wmn[SL_WARPS + wid] = kmx;
+        }
+        __syncthreads();
+        if (tid < 32) {
+            unsigned long long m0 = tid < SL_WARPS ? wmn[tid] : ~0ull, m1 = tid < SL_WARPS ? wmn[SL_WARPS + tid] : 0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                m0 = min(m0, (unsigned long long)__shfl_xor_sync(0xffffffffu, m0, o));
+                m1 = max(m1, (unsigned long long)__shfl_xor_sync(0xffffffffu, m1, o));
+            }
+            if (tid == 0) {
+                lead->rmin[rank] = m0;
+                lead->rmax[rank] = m1;
+            }
         }
     }
+    if (a.scores_out)
+        for (int c = ne + rank * SL_THREADS + tid; c < n; c += SL_CL * SL_THREADS) a.scores_out[hs * n + c] = -INFINITY;
     cluster.sync();  // every score is in the leader
     if (rank != 0) return;
-    stamp(2);
-    const unsigned long long key_lo0 = sm.kmin, key_hi0 = sm.kmax;
-    const bool any_cand = key_hi0 != 0ull;
+    SL_STAMP(2);
+    unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
+    for (int r = 0; r < SL_CL; ++r) {
+        key_lo0 = min(key_lo0, sm.rmin[r]);
+        key_hi0 = max(key_hi0, sm.rmax[r]);
+    }
 
-    // One warp resolves a boundary bucket exactly: rank its (<= 32) elements,
-    // place them in rank order (lane r holds the element of rank r), scan their
-    // tokens and pages, and let the first lane whose rule fires name the
-    // boundary.  `scratch` holds 32 keys and 32 sizes for the warp.
-    auto resolve = [&](const unsigned long long* bk, const int* bs, int m, long long xc, long long xs, long long xp,
-                       bool use_pages, unsigned long long blo, unsigned long long* scratch, unsigned long long& T,
-                       unsigned long long& fl) {
-        const unsigned long long mk = lid < m ? bk[lid] : 0ull;
-        const int msz = lid < m ? bs[lid] : 0;
-        int rk = 0;
-#pragma unroll 8
-        for (int q = 0; q < 32; ++q) {
-            const unsigned long long o = __shfl_sync(0xffffffffu, mk, q);
-            rk += (q < m && o > mk) ? 1 : 0;
-        }
-        int* ssz2 = reinterpret_cast<int*>(scratch + 32);
-        if (lid < m) {
-            scratch[rk] = mk;
-            ssz2[rk] = msz;
-        }
-        __syncwarp();
-        const unsigned long long k = lid < m ? scratch[lid] : 0ull;
-        const int sz = lid < m ? ssz2[lid] : 0;
-        const int pg = pages_of(sz);
-        int isz = sz, ipg = pg;  // inclusive scans over the ranked elements
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int ts = __shfl_up_sync(0xffffffffu, isz, o);
-            const int tp = __shfl_up_sync(0xffffffffu, ipg, o);
-            if (lid >= o) {
-                isz += ts;
-                ipg += tp;
-            }
-        }
-        const long long bc = xc + lid, bsum = xs + (isz - sz), bpg = xp + (ipg - pg);
-        const bool rc = (bc >= a.nprobe) || (bsum >= a.max_tokens);
-        const bool rp = use_pages && (bpg + pg > a.buffer_pages);
-        const unsigned fire = __ballot_sync(0xffffffffu, lid < m && (rc || rp));
-        if (fire) {
-            const int f = __ffs(fire) - 1;
-            T = __shfl_sync(0xffffffffu, k, f);
-            fl = __shfl_sync(0xffffffffu, rc ? 1u : 0u, f) ? 1ull : 0ull;
-        } else {
-            T = blo > 0 ? blo - 1 : 0ull;
-            fl = 1ull;  // nothing fires here: the token rule fires just below this bucket
-        }
-        __syncwarp();
-    };
-
-    // Per-thread view of 4 buckets after a histogram round: thread t owns
-    // buckets SL_NB-1-4t .. SL_NB-4-4t (descending), with the exclusive
-    // (count, tokens, pages) prefixes of the candidates above them.
-    struct Scan {
-        int cv[4], sv[4], pv[4];
-        long long ec, es, ep;
-    };
-    auto clear_hist = [&]() {
-        for (int b = tid; b < SL_NB; b += SL_THREADS) {
-            sm.hcp[b] = 0ull;
-            sm.hsz[b] = 0u;
-        }
-        if (tid == 0) {
-            sm.nb = sm.nb2 = 0;
-            sm.first = sm.first2 = SL_NB;
-        }
-        __syncthreads();
-    };
-    auto add_hist = [&](int b, int sz) {
-        atomicAdd(&sm.hcp[b], (1ull << 32) | (unsigned long long)(unsigned)pages_of(sz));
-        atomicAdd(&sm.hsz[b], (unsigned)sz);
-    };
-    auto scan_hist = [&](long long C, long long Sz, long long Pg, Scan& sc) {
-        unsigned long long cp4 = 0ull;
-        unsigned int s4 = 0u;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int b = SL_NB - 1 - 4 * tid - q;
-            const unsigned long long v = sm.hcp[b];
-            const unsigned int w = sm.hsz[b];
-            sc.cv[q] = (int)(v >> 32);
-            sc.pv[q] = (int)(v & 0xffffffffull);
-            sc.sv[q] = (int)w;
-            cp4 += v;
-            s4 += w;
-        }
-        unsigned long long icp = cp4;
-        unsigned int is = s4;
-        sl_scan_pair(icp, is, sm);
-        const unsigned long long ecp = icp - cp4;
-        sc.ec = C + (long long)(ecp >> 32);
-        sc.ep = Pg + (long long)(ecp & 0xffffffffull);
-        sc.es = Sz + (long long)(is - s4);
-    };
-    auto publish = [&](const Scan& sc, int fr, int& bucket, int& bcnt, long long* pre) {
-        long long xc = sc.ec, xs = sc.es, xp = sc.ep;
-        for (int q = 0; q < (fr & 3); ++q) {
-            xc += sc.cv[q];
-            xs += sc.sv[q];
-            xp += sc.pv[q];
-        }
-        bucket = SL_NB - 1 - fr;
-        bcnt = sc.cv[fr & 3];
-        pre[0] = xc;
-        pre[1] = xs;
-        pre[2] = xp;
-    };
-    auto shift_of = [&](unsigned long long lo, unsigned long long hi) {
-        const unsigned long long span = hi - lo;
-        const int bits = span ? 64 - __clzll(span) : 0;
-        return bits > SL_NB_BITS ? bits - SL_NB_BITS : 0;
-    };
-
-    // Refinement search for one boundary (the rare path: a boundary bucket with
-    // more than 32 elements).  T: selected = key > T; flags = 1 when the rank or
-    // token rule (not only the page rule) fires at the boundary element.
-    auto search = [&](bool use_pages, unsigned long long& T_out, unsigned long long& flags_out) {
-        unsigned long long lo = key_lo0, hi = key_hi0;
-        long long C = 0, Sz = 0, Pg = 0;  // totals of candidates with key > hi
-        while (true) {
-            const int shift = shift_of(lo, hi);
-            clear_hist();
-            for (int c = tid; c < n; c += SL_THREADS) {
-                const unsigned long long k = skey[c];
-                if (k == 0ull || k < lo || k > hi) continue;
-                add_hist((int)((k - lo) >> shift), ssz[c]);
-            }
-            __syncthreads();
-            Scan sc;
-            scan_hist(C, Sz, Pg, sc);
-            {
-                long long ec = sc.ec, es = sc.es, ep = sc.ep;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    if (sc.cv[q] > 0 && ((ec + sc.cv[q] > a.nprobe) || (es + sc.sv[q] >= a.max_tokens) ||
-                                         (use_pages && ep + sc.pv[q] > a.buffer_pages))) {
-                        atomicMin(&sm.first, 4 * tid + q);
-                        break;
-                    }
-                    ec += sc.cv[q];
-                    es += sc.sv[q];
-                    ep += sc.pv[q];
-                }
-            }
-            __syncthreads();
-            const int fr = sm.first;
-            if (fr == SL_NB) {
-                T_out = lo > 0 ? lo - 1 : 0ull;  // no rule fires in [lo, hi]: all of it is selected
-                flags_out = 0ull;
-                __syncthreads();
-                return;
-            }
-            if ((fr >> 2) == tid) publish(sc, fr, sm.bucket, sm.bcnt, sm.pre);
-            __syncthreads();
-            const int cnt = sm.bcnt;
-            const long long qc = sm.pre[0], qsz = sm.pre[1], qp = sm.pre[2];
-            const unsigned long long blo = lo + ((unsigned long long)sm.bucket << shift);
-            const unsigned long long bend = blo + ((1ull << shift) - 1ull);
-            const unsigned long long bhi = (bend < blo || bend > hi) ? hi : bend;
-            if (cnt <= 32) {
-                for (int c = tid; c < n; c += SL_THREADS) {
-                    const unsigned long long k = skey[c];
-                    if (k == 0ull || k < blo || k > bhi) continue;
-                    const int at = atomicAdd(&sm.nb, 1);
-                    if (at < 32) {
-                        sm.bkeys[at] = k;
-                        sm.bsz[at] = ssz[c];
-                    }
-                }
-                __syncthreads();
-                if (wid == 0) {
-                    unsigned long long T, fl;
-                    resolve(sm.bkeys, sm.bsz, min(sm.nb, 32), qc, qsz, qp, use_pages, blo, sm.rscr[0], T, fl);
-                    if (lid == 0) {
-                        sm.T = T;
-                        sm.flags = fl;
-                    }
-                }
-                __syncthreads();
-                T_out = sm.T;
-                flags_out = sm.flags;
-                __syncthreads();
-                return;
-            }
-            lo = blo;
-            hi = bhi;
-            C = qc;
-            Sz = qsz;
-            Pg = qp;
-            __syncthreads();
-        }
-    };
-
-    // First round for both boundaries at once (the common case resolves here):
-    // A = all three rules, B = rank and token rules only (the kept list before
-    // page truncation).  Returns false when a boundary bucket holds more than
-    // 32 elements; the caller then refines each boundary on its own.
-    auto search_both = [&](unsigned long long& TA, unsigned long long& TB) -> bool {
-        // buckets linear in the score: b = floor((s - smin) * scale), monotone
-        // in s; equal scores share a bucket and are ordered by the warp rank
-        auto score_of = [](unsigned long long k) {
-            const uint32_t o = (uint32_t)(k >> 32);
-            return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-        };
-        const float smin = score_of(key_lo0), smax = score_of(key_hi0);
-        const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
-        auto bucket_of = [&](unsigned long long k) {
-            const float v = (score_of(k) - smin) * scale;
-            return min(SL_NB - 1, max(0, (int)v));
-        };
-        clear_hist();
-        for (int c = tid; c < n; c += SL_THREADS) {
-            const unsigned long long k = skey[c];
-            if (k == 0ull) continue;
-            add_hist(bucket_of(k), ssz[c]);
-        }
-        __syncthreads();
-        Scan sc;
-        scan_hist(0, 0, 0, sc);
-        {
-            long long ec = sc.ec, es = sc.es, ep = sc.ep;
-            bool doneA = false, doneB = false;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                if (sc.cv[q] > 0) {
-                    const bool rule = (ec + sc.cv[q] > a.nprobe) || (es + sc.sv[q] >= a.max_tokens);
-                    if (!doneA && (rule || ep + sc.pv[q] > a.buffer_pages)) {
-                        atomicMin(&sm.first, 4 * tid + q);
-                        doneA = true;
-                    }
-                    if (!doneB && rule) {
-                        atomicMin(&sm.first2, 4 * tid + q);
-                        doneB = true;
-                    }
-                }
-                ec += sc.cv[q];
-                es += sc.sv[q];
-                ep += sc.pv[q];
-            }
-        }
-        __syncthreads();
-        const int frA = sm.first, frB = sm.first2;
-        if (frA < SL_NB && (frA >> 2) == tid) publish(sc, frA, sm.bucket, sm.bcnt, sm.pre);
-        if (frB < SL_NB && (frB >> 2) == tid) publish(sc, frB, sm.bucket2, sm.bcnt2, sm.pre2);
-        __syncthreads();
-        const bool hasA = frA < SL_NB, hasB = frB < SL_NB;
-        if ((hasA && sm.bcnt > 32) || (hasB && sm.bcnt2 > 32)) {
-            __syncthreads();
-            return false;
-        }
-        const int bA = hasA ? sm.bucket : -1, bB = hasB ? sm.bucket2 : -1;
-        unsigned long long minA = ~0ull, minB = ~0ull;  // lowest key of each boundary bucket
-        if (hasA || hasB) {
-            for (int c = tid; c < n; c += SL_THREADS) {
-                const unsigned long long k = skey[c];
-                if (k == 0ull) continue;
-                const int b = bucket_of(k);
-                if (b == bA) {
-                    const int at = atomicAdd(&sm.nb, 1);
-                    if (at < 32) {
-                        sm.bkeys[at] = k;
-                        sm.bsz[at] = ssz[c];
-                    }
-                }
-                if (b == bB) {
-                    const int at = atomicAdd(&sm.nb2, 1);
-                    if (at < 32) {
-                        sm.bkeys2[at] = k;
-                        sm.bsz2[at] = ssz[c];
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        if (wid == 0) {
-            unsigned long long T = ~0ull, fl = 0ull;
-            if (hasA) {
-                const int m = min(sm.nb, 32);
-                for (int q = 0; q < m; ++q) minA = min(minA, sm.bkeys[q]);
-                // "whole bucket kept" threshold = just below its lowest key
-                resolve(sm.bkeys, sm.bsz, m, sm.pre[0], sm.pre[1], sm.pre[2], true, minA, sm.rscr[0], T, fl);
-            } else {
-                T = key_lo0 > 0 ? key_lo0 - 1 : 0ull;
-            }
-            if (lid == 0) sm.T = T;
-        } else if (wid == 1) {
-            unsigned long long T = ~0ull, fl = 0ull;
-            if (hasB) {
-                const int m = min(sm.nb2, 32);
-                for (int q = 0; q < m; ++q) minB = min(minB, sm.bkeys2[q]);
-                resolve(sm.bkeys2, sm.bsz2, m, sm.pre2[0], sm.pre2[1], sm.pre2[2], false, minB, sm.rscr[1], T, fl);
-            } else {
-                T = key_lo0 > 0 ? key_lo0 - 1 : 0ull;
-            }
-            if (lid == 0) sm.T2 = T;
-        }
-        __syncthreads();
-        TA = sm.T;
-        TB = sm.T2;
-        __syncthreads();
-        return true;
-    };
-
+    // ---------------- leader: the two boundaries ----------------
     unsigned long long thrA = ~0ull, thrB = ~0ull;  // no candidates: nothing selected
-    if (any_cand) {
-        if (!search_both(thrA, thrB)) {
-            unsigned long long fl;
-            search(true, thrA, fl);
-            if (fl) {
+    if (key_hi0 != 0ull) {
+        if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
+            thrA = sm.T;
+            thrB = sm.T2;
+        } else {
+            search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
+            thrA = sm.T;
+            const bool token_or_rank = sm.flags != 0ull;
+            __syncthreads();
+            if (token_or_rank) {
                 thrB = thrA;
             } else {
-                unsigned long long fl2;
-                search(false, thrB, fl2);
+                search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 0, rules);
+                thrB = sm.T;
             }
         }
+        __syncthreads();
     }
-    stamp(3);
+    SL_STAMP(3);
 
     // ---------------- leader: emission in slot order ----------------
     // warp w owns the contiguous slot range [w*R, (w+1)*R); lanes take
     // consecutive slots (conflict-free); ballots count and rank
-    const int R = ((n + SL_WARPS - 1) / SL_WARPS + 31) & ~31;
-    const int w0 = wid * R, w1 = min(n, w0 + R);
+    const int R = ((ne + SL_WARPS - 1) / SL_WARPS + 31) & ~31;
+    const int w0 = wid * R, w1 = min(ne, w0 + R);
     {
         int wsel = 0, wkept = 0;
-#pragma unroll 4
         for (int base = w0; base < w1; base += 32) {
             const int c = base + lid;
             const unsigned long long k = c < w1 ? skey[c] : 0ull;
@@ -748,16 +790,15 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     }
     __syncthreads();
     int sel_base = 0, nsel = 0, nkept = 0;
-#pragma unroll
     for (int q = 0; q < SL_WARPS; ++q) {
-        if (q < wid) sel_base += sm.wsel[q];
-        nsel += sm.wsel[q];
+        const int ws = sm.wsel[q];
+        if (q < wid) sel_base += ws;
+        nsel += ws;
         nkept += sm.wkept[q];
     }
     {
         int si = sel_base;
         const unsigned lt = (1u << lid) - 1u;
-#pragma unroll 4
         for (int base = w0; base < w1; base += 32) {
             const int c = base + lid;
             const unsigned long long k = c < w1 ? skey[c] : 0ull;
@@ -772,7 +813,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         }
     }
     __syncthreads();
-    stamp(4);
+    SL_STAMP(4);
     // row offsets of the selected cells (slot order) by one block scan;
     // thread t owns entries 4t .. 4t+3
     const int ns = min(nsel, SL_SEL_MAX);
@@ -821,7 +862,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             int f = 0;
             if (pidx < dcount) {
                 const int cid = dids[pidx];
-                if (cid >= 0 && cid < n) {
+                if (cid >= 0 && cid < ne) {
                     const unsigned long long k = skey[cid];
                     f = (k != 0ull && k > thrB) ? 1 : 0;
                 }
@@ -838,7 +879,8 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         total = min(total + appended, a.exec_capacity);
     }
     __syncthreads();
-    stamp(5);
+    SL_STAMP(5);
+#undef SL_STAMP
     if (tid == 0) {
         a.sel_count[h] = min(nsel, a.nprobe);
         a.row_count[h] = total;
@@ -852,8 +894,11 @@ size_t select_smem_bytes(const SelectArgs& a) {
     for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
     const int sub = a.dim / S;
     size_t tables = 0;
-    if (S > 1)
+    if (S > 1) {
         for (int s = 0; s < S; ++s) tables += (size_t)sub * sl_ld(a.ks[s]) * sizeof(float);
+        // intermediate prefix levels (S = 4): level 0 (<= 255) and level 1
+        if (S > 2) tables += (256 + (size_t)a.ks[0] * a.ks[1]) * sizeof(float);
+    }
     const size_t lists = 3 * (size_t)SL_SEL_MAX * sizeof(int);  // reused for the selected-cell lists
     const size_t region = tables > lists ? tables : lists;
     const size_t npad = ((size_t)a.n_slots + 1) & ~size_t(1);
@@ -865,7 +910,8 @@ int select_max_slots() { return SL_MAX_SLOTS; }
 
 cudaError_t launch_select(const SelectArgs& a, cudaStream_t st) {
     const size_t sm = select_smem_bytes(a);
-    cudaError_t e = cudaFuncSetAttribute(imi_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    static int smem_set[64] = {};
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_select_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
     imi_select_kernel<<<dim3(SL_CL, a.bg), SL_THREADS, sm, st>>>(a);
     return cudaGetLastError();

@@ -184,7 +184,8 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
                  row_count: torch.Tensor, centroids: Optional[torch.Tensor] = None,
                  cell_dirty: Optional[torch.Tensor] = None, delta_cell_ids: Optional[torch.Tensor] = None,
                  delta_count: Optional[torch.Tensor] = None, kept_count: Optional[torch.Tensor] = None,
-                 scores_out: Optional[torch.Tensor] = None, phase_ns: Optional[torch.Tensor] = None) -> None:
+                 scores_out: Optional[torch.Tensor] = None, phase_ns: Optional[torch.Tensor] = None,
+                 slot_bound: int = 0) -> None:
     """Score cells, choose them (top-nprobe, token budget, page truncation) and
     write the execution row list.  q: [bg, G, D] bf16 contiguous."""
     bg, G, D = q.shape
@@ -211,6 +212,7 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
     d.row_index, d.row_count = row_index.data_ptr(), row_count.data_ptr()
     d.scores_out = scores_out.data_ptr() if scores_out is not None else None
     d.phase_ns = phase_ns.data_ptr() if phase_ns is not None else None
+    d.slot_bound = int(slot_bound)
     L = _lib.load()
     _lib.check(L.imi_select_cells(ctypes.byref(d), _stream(q.device)), "imi_select_cells")
 

@@ -122,6 +122,9 @@ typedef struct imi_select_desc {
     float* scores_out;                     /* [bg, n_slots] out or NULL */
     unsigned long long* phase_ns;          /* [bg, 8] out or NULL: device timestamps (ns) of the
                                               selection's phases, a profiling aid */
+    int32_t slot_bound;                    /* 0, or a bound on the occupied slots: every slot at or
+                                              above it is masked (padding) in every group, e.g. the
+                                              largest n_active of the build; the kernel skips them */
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
@@ -224,6 +227,14 @@ IMI_API int imi_sparse_attention_noalloc(const imi_attn_desc* desc, void* stream
  * the same q, row_index, row_count and exec_capacity. */
 IMI_API int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
                               void* stream);
+/* One decode layer in one call: append (NULL to skip), the batched cell
+ * assignment (NULL to skip; runs after the append), apply (NULL to skip),
+ * select and attention -- the order of decode_update_kv_cache followed by
+ * attn_func (runtime.py:378-392, async_update.py:112-161, retrieval.py:320-602).
+ * Every descriptor is validated before the first launch. */
+IMI_API int imi_decode_layer(const imi_append_desc* append, const imi_async_desc* async_assign,
+                             const imi_apply_desc* apply, const imi_select_desc* sel, const imi_attn_desc* attn,
+                             void* stream);
 IMI_API int imi_decode_append(const imi_append_desc* desc, void* stream);
 IMI_API int imi_async_assign(const imi_async_desc* desc, void* stream);
 IMI_API int imi_apply_updates(const imi_apply_desc* desc, void* stream);

@@ -126,7 +126,7 @@ def _decode_setup(heads=8, G=4, ctx=8192, parts=2, ks=(16, 16), iters=10, budget
     return K, V, Q, k, v, sizes, idx
 
 
-def _select(idx, q, sizes, static_len, exec_cap, scores=True):
+def _select(idx, q, sizes, static_len, exec_cap, scores=True, slot_bound=0):
     bg = q.shape[0]
     dev = q.device
     sel = torch.full((bg, sizes.nprobe), -1, dtype=torch.int32, device=dev)
@@ -138,13 +138,17 @@ def _select(idx, q, sizes, static_len, exec_cap, scores=True):
     ops.select_cells(q=q, index=idx, nprobe=sizes.nprobe, max_tokens=sizes.max_retrieval_tokens,
                      buffer_pages=sizes.buffer_size, page_size=8, padding_id=idx.n_slots - 1, static_len=static_len,
                      exec_capacity=exec_cap, sel_cells=sel, sel_count=cnt, row_index=rows, row_count=rc,
-                     kept_count=kept, scores_out=sc)
+                     kept_count=kept, scores_out=sc, slot_bound=slot_bound)
     torch.cuda.synchronize()
     return sel, cnt, rows, rc, sc, kept
 
 
-def test_select_matches_oracle_cfg0():
+@pytest.mark.parametrize("bounded", [False, True])
+def test_select_matches_oracle_cfg0(bounded):
+    """bounded: the selection only visits slots below the largest n_active
+    (everything above is padding); the results must not change."""
     K, V, Q, k, v, sizes, idx = _decode_setup()
+    bound = int(idx.n_active.max()) if bounded else 0
     heads, G = 8, 4
     static_len = 97
     exec_cap = sizes.buffer_size * 8 + 96 + 16
@@ -154,7 +158,7 @@ def test_select_matches_oracle_cfg0():
     offs = idx.cell_offsets.cpu().numpy()
     for t in range(16):
         q = Q[t].reshape(heads, G, 128).contiguous()
-        sel, cnt, rows, rc, sc, kept = _select(idx, q.cuda(), sizes, static_len, exec_cap)
+        sel, cnt, rows, rc, sc, kept = _select(idx, q.cuda(), sizes, static_len, exec_cap, slot_bound=bound)
         qb = O.bf16_bits(q)
         for h in range(heads):
             ref_sc = O.scores(qb[h], cents[h], mask[h])
@@ -171,6 +175,29 @@ def test_select_matches_oracle_cfg0():
                 exp.extend(range(offs[h, c], offs[h, c] + csz[h, c]))
             assert int(rc[h]) == len(exp)
             np.testing.assert_array_equal(rows[h, :len(exp)].cpu().numpy(), np.array(exp, dtype=np.int64).astype(np.int32))
+
+
+def test_select_repeatable_under_reruns():
+    """The same query, selected many times in both modes, gives the oracle's
+    counts every time (a cross-CTA race would show up as a rare mismatch)."""
+    K, V, Q, k, v, sizes, idx = _decode_setup()
+    heads, G = 8, 4
+    exec_cap = sizes.buffer_size * 8 + 96 + 16
+    cents, mask, csz = idx.centroids.cpu().numpy(), idx.cell_mask.cpu().numpy(), idx.cell_sizes.cpu().numpy()
+    bound = int(idx.n_active.max())
+    for t in range(16):
+        qb = O.bf16_bits(Q[t].reshape(heads, G, 128))
+        exp = []
+        for h in range(heads):
+            ref_sel, pre = O.select(O.scores(qb[h], cents[h], mask[h]), csz[h], sizes.nprobe,
+                                    sizes.max_retrieval_tokens, sizes.buffer_size, 8, idx.n_slots - 1)
+            exp.append((len(ref_sel), int((pre != idx.n_slots - 1).sum())))
+        qd = Q[t].reshape(heads, G, 128).contiguous().cuda()
+        for rep in range(6):
+            for bnd in (0, bound):
+                _, cnt, _, _, _, kept = _select(idx, qd, sizes, 97, exec_cap, scores=False, slot_bound=bnd)
+                got = list(zip(cnt.tolist(), kept.tolist()))
+                assert got == exp, (t, rep, bnd)
 
 
 def _zone(K, V, heads, static_len, cap):
