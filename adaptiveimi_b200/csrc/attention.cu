@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     // Launched as a programmatic dependent of the select kernel: everything
     // above overlaps its tail; every global read comes after this wait.
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    // the next layer's append (a programmatic dependent) may start launching
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     const int rows_total = a.row_count[h];
     int chunk = (rows_total + a.splits - 1) / a.splits;
@@ -420,17 +422,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     // programmatic dependent launch: the CTAs may start (barrier set-up) while
     // the kernel before them in the stream finishes; they wait for it with
     // griddepcontrol.wait before their first global read
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.splits, a.bg);
-    cfg.blockDim = dim3(AT_WARPS * 32);
-    cfg.dynamicSmemBytes = sm;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, imi_attn_kernel, a);
+    e = launch_pdl(imi_attn_kernel, dim3(a.splits, a.bg), dim3(AT_WARPS * 32), sm, st, a);
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess || a.counters) return e;

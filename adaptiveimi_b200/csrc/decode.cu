@@ -48,7 +48,11 @@ __global__ void imi_similarity_kernel(const uint16_t* __restrict__ q, const floa
 // (optionally) the async-update batch slot (runtime.py:378-392,
 // async_update.py:115-117).  One warp per (group, tensor).
 // ----------------------------------------------------------------------------
-__global__ void imi_append_kernel(AppendArgs a) {
+__global__ void imi_append_kernel(const __grid_constant__ AppendArgs a) {
+    // programmatic dependent of the previous kernel: wait for it, then let the
+    // next one (the selection) start its launch
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int h = blockIdx.x;
     const int t = threadIdx.x >> 5;  // 0 = keys, 1 = values
     const int lane = threadIdx.x & 31;
@@ -386,8 +390,7 @@ cudaError_t launch_similarity(const uint16_t* q, const float* cent, float* out, 
 }
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t st) {
-    imi_append_kernel<<<a.bg, 64, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(imi_append_kernel, dim3(a.bg), dim3(64), 0, st, a);
 }
 
 size_t async_smem_bytes(const AsyncArgs& a) {

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/imi_b200.h"
 
@@ -34,6 +35,26 @@ cudaError_t launch_apply(const ApplyArgs& a, cudaStream_t st);
 size_t build_workspace_bytes(int heads, int n, int dim, int parts, const int* ks);
 void set_last_error(const std::string& msg);
 cudaError_t ensure_smem(const void* func, size_t bytes, int* cache, int cache_len);
+
+// Programmatic dependent launch: the kernel may be scheduled while the kernel
+// before it in the stream is still running (once that one has executed
+// griddepcontrol.launch_dependents or finished); it must execute
+// griddepcontrol.wait before touching memory the earlier kernels write.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why);
 
 }  // namespace imi

@@ -586,6 +586,9 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     // first half of the cluster barrier that guards the DSMEM stores: every
     // CTA is running
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    // launched as a programmatic dependent (of the append): everything above
+    // overlapped the previous kernel; every global read comes after this
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
     const int32_t* sizes = a.cell_sizes + hs * n;
     const uint8_t* mask = a.cell_mask + hs * n;
@@ -913,8 +916,7 @@ cudaError_t launch_select(const SelectArgs& a, cudaStream_t st) {
     static int smem_set[64] = {};
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_select_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
-    imi_select_kernel<<<dim3(SL_CL, a.bg), SL_THREADS, sm, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(imi_select_kernel, dim3(SL_CL, a.bg), dim3(SL_THREADS), sm, st, a);
 }
 
 }  // namespace imi
