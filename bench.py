@@ -49,6 +49,11 @@ CFG = dict(model="Llama-3-8B-geometry", layers=32, q_heads=32, kv_heads=8, head_
            subspace_parts=2, retrieval_budget=0.1, static_start=32, static_end=64, buffer_cluster_num=32,
            max_new_length=257, theta=500000.0, components=64)
 KMEANS = {"max_iters": 20, "tol": 0.0005, "early_stop_min_iter": 20, "early_stop_rel_tol": 0.0005}
+# DRAM bytes per attention launch at this geometry, from one ncu capture of
+# `python bench.py --layers 2 --steps 2 --warmup 3 --no-cpu-baseline` with
+# --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+# -k regex:imi_attn_kernel -s 4 -c 3 (each launch is one full layer).
+ATTN_TRAFFIC_BYTES = 50_226_539
 ASYNC = {"enabled": True, "batch": 16, "threshold": 16, "delta_tokens": 512}
 
 
@@ -210,11 +215,12 @@ def run_ours(args):
     qd, kd, vd = decode_inputs(means, G, ctx, steps_total, dev)
 
     def step(t, q_src, k_src, v_src, out_sink=None):
+        outs = []
         for l in range(L):
             cache.decode_update_kv_cache(k_src[l], v_src[l], l)
-            o = imi_decode_attn(q_src[l], None, None, l, cache)
-            if out_sink is not None:
-                out_sink[l].copy_(o, non_blocking=True)
+            outs.append(imi_decode_attn(q_src[l], None, None, l, cache))
+        if out_sink is not None:  # the step's result: every layer's output, one read-back
+            out_sink.copy_(torch.stack(outs), non_blocking=True)
 
     # ---- warmup (device inputs)
     for t in range(args.warmup):
@@ -299,7 +305,9 @@ def run_ours(args):
         "roofline": {"kernel": "imi_attn_kernel (gather attention with in-kernel split merge)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": None,
+                     "traffic": ATTN_TRAFFIC_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 3 launches of "
+                                       "the same kernel on the same geometry (profiles/imi_attn_kernel_cfg1_128K.md)",
                      "algorithmic_bytes_per_launch": int(attn["algo_bytes"]),
                      "avg_launch_us": round(attn_avg_us, 3), "launches_timed": attn["launches"],
                      "rows_per_launch": attn["rows_per_launch"]},
@@ -325,9 +333,10 @@ def run_ours(args):
 
 def attention_kernel_pass(cache, q_last, L, hl, G, dev, repeats=6):
     """Live CUDA-event timing of the attention kernel alone (imi_sparse_attention:
-    gather attention + split combine) on every layer's row list of the last
-    decode step, cycling through the 32 layers so that each launch streams its
-    rows from HBM (the layers' rows together exceed L2).
+    gather attention with the in-kernel split merge) on every layer's row list
+    of the last decode step: sweeps of the 32 layers launched back to back (as
+    in the decode pipeline), one event pair per sweep, so each launch streams
+    its rows from HBM (the layers' rows together exceed L2).
 
     Algorithmic bytes per launch = rows * (256 B key + 256 B value + 4 B row
     index) + q and out (bf16) + the split partials written and read back."""
@@ -350,27 +359,44 @@ def attention_kernel_pass(cache, q_last, L, hl, G, dev, repeats=6):
     part_o = torch.empty((bg, cache.splits, G, 128), dtype=torch.float32, device=dev)
     part_ml = torch.empty((bg, cache.splits, G, 2), dtype=torch.float32, device=dev)
     counters = torch.zeros((bg,), dtype=torch.int32, device=dev)
+    # one descriptor per layer, built once: the timed loop is C-ABI calls only,
+    # so launches queue back to back and the events bracket kernel time
+    import ctypes
+    from adaptiveimi_b200 import _lib
+    L_ = _lib.load()
+    descs = []
+    for l in range(L):
+        q, r = rows[l]
+        d = _lib.AttnDesc()
+        d.bg, d.G, d.splits, d.exec_capacity = bg, G, cache.splits, cache.execution_stride
+        d.scale = 1.0 / math.sqrt(128)
+        d.q, d.row_index, d.row_count = q.data_ptr(), r.data_ptr(), rcs[l].data_ptr()
+        d.list_keys, d.list_values = cache.index[l].list_keys.data_ptr(), cache.index[l].list_values.data_ptr()
+        d.list_rows = cache.index[l].list_keys.shape[1]
+        d.static_keys, d.static_values = cache.steady_zone_keys[l].data_ptr(), cache.steady_zone_values[l].data_ptr()
+        d.static_rows = cache.static_capacity
+        d.part_o, d.part_ml, d.out, d.counters = part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr(), \
+            counters.data_ptr()
+        descs.append(d)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    # one event pair per sweep over the L layers: events between launches
+    # would break the programmatic-launch overlap the decode pipeline has
     evs = []
     torch.cuda.synchronize()
     for rep in range(repeats + 1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
         for l in range(L):
-            q, r = rows[l]
-            zk = cache.steady_zone_keys[l].view(bg, cache.static_capacity, 128)
-            zv = cache.steady_zone_values[l].view(bg, cache.static_capacity, 128)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            ops.sparse_attention(q=q, row_index=r, row_count=rcs[l], list_keys=cache.index[l].list_keys,
-                                 list_values=cache.index[l].list_values, static_keys=zk, static_values=zv, out=out,
-                                 part_o=part_o, part_ml=part_ml, splits=cache.splits, counters=counters)
-            b.record()
-            if rep > 0:  # the first sweep is warmup
-                evs.append((a, b))
+            _lib.check(L_.imi_sparse_attention(ctypes.byref(descs[l]), stream), "imi_sparse_attention")
+        b.record()
+        if rep > 0:  # the first sweep is warmup
+            evs.append((a, b))
     torch.cuda.synchronize()
-    times = [a.elapsed_time(b) * 1e3 for a, b in evs]
+    times = [a.elapsed_time(b) * 1e3 / L for a, b in evs]
     total_rows = sum(int(rc.to(torch.int64).sum()) for rc in rcs)
     rows_per_launch = total_rows / L
     algo = rows_per_launch * (512 + 4) + bg * G * 128 * 2 * 2 + bg * cache.splits * G * (128 + 2) * 4 * 2
-    return {"avg_us": sum(times) / len(times), "algo_bytes": algo, "launches": len(times),
+    return {"avg_us": sum(times) / len(times), "algo_bytes": algo, "launches": len(times) * L,
             "rows_per_launch": rows_per_launch}
 
 
