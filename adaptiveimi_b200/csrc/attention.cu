@@ -71,7 +71,7 @@ IMI_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     return false;
 }
-// One row, global -> shared, completing on `bar` (no multicast).
+// One row, global -> shared, completing on `bar`; a plain load into this CTA only.
 IMI_DEV void bulk_row(uint32_t dst, const void* src, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                  "l"(src), "r"((uint32_t)AT_ROWB), "r"(bar)
@@ -313,14 +313,22 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
         }
     }
     if (!a.counters) return;  // a separate merge launch follows
-    // the last CTA of this group merges the split partials (the counter self-resets)
+    // the last CTA of this group merges the split partials (the counter
+    // self-resets): the block barrier orders every thread's partial stores
+    // before thread 0's release, and thread 0's acquire plus the barrier
+    // order the merging CTA's loads after all of them
     __shared__ int s_last;
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(&a.counters[h], 1) == a.splits - 1);
+    if (threadIdx.x == 0) {
+        unsigned old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;\n"
+                     : "=r"(old)
+                     : "l"(a.counters + h)
+                     : "memory");
+        s_last = old == (unsigned)(a.splits - 1);
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     // Parallel merge.  Warp g reduces query head g's (m, l) over the splits
     // (lanes stride the splits, loads independent) and leaves one weight
     // 2^(m_q - M) per split in shared memory; then every thread sums float4

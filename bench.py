@@ -170,6 +170,7 @@ def decode_inputs(means_per_layer, G, ctx, steps, dev, seed=0):
 def run_ours(args):
     from adaptiveimi_b200.attn import imi_decode_attn
     from adaptiveimi_b200.cache import adpimi_cache
+    from adaptiveimi_b200.sharding import max_over_ranks, shard_kv_heads
 
     ws, rank, local = dist_env()
     if ws > 1:
@@ -178,10 +179,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     L, ctx, kvh, G = args.layers, args.context, CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"]
-    if kvh % ws != 0:
-        raise SystemExit(f"{kvh} KV heads do not shard over {ws} GPUs")
-    hl = kvh // ws
-    head0 = rank * hl
+    head0, hl = shard_kv_heads(kvh, ws, rank)
     steps_total = args.steps + args.warmup
     cache = adpimi_cache(
         valid_start=[0], layer_num=L, batch_size=1, max_length=ctx + CFG["max_new_length"], num_key_value_heads=hl,
@@ -274,10 +272,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
     # ---- max over ranks
-    vals = torch.tensor([dev_ms, e2e_ms, attn["avg_us"], build_ms], dtype=torch.float64, device=dev)
-    if ws > 1:
-        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
-    dev_ms, e2e_ms, attn_avg_us, build_ms_max = vals.tolist()
+    dev_ms, e2e_ms, attn_avg_us, build_ms_max = max_over_ranks([dev_ms, e2e_ms, attn["avg_us"], build_ms], dev)
     if rank != 0:
         if ws > 1:
             torch.distributed.destroy_process_group()
