@@ -47,7 +47,7 @@ class SelectDesc(ctypes.Structure):
         ("delta_capacity", i32), ("exec_capacity", i32),
         ("sel_cells", P), ("sel_count", P), ("kept_count", P), ("row_index", P), ("row_count", P),
         ("scores_out", P), ("phase_ns", P),
-        ("slot_bound", i32),
+        ("slot_bound", i32), ("key_base", i32), ("cand_out", P),
     ]
 
 
@@ -60,7 +60,23 @@ class AttnDesc(ctypes.Structure):
         ("static_keys", P), ("static_values", P), ("static_rows", i64),
         ("delta_keys", P), ("delta_values", P), ("delta_rows", i64),
         ("part_o", P), ("part_ml", P), ("out", P), ("counters", P), ("status", P),
+        ("o_part", P), ("ml_part", P),
     ]
+
+
+class MergeDesc(ctypes.Structure):
+    _fields_ = [
+        ("bg", i32), ("shards", i32), ("cap", i32), ("rank", i32), ("key_base", i32),
+        ("cand", P), ("cell_offsets", P), ("n_slots", i32),
+        ("nprobe", i32), ("max_tokens", i32), ("buffer_pages", i32), ("page_size", i32),
+        ("static_len", i32), ("exec_capacity", i32),
+        ("sel_cells", P), ("sel_count", P), ("row_index", P), ("row_count", P),
+    ]
+
+
+class CombineDesc(ctypes.Structure):
+    _fields_ = [("shards", i32), ("bg", i32), ("G", i32), ("part_stride", i64), ("o_parts", P), ("ml_parts", P),
+                ("out", P)]
 
 
 class AppendDesc(ctypes.Structure):
@@ -97,7 +113,7 @@ EXPORTS = (
     "imi_abi_version", "imi_last_error", "imi_build_workspace_size", "imi_build_index",
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
     "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_decode_layer",
-    "imi_sparse_attention_noalloc",
+    "imi_merge_candidates", "imi_combine_partials", "imi_sparse_attention_noalloc",
 )
 
 _lib = None
@@ -133,6 +149,8 @@ def load():
         L.imi_sparse_attention_noalloc.argtypes = [ctypes.POINTER(AttnDesc), P]
         L.imi_decode_attend.argtypes = [ctypes.POINTER(SelectDesc), ctypes.POINTER(AttnDesc),
                                         ctypes.POINTER(ApplyDesc), P]
+        L.imi_merge_candidates.argtypes = [ctypes.POINTER(MergeDesc), P]
+        L.imi_combine_partials.argtypes = [ctypes.POINTER(CombineDesc), P]
         L.imi_decode_layer.argtypes = [ctypes.POINTER(AppendDesc), ctypes.POINTER(AsyncDesc),
                                        ctypes.POINTER(ApplyDesc), ctypes.POINTER(SelectDesc),
                                        ctypes.POINTER(AttnDesc), P]

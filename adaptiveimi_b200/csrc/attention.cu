@@ -353,7 +353,13 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
         }
 #pragma unroll
         for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
-        if (lane == 0) sL[warp] = L;
+        if (lane == 0) {
+            sL[warp] = L;
+            if (a.ml_part) {  // sequence sharding: the group's (max, sum) for the cross-shard combine
+                a.ml_part[((size_t)h * a.G + warp) * 2 + 0] = M;
+                a.ml_part[((size_t)h * a.G + warp) * 2 + 1] = L;
+            }
+        }
     }
     __syncthreads();
     const int cols = a.G * 32;  // float4 columns of the [G][128] output
@@ -385,13 +391,17 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             acc.z += v.z;
             acc.w += v.w;
         }
-        const float L = sL[gg];
-        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-        uint2 packed;
-        packed.x = pack_bf16(acc.x * inv, acc.y * inv);
-        packed.y = pack_bf16(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + ((size_t)h * a.G + gg) * 128 + 4 * d4) =
-            packed;
+        if (a.o_part)  // sequence sharding: unnormalised, combined across shards later
+            *reinterpret_cast<float4*>(a.o_part + ((size_t)h * a.G + gg) * 128 + 4 * d4) = acc;
+        if (a.out) {
+            const float L = sL[gg];
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            uint2 packed;
+            packed.x = pack_bf16(acc.x * inv, acc.y * inv);
+            packed.y = pack_bf16(acc.z * inv, acc.w * inv);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + ((size_t)h * a.G + gg) * 128 +
+                                      4 * d4) = packed;
+        }
     }
     if (threadIdx.x == 0) a.counters[h] = 0;
 }
@@ -414,6 +424,43 @@ __global__ void imi_combine_kernel(AttnArgs a) {
         const float r = L > 0.0f ? acc / L : 0.0f;
         reinterpret_cast<__nv_bfloat16*>(a.out)[((size_t)h * a.G + gg) * 128 + d] = __float2bfloat16_rn(r);
     }
+}
+
+// Sequence sharding: log-sum-exp combine of the shards' partials, one CTA per
+// group, one thread per float4 column of the [G][128] output.
+__global__ void imi_combine_shards_kernel(const __grid_constant__ CombineArgs a) {
+    const int h = blockIdx.x;
+    const int col = threadIdx.x;
+    if (col >= a.G * 32) return;
+    const int gg = col >> 5, d4 = col & 31;
+    float M = -INFINITY;
+    const size_t ps = a.part_stride ? (size_t)a.part_stride : (size_t)a.bg * a.G * 128;
+    const size_t ms = a.part_stride ? (size_t)a.part_stride : (size_t)a.bg * a.G * 2;
+    for (int s = 0; s < a.shards; ++s) M = fmaxf(M, a.ml_parts[s * ms + ((size_t)h * a.G + gg) * 2]);
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float L = 0.0f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < a.shards; ++s) {
+            const size_t pg = (size_t)h * a.G + gg;
+            const float f = exp2f(a.ml_parts[s * ms + pg * 2] - M);
+            const float4 v = reinterpret_cast<const float4*>(a.o_parts + s * ps + pg * 128)[d4];
+            acc.x += v.x * f;
+            acc.y += v.y * f;
+            acc.z += v.z * f;
+            acc.w += v.w * f;
+            L += a.ml_parts[s * ms + pg * 2 + 1] * f;
+        }
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    uint2 packed;
+    packed.x = pack_bf16(acc.x * inv, acc.y * inv);
+    packed.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + ((size_t)h * a.G + gg) * 128 + 4 * d4) = packed;
+}
+
+cudaError_t launch_combine_shards(const CombineArgs& a, cudaStream_t st) {
+    imi_combine_shards_kernel<<<a.bg, a.G * 32, 0, st>>>(a);
+    return cudaGetLastError();
 }
 
 size_t attn_smem_bytes(const AttnArgs& a) {

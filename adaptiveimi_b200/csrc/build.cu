@@ -393,7 +393,10 @@ __global__ void inertia_kernel(Dev b, int it, int max_iters, int min_iter, float
     float inertia = 0.0f;
     if (eval) {
         const float* md = b.md + (size_t)t * b.n;
+        // sequential sum in sample order; float4 loads only from a 16-byte
+        // boundary (the task's base offset t * n is not one when n is odd)
         int i = 0;
+        for (; i < b.n && (reinterpret_cast<uintptr_t>(md + i) & 15) != 0; ++i) inertia = __fadd_rn(inertia, md[i]);
         for (; i + 4 <= b.n; i += 4) {
             const float4 v = *reinterpret_cast<const float4*>(md + i);
             inertia = __fadd_rn(inertia, v.x);
@@ -537,7 +540,6 @@ __global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix
     const int t = blockIdx.x;
     if (b.done[t]) return;
     const int k = b.ks[task_s(b, t)];
-    __shared__ int red[32];
     __shared__ int carry_c, carry_e;
     if (threadIdx.x == 0) {
         carry_c = 0;
@@ -600,7 +602,6 @@ __global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix
         __syncthreads();
     }
     if (threadIdx.x == 0) b.offs[(size_t)t * (b.kst + 1) + k] = carry_c;
-    (void)red;
 }
 
 // centroid[c][d] = (sum over members in sample order) * (1 / size); empty cells

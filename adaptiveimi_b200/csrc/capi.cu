@@ -92,9 +92,11 @@ static int check_select(const imi_select_desc* d) {
     if (d->bg <= 0 || d->G <= 0 || d->n_slots <= 0 || d->nprobe <= 0 || d->page_size <= 0)
         return fail(IMI_ERR_INVALID, "imi_select_cells: bad sizes");
     if (!d->q || !d->cell_code || !d->cell_sizes || !d->cell_offsets || !d->cell_mask || !d->centroids ||
-        !d->sub_centroids || !d->sel_cells || !d->sel_count || !d->row_index || !d->row_count)
+        !d->sub_centroids || !d->sel_cells || !d->sel_count || (!d->row_index != !d->row_count))
         return fail(IMI_ERR_INVALID, "imi_select_cells: null pointer in descriptor");
     if (d->nprobe > 2048) return fail(IMI_ERR_INVALID, "imi_select_cells: nprobe > 2048 is not supported");
+    if (d->key_base < 0 || (int64_t)d->key_base + d->n_slots > 0x7fffffffLL)
+        return fail(IMI_ERR_INVALID, "imi_select_cells: key_base + n_slots must fit in 31 bits");
     if (d->static_len < 0 || d->static_len + (int64_t)d->buffer_pages * d->page_size > d->exec_capacity)
         return fail(IMI_ERR_INVALID, "imi_select_cells: exec_capacity < static_len + buffer_pages*page_size");
     long long table = 1;
@@ -120,8 +122,12 @@ static int check_attention(const imi_attn_desc* d) {
     if (d->bg <= 0 || d->G <= 0 || d->G > 8 || d->splits <= 0 || d->splits > 4096)
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: need 1 <= G <= 8 and 1 <= splits <= 4096");
     if (!d->q || !d->row_index || !d->row_count || !d->list_keys || !d->list_values || !d->static_keys ||
-        !d->static_values || !d->part_o || !d->part_ml || !d->out)
+        !d->static_values || !d->part_o || !d->part_ml || (!d->out && !d->o_part))
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: null pointer in descriptor");
+    if ((d->o_part || d->ml_part) && (!d->o_part || !d->ml_part || !d->counters || !aligned16(d->o_part) ||
+                                      (reinterpret_cast<uintptr_t>(d->ml_part) & 7u) != 0))
+        return fail(IMI_ERR_INVALID,
+                    "imi_sparse_attention: o_part and ml_part go together, need counters, and must be 16/8-byte aligned");
     if (!aligned16(d->list_keys) || !aligned16(d->list_values) || !aligned16(d->static_keys) ||
         !aligned16(d->static_values) || !aligned16(d->q))
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: K/V/q buffers must be 16-byte aligned");
@@ -232,6 +238,30 @@ int imi_decode_layer(const imi_append_desc* app, const imi_async_desc* as, const
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_layer(async assignment)");
     }
     return launch_decode_attend(sel, attn, apply, stream);
+}
+
+int imi_merge_candidates(const imi_merge_desc* d, void* stream) {
+    if (!d || !d->cand || !d->cell_offsets || !d->sel_cells || !d->sel_count ||
+        !d->row_index || !d->row_count)
+        return fail(IMI_ERR_INVALID, "imi_merge_candidates: null pointer");
+    if (d->bg <= 0 || d->shards <= 0 || d->cap <= 0 || d->rank < 0 || d->rank >= d->shards || d->n_slots <= 0 ||
+        d->nprobe <= 0 || d->nprobe > 2048 || d->page_size <= 0 || d->static_len < 0 || d->key_base < 0)
+        return fail(IMI_ERR_INVALID, "imi_merge_candidates: bad sizes");
+    if (d->cap > 2049) return fail(IMI_ERR_INVALID, "imi_merge_candidates: cap (nprobe + 1) > 2049");
+    if (d->static_len + (int64_t)d->buffer_pages * d->page_size > d->exec_capacity)
+        return fail(IMI_ERR_INVALID, "imi_merge_candidates: exec_capacity < static_len + buffer_pages*page_size");
+    if (imi::merge_smem_bytes(*d) > 227 * 1024)
+        return fail(IMI_ERR_INVALID, "imi_merge_candidates: shards * cap too large for one CTA's shared memory");
+    return cuda_status(imi::launch_merge(*d, S(stream)), "imi_merge_candidates");
+}
+
+int imi_combine_partials(const imi_combine_desc* d, void* stream) {
+    if (!d || !d->o_parts || !d->ml_parts || !d->out) return fail(IMI_ERR_INVALID, "imi_combine_partials: null pointer");
+    if (d->shards <= 0 || d->bg <= 0 || d->G <= 0 || d->G > 8)
+        return fail(IMI_ERR_INVALID, "imi_combine_partials: need shards, bg > 0 and 1 <= G <= 8");
+    if (!aligned16(d->o_parts) || (d->part_stride % 4) != 0 || (reinterpret_cast<uintptr_t>(d->out) & 7u) != 0)
+        return fail(IMI_ERR_INVALID, "imi_combine_partials: o_parts 16-byte, out 8-byte aligned");
+    return cuda_status(imi::launch_combine_shards(*d, S(stream)), "imi_combine_partials");
 }
 
 int imi_decode_append(const imi_append_desc* d, void* stream) {

@@ -18,6 +18,8 @@ using AppendArgs = imi_append_desc;
 using AsyncArgs = imi_async_desc;
 using ApplyArgs = imi_apply_desc;
 using BuildArgs = imi_build_desc;
+using MergeArgs = imi_merge_desc;
+using CombineArgs = imi_combine_desc;
 
 cudaError_t launch_similarity(const uint16_t* q, const float* cent, float* out, int bg, int G, int n_cells, int dim,
                               long long out_stride, cudaStream_t st);
@@ -26,6 +28,9 @@ int select_max_slots();
 cudaError_t launch_select(const SelectArgs& a, cudaStream_t st);
 size_t attn_smem_bytes(const AttnArgs& a);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+size_t merge_smem_bytes(const MergeArgs& a);
+cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
+cudaError_t launch_combine_shards(const CombineArgs& a, cudaStream_t st);
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t st);
 size_t async_smem_bytes(const AsyncArgs& a);
 cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st);

@@ -708,7 +708,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
                         s = __fmaf_rn(qs[d + 3], v.w, s);
                     }
                 }
-                key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)c);
+                key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)(a.key_base + c));
                 kmn = min(kmn, key);
                 kmx = max(kmx, key);
             }
@@ -780,18 +780,37 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const int w0 = wid * R, w1 = min(ne, w0 + R);
     {
         int wsel = 0, wkept = 0;
+        unsigned long long nx = 0ull;  // highest-ranked candidate left out (the stop marker)
         for (int base = w0; base < w1; base += 32) {
             const int c = base + lid;
             const unsigned long long k = c < w1 ? skey[c] : 0ull;
             wsel += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrA));
             wkept += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrB));
+            if (k != 0ull && k <= thrA) nx = max(nx, k);
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) nx = max(nx, (unsigned long long)__shfl_xor_sync(0xffffffffu, nx, o));
         if (lid == 0) {
             sm.wsel[wid] = wsel;
             sm.wkept[wid] = wkept;
+            sm.rscr[0][wid] = nx;
         }
     }
     __syncthreads();
+    if (tid == 0 && a.cand_out) {  // the stop marker after the selected cells, then the count
+        unsigned long long nx = 0ull;
+        for (int q = 0; q < SL_WARPS; ++q) nx = max(nx, sm.rscr[0][q]);
+        int ns = 0;
+        for (int q = 0; q < SL_WARPS; ++q) ns += sm.wsel[q];
+        ns = min(ns, a.nprobe);
+        unsigned long long* rec = a.cand_out + hs * (2 * (size_t)(a.nprobe + 1) + 1);
+        if (nx) {
+            const int slot = (int)(0xffffffffu - (uint32_t)nx) - a.key_base;
+            rec[ns] = nx;
+            rec[a.nprobe + 1 + ns] = (unsigned long long)ssz[slot];
+        }
+        rec[2 * (a.nprobe + 1)] = (unsigned long long)(ns + (nx ? 1 : 0));
+    }
     int sel_base = 0, nsel = 0, nkept = 0;
     for (int q = 0; q < SL_WARPS; ++q) {
         const int ws = sm.wsel[q];
@@ -809,7 +828,14 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             const unsigned fm = __ballot_sync(0xffffffffu, fin);
             if (fin) {
                 const int my = si + __popc(fm & lt);
-                if (my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = c;
+                if (my < a.nprobe) {
+                    a.sel_cells[hs * a.nprobe + my] = c;
+                    if (a.cand_out) {
+                        unsigned long long* rec = a.cand_out + hs * (2 * (size_t)(a.nprobe + 1) + 1);
+                        rec[my] = k;
+                        rec[a.nprobe + 1 + my] = (unsigned long long)ssz[c];
+                    }
+                }
                 if (my < SL_SEL_MAX) sel_slot[my] = c;
             }
             si += __popc(fm);
@@ -817,6 +843,13 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     }
     __syncthreads();
     SL_STAMP(4);
+    if (a.row_index == nullptr) {  // candidates only (the sharded merge writes the rows)
+        if (tid == 0) {
+            a.sel_count[h] = min(nsel, a.nprobe);
+            if (a.kept_count) a.kept_count[h] = nkept;
+        }
+        return;
+    }
     // row offsets of the selected cells (slot order) by one block scan;
     // thread t owns entries 4t .. 4t+3
     const int ns = min(nsel, SL_SEL_MAX);
@@ -889,6 +922,151 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         a.row_count[h] = total;
         if (a.kept_count) a.kept_count[h] = nkept;
     }
+}
+
+// ---------------------------------------------------------------------------
+// Sequence sharding: the global selection over every shard's candidates.
+// One CTA per group.  The candidates (keys carry global cell ids, so every
+// shard orders them alike) are loaded into shared memory, the two boundaries
+// are found exactly as in the per-shard selection, and this shard's cells
+// above boundary A become its selected cells and its row list.  A shard's
+// part of the global selection is a prefix of its own order, so its local
+// selection under the global rules plus its stop marker cover it.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_constant__ MergeArgs a) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
+    const int h = blockIdx.x;
+    const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
+    const size_t hs = h;
+    const int ne = a.shards * a.cap;
+    const int npad = (ne + 1) & ~1;
+    unsigned char* p = dyn + ((sizeof(SelHdr) + 15) & ~size_t(15));
+    unsigned long long* skey = reinterpret_cast<unsigned long long*>(p);
+    p += sizeof(unsigned long long) * npad;
+    int* ssz = reinterpret_cast<int*>(p);
+    p += sizeof(int) * npad;
+    int* sel_slot = reinterpret_cast<int*>(p);
+    int* sel_start = sel_slot + SL_SEL_MAX;
+    int* sel_off = sel_start + SL_SEL_MAX;
+    SelRules rules;
+    rules.nprobe = a.nprobe;
+    rules.max_tokens = a.max_tokens;
+    rules.buffer_pages = a.buffer_pages;
+    rules.page_size = a.page_size;
+    rules.pg_shift = __ffs(a.page_size) - 1;
+    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
+
+    const size_t rec_len = 2 * (size_t)a.cap + 1;
+    unsigned long long kmn = ~0ull, kmx = 0ull;
+    for (int e = tid; e < ne; e += SL_THREADS) {
+        const int s = e / a.cap, j = e - s * a.cap;
+        const unsigned long long* rec = a.cand + ((size_t)s * a.bg + hs) * rec_len;
+        const bool valid = j < (int)rec[2 * a.cap];
+        const unsigned long long k = valid ? rec[j] : 0ull;
+        skey[e] = k;
+        ssz[e] = valid && k ? (int)rec[a.cap + j] : 0;
+        if (k) {
+            kmn = min(kmn, k);
+            kmx = max(kmx, k);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmn = min(kmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmn, o));
+        kmx = max(kmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    if (lid == 0) {
+        sm.rscr[0][wid] = kmn;
+        sm.rscr[1][wid] = kmx;
+    }
+    __syncthreads();
+    unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
+    for (int q = 0; q < SL_WARPS; ++q) {
+        key_lo0 = min(key_lo0, sm.rscr[0][q]);
+        key_hi0 = max(key_hi0, sm.rscr[1][q]);
+    }
+    __syncthreads();
+    unsigned long long thrA = ~0ull;
+    if (key_hi0 != 0ull) {
+        if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
+            thrA = sm.T;
+        } else {
+            search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
+            thrA = sm.T;
+        }
+        __syncthreads();
+    }
+
+    // this shard's candidates sit in slot order at [rank * cap, rank * cap + count)
+    const int base = a.rank * a.cap;
+    const int cnt = (int)a.cand[((size_t)a.rank * a.bg + hs) * rec_len + 2 * a.cap];
+    const int per = (cnt + SL_THREADS - 1) / SL_THREADS;  // contiguous entries per thread (<= 5)
+    const int e0 = min(cnt, tid * per), e1 = min(cnt, e0 + per);
+    unsigned int nloc = 0, sloc = 0;
+    for (int e = e0; e < e1; ++e) {
+        const unsigned long long k = skey[base + e];
+        if (k != 0ull && k > thrA) {
+            ++nloc;
+            sloc += (unsigned)ssz[base + e];
+        }
+    }
+    unsigned long long ix = nloc;
+    unsigned int iy = sloc;
+    sl_scan_pair(ix, iy, sm);
+    if (tid == SL_THREADS - 1) {
+        sm.wsel[0] = (int)ix;
+        sm.wkept[0] = (int)iy;
+    }
+    const int32_t* offs = a.cell_offsets + hs * (a.n_slots + 1);
+    {
+        int my = (int)(ix - nloc);
+        int run = a.static_len + (int)(iy - sloc);
+        for (int e = e0; e < e1; ++e) {
+            const unsigned long long k = skey[base + e];
+            if (k != 0ull && k > thrA) {
+                const int slot = (int)(0xffffffffu - (uint32_t)k) - a.key_base;
+                if (my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = slot;
+                if (my < SL_SEL_MAX) {
+                    sel_slot[my] = slot;
+                    sel_start[my] = run;
+                    sel_off[my] = offs[slot];
+                }
+                ++my;
+                run += ssz[base + e];
+            }
+        }
+    }
+    __syncthreads();
+    const int ntot = sm.wsel[0], rows_sel = sm.wkept[0];
+    int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
+    for (int r = tid; r < a.static_len; r += SL_THREADS) rows[r] = (1 << 30) | r;
+    const int ns = min(ntot, SL_SEL_MAX);
+    for (int i = wid; i < ns; i += SL_WARPS) {
+        const int s0 = sel_start[i], off = sel_off[i];
+        const int sz = (i + 1 < ns ? sel_start[i + 1] : a.static_len + rows_sel) - s0;
+        for (int jj = lid; jj < sz; jj += 32)
+            if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
+    }
+    if (tid == 0) {
+        a.sel_count[h] = min(ntot, a.nprobe);
+        a.row_count[h] = min(a.static_len + rows_sel, a.exec_capacity);
+    }
+}
+
+size_t merge_smem_bytes(const MergeArgs& a) {
+    const size_t ne = (size_t)a.shards * a.cap;
+    const size_t npad = (ne + 1) & ~size_t(1);
+    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + 3 * (size_t)SL_SEL_MAX * sizeof(int) + 16;
+}
+
+cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {
+    const size_t sm = merge_smem_bytes(a);
+    static int smem_set[64] = {};
+    cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_merge_kernel), sm, smem_set, 64);
+    if (e != cudaSuccess) return e;
+    imi_merge_kernel<<<a.bg, SL_THREADS, sm, st>>>(a);
+    return cudaGetLastError();
 }
 
 size_t select_smem_bytes(const SelectArgs& a) {

@@ -125,6 +125,14 @@ typedef struct imi_select_desc {
     int32_t slot_bound;                    /* 0, or a bound on the occupied slots: every slot at or
                                               above it is masked (padding) in every group, e.g. the
                                               largest n_active of the build; the kernel skips them */
+    int32_t key_base;                      /* 0, or this shard's global cell-id offset: ties between
+                                              equal scores go to the lower key_base + slot */
+    unsigned long long* cand_out;          /* [bg, 2 * (nprobe + 1) + 1] out or NULL: this shard's
+                                              candidates for imi_merge_candidates -- ranking keys
+                                              (ordered score bits, then ~(key_base + slot)) of the
+                                              selected cells in slot order, then the stop marker (the
+                                              highest-ranked cell left out, if any); their sizes from
+                                              offset nprobe + 1; the entry count last */
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
@@ -151,7 +159,43 @@ typedef struct imi_attn_desc {
                                               separate merge kernel runs */
     int32_t* status;                       /* [1] or NULL: bit 0 is set when a wait for a row
                                               copy gave up (the output is then not valid) */
+    float* o_part;                         /* [bg, G, 128] out or NULL: unnormalised output (sequence
+                                              sharding); needs counters */
+    float* ml_part;                        /* [bg, G, 2] out or NULL: (max in log2 units, sum) */
 } imi_attn_desc;
+
+/* Sequence sharding: the global selection over every shard's candidates.
+ * Each shard ran imi_select_cells under the global rules with key_base = its
+ * global cell-id offset and row_index = NULL; its candidates are its selected
+ * cells (slot order) followed by its stop marker (next_key).  Every shard runs
+ * this merge on the same all-gathered candidates, so every shard finds the same
+ * boundary; it then writes its own selected cells and row list. */
+typedef struct imi_merge_desc {
+    int32_t bg, shards, cap;               /* cap = nprobe + 1 (the select's candidate slots) */
+    int32_t rank;                          /* this shard */
+    int32_t key_base;                      /* this shard's global cell-id offset */
+    const unsigned long long* cand;        /* [shards, bg, 2 * cap + 1]: every shard's cand_out */
+    const int32_t* cell_offsets;           /* this shard's [bg, n_slots + 1] */
+    int32_t n_slots;                       /* this shard's slots */
+    int32_t nprobe, max_tokens, buffer_pages, page_size;  /* the global rules */
+    int32_t static_len;                    /* steady-zone rows this shard attends (0 on all but one) */
+    int32_t exec_capacity;
+    int32_t* sel_cells;                    /* [bg, nprobe] out: this shard's selected slots, ascending */
+    int32_t* sel_count;                    /* [bg] out */
+    int32_t* row_index;                    /* [bg, exec_capacity] out */
+    int32_t* row_count;                    /* [bg] out */
+} imi_merge_desc;
+
+/* Sequence sharding: combine the shards' unnormalised attention partials
+ * (imi_attn_desc o_part / ml_part) by log-sum-exp into the bf16 output. */
+typedef struct imi_combine_desc {
+    int32_t shards, bg, G;
+    int64_t part_stride;                   /* floats from one shard's partials to the next */
+    const float* o_parts;                  /* shard s: [bg, G, 128] at o_parts + s * part_stride */
+    const float* ml_parts;                 /* shard s: [bg, G, 2] at ml_parts + s * part_stride:
+                                              (max in log2 units, sum) */
+    void* out;                             /* [bg, G, 128] bf16 */
+} imi_combine_desc;
 
 typedef struct imi_append_desc {
     int32_t bg, dim;
@@ -236,6 +280,10 @@ IMI_API int imi_decode_layer(const imi_append_desc* append, const imi_async_desc
                              const imi_apply_desc* apply, const imi_select_desc* sel, const imi_attn_desc* attn,
                              void* stream);
 IMI_API int imi_decode_append(const imi_append_desc* desc, void* stream);
+/* Sequence sharding (no counterpart in the reference: its cache is one GPU):
+ * the global candidate merge and the partial combine. */
+IMI_API int imi_merge_candidates(const imi_merge_desc* desc, void* stream);
+IMI_API int imi_combine_partials(const imi_combine_desc* desc, void* stream);
 IMI_API int imi_async_assign(const imi_async_desc* desc, void* stream);
 IMI_API int imi_apply_updates(const imi_apply_desc* desc, void* stream);
 

@@ -94,6 +94,17 @@ def test_build_imi4_and_ivf_against_oracle():
         _check_build_against_oracle(k, v, idx, parts, ks, it, 5e-4, 2, 5e-4)
 
 
+def test_build_odd_token_count_against_oracle():
+    """An odd token count: per-task arrays then start off 16-byte boundaries
+    (the early-stop inertia sum reads them with vector loads)."""
+    K, V, _ = make_layer(3, 12, 2800, 128, 40, 11, 500000.0, n_queries=1)
+    k, v = K[:, :2699].contiguous(), V[:, :2699].contiguous()
+    for parts, ks, it, mi in ((2, (24, 21), 8, 2), (4, (3, 4, 3, 2), 5, 5)):
+        n_slots = int(np.prod(ks)) + 1
+        idx = _gpu_build(k, v, parts, ks, it, n_slots, 5e-4, mi, 5e-4)
+        _check_build_against_oracle(k, v, idx, parts, ks, it, 5e-4, mi, 5e-4)
+
+
 def test_build_strided_model_layout():
     """Keys taken straight from a [T, H, D] prefill tensor (no transpose copy)."""
     K, V, _ = make_layer(4, 16, 3000, 128, 32, 9, 500000.0)
