@@ -63,6 +63,13 @@ struct Dev {
     uint8_t* used;         // [heads][G]
     int32_t* g2c;          // [heads][G]
     int G;
+    // tensor-core E-step: centroids split into bf16 hi + lo halves in the
+    // K-major core-matrix layout, their squared norms, and the padded count
+    uint16_t* chi;         // [T][npad][sub]
+    uint16_t* clo;         // [T][npad][sub]
+    float* cn;             // [T][npad]
+    int npad;              // centroids rounded up to 16 (0 when the tensor-core E-step is not used)
+    int32_t* status;       // [1] or null
 };
 
 IMI_DEV int task_h(const Dev& b, int t) { return t / b.S; }
@@ -422,6 +429,319 @@ __global__ void inertia_kernel(Dev b, int it, int max_iters, int min_iter, float
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core E-step (tcgen05 MMA into TMEM) with an exact recheck.
+//
+// The reference's labels come from exact fp32 distances in its 8-lane order.
+// Here a 128-sample tile meets every centroid on the tensor cores and TMEM
+// receives an approximate d~(x, c) = ||c||^2 - 2 x.c: the samples are bf16
+// (exact), extended by a [1, 1] column pair; the centroids go in as -2c split
+// into bf16 hi + lo halves, extended by ||c||^2 split the same way; fp32
+// accumulation.  The splits leave under 2^-18 relative of each term, the fp32
+// accumulation of the exact products under 2^-16 of sum |x_i c_i|, and the
+// exact routine's own rounding under 2^-19 of the distance, so every centroid
+// with d~ within 2^-11 (||x||^2 + max ||c||^2) of the minimum d~ is
+// recomputed with the exact 8-lane routine and the exact minimum wins (the
+// lowest index on ties): labels and minimum distances are those of the exact
+// E-step.  Usually the second-smallest d~ is outside that band and only the
+// approximate winner is recomputed.
+//
+// Operands sit in shared memory in the K-major, no-swizzle core-matrix
+// layout: 8 rows x 16 bytes per core matrix, core matrices 128 B apart along
+// K, 8-row groups KC*16 B apart (KC = SUB + 16 columns).  Sample tiles are
+// double-buffered: the next tile's rows stream in (cp.async) during the
+// current tile's MMAs and epilogue.
+// ---------------------------------------------------------------------------
+constexpr int TC_M = 128;                 // samples per tile = TMEM lanes
+constexpr int TC_THREADS = 128;           // warp w owns TMEM lanes 32w .. 32w+31
+constexpr int TC_WAIT_LIMIT = 1 << 20;    // polls of the MMA-done barrier before giving up
+constexpr float TC_PAD_NORM = 3.0e38f;    // ||c||^2 of a padding row: never the minimum, still finite
+
+template <int KC>
+IMI_DEV int core_off(int r, int d) {
+    return (r >> 3) * (KC * 8) + (d >> 3) * 64 + (r & 7) * 8 + (d & 7);
+}
+
+IMI_DEV uint32_t tc_smem(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// shared-memory matrix descriptor: start address, leading / stride byte
+// offsets (16-byte units), descriptor version 1 (sm_100), no swizzle
+IMI_DEV uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+IMI_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+IMI_DEV bool tc_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+IMI_DEV bool tc_wait(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < TC_WAIT_LIMIT; ++i)
+        if (tc_try_wait(bar, parity)) return true;
+    return false;
+}
+
+IMI_DEV void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+IMI_DEV uint16_t bf16_bits_rn(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+
+// centroid c of task t -> B rows of the two MMA chains (core-matrix layout,
+// KC = SUB + 16 columns): hi row = [bf16(-2c), hi(||c||^2), lo(||c||^2), 0..],
+// lo row = [bf16(-2c - hi), 0..]; padding rows carry only a huge norm
+template <int SUB>
+__global__ void cent_split_kernel(Dev b) {
+    constexpr int KC = SUB + 16;
+    const int t = blockIdx.y, c = blockIdx.x;
+    if (b.done[t]) return;
+    const int k = b.ks[task_s(b, t)];
+    const float* src = b.cent + ((size_t)t * b.kmax + c) * SUB;
+    uint16_t* hi = b.chi + (size_t)t * b.npad * KC;
+    uint16_t* lo = b.clo + (size_t)t * b.npad * KC;
+    float sq = 0.0f;
+    for (int d = threadIdx.x; d < SUB; d += 32) {
+        const float v = c < k ? src[d] : 0.0f;
+        const float m2 = -2.0f * v;  // exact (power of two)
+        const uint16_t h = bf16_bits_rn(m2);
+        hi[core_off<KC>(c, d)] = h;
+        lo[core_off<KC>(c, d)] = bf16_bits_rn(m2 - bf16_bits_to_f32(h));
+        sq = fmaf(v, v, sq);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (threadIdx.x < 16) {
+        const float nrm = c < k ? sq : TC_PAD_NORM;
+        const uint16_t nh = bf16_bits_rn(nrm);
+        const uint16_t nl = bf16_bits_rn(nrm - bf16_bits_to_f32(nh));
+        const int d = SUB + threadIdx.x;
+        hi[core_off<KC>(c, d)] = threadIdx.x == 0 ? nh : (threadIdx.x == 1 ? nl : (uint16_t)0);
+        lo[core_off<KC>(c, d)] = 0;
+        if (threadIdx.x == 0) b.cn[(size_t)t * b.npad + c] = c < k ? sq : 0.0f;
+    }
+}
+
+template <int SUB>
+__global__ void __launch_bounds__(TC_THREADS) estep_tc_kernel(Dev b, int tiles_per_cta, int ncols) {
+    constexpr int KC = SUB + 16;        // K columns of the hi chain (the lo chain uses the first SUB)
+    constexpr int CPR = SUB / 8;        // 16-byte chunks per sample row
+    constexpr int CFLD = SUB + 4;       // row stride of the exact centroids (breaks bank conflicts)
+    const int t = blockIdx.y;
+    if (b.done[t]) return;  // the whole CTA, before any TMEM is allocated
+    extern __shared__ __align__(1024) unsigned char tsm[];
+    const int k = b.ks[task_s(b, t)], npad = b.npad;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    uint16_t* As0 = reinterpret_cast<uint16_t*>(tsm);  // two [TC_M][KC] sample tiles
+    uint16_t* As1 = As0 + TC_M * KC;
+    uint16_t* Bh = As1 + TC_M * KC;                    // [npad][KC]
+    uint16_t* Bl = Bh + npad * KC;
+    float* cf = reinterpret_cast<float*>(Bl + npad * KC);  // [k][CFLD] exact centroids
+    unsigned long long* mbar = reinterpret_cast<unsigned long long*>(cf + (size_t)npad * CFLD);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_smem(tslot)),
+                     "r"(ncols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    const int ntiles = (b.n + TC_M - 1) / TC_M;
+    const int tile0 = blockIdx.x * tiles_per_cta, tile1 = min(ntiles, tile0 + tiles_per_cta);
+    // the sample rows of a tile into a buffer: thread tid takes chunks tid, tid + 128, ...;
+    // 8..16 consecutive threads cover one row (coalesced); rows past n are zero
+    auto load_tile = [&](int tile, uint16_t* dst) {
+#pragma unroll
+        for (int q = 0; q < CPR; ++q) {
+            const int e = tid + TC_THREADS * q;
+            const int r = e / CPR, j = e - r * CPR;
+            const int i = tile * TC_M + r;
+            const uint16_t* src = sample_ptr(b, t, i < b.n ? i : 0) + 8 * j;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(tc_smem(dst + core_off<KC>(r, 8 * j))),
+                         "l"(src), "r"(i < b.n ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (tile0 < tile1) load_tile(tile0, As0);
+    {  // the constant [1, 1, 0, ..] columns of both sample buffers
+        const int r = tid;
+        for (int d = SUB; d < KC; ++d) {
+            const uint16_t v = d < SUB + 2 ? (uint16_t)0x3F80u : (uint16_t)0;  // bf16 1.0
+            As0[core_off<KC>(r, d)] = v;
+            As1[core_off<KC>(r, d)] = v;
+        }
+    }
+    {  // this task's B rows (both chains) and the exact centroids
+        const uint4* sh = reinterpret_cast<const uint4*>(b.chi + (size_t)t * npad * KC);
+        const uint4* sl = reinterpret_cast<const uint4*>(b.clo + (size_t)t * npad * KC);
+        uint4* dh = reinterpret_cast<uint4*>(Bh);
+        uint4* dl = reinterpret_cast<uint4*>(Bl);
+        for (int e = tid; e < npad * KC / 8; e += TC_THREADS) {
+            dh[e] = sh[e];
+            dl[e] = sl[e];
+        }
+        const float* sc = b.cent + (size_t)t * b.kmax * SUB;
+        for (int e = tid; e < k * SUB / 4; e += TC_THREADS) {
+            const int c = e / (SUB / 4), q = e - c * (SUB / 4);
+            *reinterpret_cast<float4*>(cf + c * CFLD + 4 * q) = *reinterpret_cast<const float4*>(sc + 4 * e);
+        }
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_smem(mbar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    float cmax = 0.0f;  // max ||c||^2 of the task's centroids (the band's scale)
+    for (int c = 0; c < k; ++c) cmax = fmaxf(cmax, __ldg(b.cn + (size_t)t * npad + c));
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tslot;
+
+    // instruction descriptor: fp32 accumulator, bf16 A and B, both K-major,
+    // N = npad, M = 128
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(npad >> 3) << 17) |
+                           ((uint32_t)(TC_M >> 4) << 24);
+    const uint32_t bh0 = tc_smem(Bh), bl0 = tc_smem(Bl);
+    constexpr uint32_t LBO = 128, SBO = KC * 16;
+    const uint32_t bar = tc_smem(mbar);
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+    uint32_t phase = 0;
+    int failed = 0;
+    for (int tile = tile0; tile < tile1; ++tile) {
+        uint16_t* As = ((tile - tile0) & 1) ? As1 : As0;
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t a0 = tc_smem(As);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+            for (int kk = 0; kk < KC / 16; ++kk)
+                umma_bf16(tmem, umma_desc(a0 + kk * 2 * LBO, LBO, SBO), umma_desc(bh0 + kk * 2 * LBO, LBO, SBO), idesc,
+                          kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < SUB / 16; ++kk)
+                umma_bf16(tmem, umma_desc(a0 + kk * 2 * LBO, LBO, SBO), umma_desc(bl0 + kk * 2 * LBO, LBO, SBO), idesc,
+                          1u);
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                         : "memory");
+        }
+        if (tile + 1 < tile1) load_tile(tile + 1, As == As0 ? As1 : As0);  // overlaps the MMAs and the epilogue
+        const bool ok = tc_wait(bar, phase);
+        if (__syncthreads_or(!ok)) {
+            failed = 1;
+            break;
+        }
+        phase ^= 1u;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // epilogue: sample row tid of the tile
+        float m1 = INFINITY, m2 = INFINITY;
+        int i1 = 0;
+        for (int c0 = 0; c0 < npad; c0 += 16) {
+            uint32_t r[16];
+            tc_ld16(taddr + (uint32_t)c0, r);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float v = __uint_as_float(r[j]);
+                if (v < m1) {
+                    m2 = m1;
+                    m1 = v;
+                    i1 = c0 + j;
+                } else if (v < m2) {
+                    m2 = v;
+                }
+            }
+        }
+        float x[SUB];
+#pragma unroll
+        for (int j = 0; j < CPR; ++j) {
+            const uint4 v = *reinterpret_cast<const uint4*>(As + core_off<KC>(tid, 8 * j));
+            x[8 * j + 0] = bf16lo(v.x);
+            x[8 * j + 1] = bf16hi(v.x);
+            x[8 * j + 2] = bf16lo(v.y);
+            x[8 * j + 3] = bf16hi(v.y);
+            x[8 * j + 4] = bf16lo(v.z);
+            x[8 * j + 5] = bf16hi(v.z);
+            x[8 * j + 6] = bf16lo(v.w);
+            x[8 * j + 7] = bf16hi(v.w);
+        }
+        float xn = 0.0f;
+#pragma unroll
+        for (int d = 0; d < SUB; ++d) xn = fmaf(x[d], x[d], xn);
+        const float band = ldexpf(xn + cmax, -11);
+        float best;
+        int bi;
+        const bool single = m2 > m1 + band;  // one candidate: the approximate winner
+        if (single) {
+            bi = i1;
+            best = dist_lanes8<SUB>(x, cf + i1 * CFLD);
+        } else {
+            best = FLT_MAX;
+            bi = 0;
+        }
+        // several within the band: recompute them all, in index order; the
+        // TMEM loads are warp-wide, so the whole warp walks the chunks when
+        // any lane needs them
+        if (__any_sync(0xffffffffu, !single)) {
+            const float thr = single ? -INFINITY : m1 + band;
+            for (int c0 = 0; c0 < npad; c0 += 16) {
+                uint32_t r[16];
+                tc_ld16(taddr + (uint32_t)c0, r);
+                unsigned cand = 0u;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (c0 + j < k && __uint_as_float(r[j]) <= thr) cand |= 1u << j;
+                while (cand) {
+                    const int c = c0 + __ffs(cand) - 1;
+                    cand &= cand - 1u;
+                    const float dd = dist_lanes8<SUB>(x, cf + c * CFLD);
+                    if (dd < best) {
+                        best = dd;
+                        bi = c;
+                    }
+                }
+            }
+        }
+        const int i = tile * TC_M + tid;
+        if (i < b.n) {
+            b.labels[(size_t)t * b.n + i] = bi;
+            b.md[(size_t)t * b.n + i] = best;
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();  // TMEM and this sample buffer are free again
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (failed) {
+        // report, then let the MMAs in flight finish (bounded) before TMEM goes
+        if (tid == 0 && b.status) atomicOr(b.status, 1);
+        (void)tc_wait(bar, phase);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Stable counting sort by an 8-bit digit (one LSD radix pass).
 //   key(t, i) = (keys[t*key_tstride + i] >> shift) & 255
 //   element at position p is perm_in[t][p] (or p when perm_in is null)
@@ -606,34 +926,79 @@ __global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix
 
 // centroid[c][d] = (sum over members in sample order) * (1 / size); empty cells
 // take the iteration's next reseed draw (kmeans_core.cpp:268-311).
-__global__ void __launch_bounds__(BT) msum_kernel(Dev b, int it, const int32_t* perm) {
+// One warp per cell: lane l owns the bf16 pair l of the row (dims 2l, 2l+1;
+// also pair l+32 when sub = 128; lanes 16..31 idle when sub = 32).  The member
+// list is read 32 indices at a time (one coalesced load, broadcast by
+// shuffle) and all 32 members' rows are requested before the adds, so each
+// warp keeps 32 row loads in flight; every dim's sum is still one chain of
+// fp32 adds in sample order.
+constexpr int MS_WARPS = 8;
+template <int SUB>
+__global__ void __launch_bounds__(MS_WARPS * 32) msum_kernel(Dev b, int it, const int32_t* perm) {
+    constexpr int NPAIR = SUB / 2;       // bf16 pairs per subvector (16, 32 or 64)
+    constexpr bool TWO = NPAIR > 32;     // sub = 128: each lane owns pairs l and l + 32
     const int t = blockIdx.y;
     if (b.done[t]) return;
     const int k = b.ks[task_s(b, t)];
-    const int e = blockIdx.x * BT + threadIdx.x;
-    const int c = e / b.sub, d = e - c * b.sub;
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.x * MS_WARPS + (threadIdx.x >> 5);
     if (c >= k) return;
+    const bool live = NPAIR >= 32 || lane < NPAIR;
     const int cnt = b.counts[(size_t)t * b.kst + c];
-    float* out = b.cent + ((size_t)t * b.kmax + c) * b.sub + d;
+    float* out = b.cent + ((size_t)t * b.kmax + c) * SUB;
+    // this lane's first pair of sample 0; sample i is tstride elements further
+    const unsigned char* base = reinterpret_cast<const unsigned char*>(sample_ptr(b, t, 0)) + 4 * lane;
+    const long long tbytes = 2 * b.tstride;
     if (cnt > 0) {
-        const int off = b.offs[(size_t)t * (b.kst + 1) + c];
-        const int32_t* pm = perm + (size_t)t * b.n + off;
-        float s = 0.0f;
-        int m = 0;
-        for (; m + 8 <= cnt; m += 8) {
-            float v[8];
+        const int32_t* pm = perm + (size_t)t * b.n + b.offs[(size_t)t * (b.kst + 1) + c];
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        for (int m0 = 0; m0 < cnt; m0 += 32) {
+            const int nb = min(32, cnt - m0);
+            const int mine = lane < nb ? __ldg(pm + m0 + lane) : 0;
+            uint32_t v[32], w[32];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) v[q] = bf16_bits_to_f32(sample_ptr(b, t, pm[m + q])[d]);
+            for (int j = 0; j < 32; ++j) {
+                const unsigned char* row = base + (long long)__shfl_sync(0xffffffffu, mine, j) * tbytes;
+                v[j] = live ? __ldg(reinterpret_cast<const uint32_t*>(row)) : 0u;
+                w[j] = TWO ? __ldg(reinterpret_cast<const uint32_t*>(row + 128)) : 0u;
+            }
+            if (nb == 32) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) s = __fadd_rn(s, v[q]);
+                for (int j = 0; j < 32; ++j) {
+                    s0 = __fadd_rn(s0, bf16lo(v[j]));
+                    s1 = __fadd_rn(s1, bf16hi(v[j]));
+                    if (TWO) {
+                        s2 = __fadd_rn(s2, bf16lo(w[j]));
+                        s3 = __fadd_rn(s3, bf16hi(w[j]));
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (j < nb) {
+                        s0 = __fadd_rn(s0, bf16lo(v[j]));
+                        s1 = __fadd_rn(s1, bf16hi(v[j]));
+                        if (TWO) {
+                            s2 = __fadd_rn(s2, bf16lo(w[j]));
+                            s3 = __fadd_rn(s3, bf16hi(w[j]));
+                        }
+                    }
+                }
+            }
         }
-        for (; m < cnt; ++m) s = __fadd_rn(s, bf16_bits_to_f32(sample_ptr(b, t, pm[m])[d]));
         const float inv = __fdiv_rn(1.0f, (float)cnt);
-        *out = __fmul_rn(s, inv);
+        if (live) {
+            out[2 * lane] = __fmul_rn(s0, inv);
+            out[2 * lane + 1] = __fmul_rn(s1, inv);
+            if (TWO) {
+                out[64 + 2 * lane] = __fmul_rn(s2, inv);
+                out[65 + 2 * lane] = __fmul_rn(s3, inv);
+            }
+        }
     } else {
         const int r = b.erank[(size_t)t * b.kst + c];
-        const int i = b.reseed[(size_t)it * b.kst + r];
-        *out = bf16_bits_to_f32(sample_ptr(b, t, i)[d]);
+        const uint16_t* row = sample_ptr(b, t, b.reseed[(size_t)it * b.kst + r]);
+        for (int d = lane; d < SUB; d += 32) out[d] = bf16_bits_to_f32(row[d]);
     }
 }
 
@@ -767,8 +1132,13 @@ namespace {
 
 struct Layout {
     size_t labels, md, perm_a, perm_b, part_lo, part_hi, part_minl, part_bad, hist, dig_off, dig_tot, counts, offs,
-        erank, draws_u, first, reseed, done, prev, iters, used, g2c, total;
+        erank, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, total;
+    int npad;
 };
+
+// centroids per task rounded up to the MMA's N granularity; 0 when k > 256
+// (the tensor-core E-step then is not used)
+int tc_npad(int kmax) { return kmax <= 256 ? ((kmax + 15) / 16) * 16 : 0; }
 
 Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters, bool own_labels) {
     const int S = parts == 0 ? 1 : parts;
@@ -809,6 +1179,11 @@ Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters
     L.iters = take((size_t)T * 4);
     L.used = take((size_t)heads * G);
     L.g2c = take((size_t)heads * G * 4);
+    L.npad = tc_npad(kmax);
+    const size_t sub = (size_t)dim / S;
+    L.chi = take((size_t)T * L.npad * (sub + 16) * 2);
+    L.clo = take((size_t)T * L.npad * (sub + 16) * 2);
+    L.cn = take((size_t)T * L.npad * 4);
     L.total = o;
     return L;
 }
@@ -843,8 +1218,32 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
         cudaSuccess)
         return e;
     const int two_pass = kmax_all > 256;
+    // tensor-core E-step when every task's k fits one MMA (N <= 256)
+    const bool tc = d.npad > 0;
+    int tc_ncols = 32, tc_ctas = 1, tc_tiles = 1;
+    size_t tc_smem_bytes = 0;
+    if (tc) {
+        while (tc_ncols < d.npad) tc_ncols <<= 1;
+        const size_t need = 2 * (size_t)TC_M * (SUB + 16) * 2 + 2 * (size_t)d.npad * (SUB + 16) * 2 +
+                            (size_t)d.npad * (SUB + 4) * 4 + 16 + 1024;
+        // at most 512 / ncols resident CTAs per SM, so their TMEM always fits
+        const size_t cap = 232448 / (512 / tc_ncols) - 3072;
+        tc_smem_bytes = std::max(need, std::min(cap, (size_t)232448));
+        if ((e = cudaFuncSetAttribute(estep_tc_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)tc_smem_bytes)) != cudaSuccess)
+            return e;
+        const int ntiles = (d.n + TC_M - 1) / TC_M;
+        tc_ctas = std::max(1, std::min(ntiles, (148 * (512 / tc_ncols) + d.T - 1) / d.T));
+        tc_tiles = (ntiles + tc_ctas - 1) / tc_ctas;
+        tc_ctas = (ntiles + tc_tiles - 1) / tc_tiles;
+    }
     for (int it = 0; it < a.max_iters; ++it) {
-        estep_kernel<SUB><<<dim3((d.n + BT - 1) / BT, d.T), BT, es_smem, st>>>(d);
+        if (tc) {
+            cent_split_kernel<SUB><<<dim3(d.npad, d.T), 32, 0, st>>>(d);
+            estep_tc_kernel<SUB><<<dim3(tc_ctas, d.T), TC_THREADS, tc_smem_bytes, st>>>(d, tc_tiles, tc_ncols);
+        } else {
+            estep_kernel<SUB><<<dim3((d.n + BT - 1) / BT, d.T), BT, es_smem, st>>>(d);
+        }
         const int eval = it >= std::max(0, a.early_stop_min_iter - 2) ? 1 : 0;
         inertia_kernel<<<d.T, 32, 0, st>>>(d, it, a.max_iters, a.early_stop_min_iter, a.tol, a.early_stop_rel_tol,
                                             eval);
@@ -877,7 +1276,7 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
             label_count_kernel<<<dim3(std::min(d.NB, 64), d.T), BT, 0, st>>>(d);
         }
         cell_prefix_kernel<<<d.T, 1024, 0, st>>>(d, two_pass ? 0 : 1);
-        msum_kernel<<<dim3((kmax_all * d.sub + BT - 1) / BT, d.T), BT, 0, st>>>(d, it, perm);
+        msum_kernel<SUB><<<dim3((kmax_all + MS_WARPS - 1) / MS_WARPS, d.T), MS_WARPS * 32, 0, st>>>(d, it, perm);
     }
     return cudaGetLastError();
 }
@@ -968,6 +1367,11 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
     d.iters_run = reinterpret_cast<int32_t*>(ws + L.iters);
     d.used = ws + L.used;
     d.g2c = reinterpret_cast<int32_t*>(ws + L.g2c);
+    d.npad = L.npad;
+    d.chi = reinterpret_cast<uint16_t*>(ws + L.chi);
+    d.clo = reinterpret_cast<uint16_t*>(ws + L.clo);
+    d.cn = reinterpret_cast<float*>(ws + L.cn);
+    d.status = a.status;
     d.G = (int)G;
     // per-cell work arrays use stride d.kst (max k); sub-centroids use a.kmax
     // ---- host draws (the reference's seeds, the same <random> algorithms)

@@ -85,7 +85,7 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
                 max_iters: int = 25, tol: float = 5e-4, early_stop_min_iter: int = 5,
                 early_stop_rel_tol: float = 5e-4, list_keys: Optional[torch.Tensor] = None,
                 list_values: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-                kmax: Optional[int] = None) -> IMIIndex:
+                kmax: Optional[int] = None, status: Optional[torch.Tensor] = None) -> IMIIndex:
     """Build the IMI of one layer on the device.
 
     keys / values: [heads, n, D] bf16 CUDA views whose last dim is contiguous
@@ -136,6 +136,7 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
                  "sub_labels", "n_active", "iters_run"):
         setattr(d, name, out[name].data_ptr())
     d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    d.status = status.data_ptr() if status is not None else None
     L = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(L.imi_build_index(ctypes.byref(d), _stream(dev)), "imi_build_index")

@@ -95,6 +95,8 @@ typedef struct imi_build_desc {
     int32_t* iters_run;                    /* [heads, S] Lloyd iterations entered, or NULL */
     void* workspace;
     size_t workspace_bytes;
+    int32_t* status;                       /* [1] or NULL: bit 0 is set when a wait of the tensor-core
+                                              E-step gave up (the labels are then not valid) */
 } imi_build_desc;
 
 typedef struct imi_select_desc {

@@ -32,9 +32,12 @@ def _build_cfg0(heads=8, ctx=8192, G=4, seed=0, parts=2, ks=(16, 16), iters=10, 
 
 def _gpu_build(k, v, parts, ks, iters, n_slots, tol=0.0, min_iter=None, rel_tol=0.0):
     kd, vd = k.cuda(), v.cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
     idx = ops.build_index(kd, vd, parts=parts, ks=ks, n_slots=n_slots, max_iters=iters, tol=tol,
-                          early_stop_min_iter=iters if min_iter is None else min_iter, early_stop_rel_tol=rel_tol)
+                          early_stop_min_iter=iters if min_iter is None else min_iter, early_stop_rel_tol=rel_tol,
+                          status=status)
     torch.cuda.synchronize()
+    assert int(status) == 0  # no wait of the tensor-core E-step gave up
     return idx
 
 
