@@ -185,32 +185,77 @@ __global__ void kpp_first_kernel(Dev b) {
         b.cent[(size_t)t * b.kmax * b.sub + d] = bf16_bits_to_f32(x[d]);
 }
 
+// Distances of every sample to the newest centroid; min with the running
+// min-distance; the block's exact Q64.64 sum.  The sample rows are staged in
+// shared memory 256 at a time by coalesced 16-byte cp.async (8-16 threads per
+// row), double-buffered, so the pass streams at DRAM speed; each thread then
+// reads its own row (a 16-byte pad per row keeps those reads conflict-free).
 template <int SUB>
 __global__ void __launch_bounds__(BT) kpp_update_kernel(Dev b, int c) {
+    constexpr int CPR = SUB / 8;    // 16-byte chunks per row
+    constexpr int PITCH = SUB + 8;  // bf16 per staged row
     const int t = blockIdx.y;
     if (c >= b.ks[task_s(b, t)]) return;
+    extern __shared__ __align__(16) uint16_t kst[];  // [2][BT][PITCH]
     __shared__ __align__(16) float cp[SUB];
     __shared__ unsigned long long rlo[BT / 32], rhi[BT / 32];
     __shared__ int rl[BT / 32], rb[BT / 32];
+    const int base = blockIdx.x * SPB;
+    auto stage = [&](int j, int buf) {
+#pragma unroll
+        for (int q = 0; q < CPR; ++q) {
+            const int e = threadIdx.x + BT * q;
+            const int r = e / CPR, ch = e - r * CPR;
+            const int i = base + j * BT + r;
+            const uint16_t* src = sample_ptr(b, t, i < b.n ? i : 0) + 8 * ch;
+            const uint32_t dst =
+                static_cast<uint32_t>(__cvta_generic_to_shared(kst + ((size_t)buf * BT + r) * PITCH + 8 * ch));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(i < b.n ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0, 0);
     const float* cprev = b.cent + ((size_t)t * b.kmax + (c - 1)) * SUB;
     for (int d = threadIdx.x; d < SUB; d += BT) cp[d] = cprev[d];
-    __syncthreads();
     u128 acc{0ull, 0ull};
     int minl = INT_MAX, bad = 0;
     float* md = b.md + (size_t)t * b.n;
-#pragma unroll 1
-    for (int j = 0; j < SPB / BT; ++j) {
-        const int i = blockIdx.x * SPB + j * BT + threadIdx.x;
-        if (i >= b.n) break;
-        float x[SUB];
-        load_sample<SUB>(b, t, i, x);
-        const float d = dist_lanes8<SUB>(x, cp);
-        const float prev = (c == 1) ? FLT_MAX : md[i];
-        const float m = (d < prev) ? d : prev;
-        md[i] = m;
-        int l;
-        acc = u128_add(acc, to_units(m, l, bad));
-        minl = min(minl, l);
+    constexpr int NIT = SPB / BT;
+    for (int j = 0; j < NIT; ++j) {
+        if (j + 1 < NIT && base + (j + 1) * BT < b.n) {
+            stage(j + 1, (j + 1) & 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int i = base + j * BT + threadIdx.x;
+        if (i < b.n) {
+            float x[SUB];
+            const uint4* row = reinterpret_cast<const uint4*>(kst + ((size_t)(j & 1) * BT + threadIdx.x) * PITCH);
+#pragma unroll
+            for (int q = 0; q < CPR; ++q) {
+                const uint4 v = row[q];
+                x[8 * q + 0] = bf16lo(v.x);
+                x[8 * q + 1] = bf16hi(v.x);
+                x[8 * q + 2] = bf16lo(v.y);
+                x[8 * q + 3] = bf16hi(v.y);
+                x[8 * q + 4] = bf16lo(v.z);
+                x[8 * q + 5] = bf16hi(v.z);
+                x[8 * q + 6] = bf16lo(v.w);
+                x[8 * q + 7] = bf16hi(v.w);
+            }
+            const float d = dist_lanes8<SUB>(x, cp);
+            const float prev = (c == 1) ? FLT_MAX : md[i];
+            const float m = (d < prev) ? d : prev;
+            md[i] = m;
+            int l;
+            acc = u128_add(acc, to_units(m, l, bad));
+            minl = min(minl, l);
+        }
+        __syncthreads();  // this buffer is refilled two iterations on
+        if (base + (j + 1) * BT >= b.n) break;
     }
     // block reduce
     for (int o = 16; o > 0; o >>= 1) {
@@ -245,6 +290,11 @@ __global__ void __launch_bounds__(BT) kpp_update_kernel(Dev b, int c) {
     }
 }
 
+template <int SUB>
+size_t kpp_update_smem() {
+    return (size_t)2 * BT * (SUB + 8) * 2;
+}
+
 // One CTA (1024 threads) per task: exact total, target, first crossing index.
 __global__ void __launch_bounds__(1024) kpp_pick_kernel(Dev b, int c) {
     const int t = blockIdx.x;
@@ -257,24 +307,71 @@ __global__ void __launch_bounds__(1024) kpp_pick_kernel(Dev b, int c) {
     __shared__ unsigned long long s_tlo, s_thi;
     __shared__ unsigned long long wlo[32], whi[32];
     const int tid = threadIdx.x;
-    if (tid == 0) {
-        // sequential inclusive prefix over the block partials (NB is small)
-        u128 run{0ull, 0ull};
+    {   // inclusive prefix of the block partials (one per thread, in chunks of 1024),
+        // their minimum lsb and any unrepresentable value
+        const int lane = tid & 31, w = tid >> 5;
+        u128 carry{0ull, 0ull};
         int ml = INT_MAX, bb = 0;
-        for (int q = 0; q < b.NB; ++q) {
-            const size_t o = (size_t)t * b.NB + q;
-            run = u128_add(run, u128{b.part_lo[o], b.part_hi[o]});
-            plo[q] = run.lo;
-            phi[q] = run.hi;
-            ml = min(ml, b.part_minl[o]);
-            bb |= b.part_bad[o];
+        for (int q0 = 0; q0 < b.NB; q0 += 1024) {
+            const int q = q0 + tid;
+            u128 v{0ull, 0ull};
+            if (q < b.NB) {
+                const size_t o = (size_t)t * b.NB + q;
+                v = u128{b.part_lo[o], b.part_hi[o]};
+                ml = min(ml, b.part_minl[o]);
+                bb |= b.part_bad[o];
+            }
+            u128 x = v;
+            for (int o = 1; o < 32; o <<= 1) {
+                u128 y = u128_shfl_up(x, o);
+                if (lane >= o) x = u128_add(x, y);
+            }
+            if (lane == 31) {
+                wlo[w] = x.lo;
+                whi[w] = x.hi;
+            }
+            __syncthreads();
+            if (w == 0) {
+                u128 y{wlo[lane], whi[lane]};
+                for (int o = 1; o < 32; o <<= 1) {
+                    u128 z = u128_shfl_up(y, o);
+                    if (lane >= o) y = u128_add(y, z);
+                }
+                wlo[lane] = y.lo;
+                whi[lane] = y.hi;
+            }
+            __syncthreads();
+            if (w > 0) x = u128_add(x, u128{wlo[w - 1], whi[w - 1]});
+            x = u128_add(x, carry);
+            if (q < b.NB) {
+                plo[q] = x.lo;
+                phi[q] = x.hi;
+            }
+            carry = u128_add(carry, u128{wlo[31], whi[31]});
+            __syncthreads();
         }
-        s_minl = ml;
-        s_bad = bb;
-        s_sel = -1;
-        s_blk = -1;
-        s_tlo = run.lo;
-        s_thi = run.hi;
+        for (int o = 16; o > 0; o >>= 1) {
+            ml = min(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+            bb |= __shfl_xor_sync(0xffffffffu, bb, o);
+        }
+        if (lane == 0) {
+            wlo[w] = (unsigned long long)(unsigned)ml;
+            whi[w] = (unsigned long long)bb;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int m2 = INT_MAX, b2 = 0;
+            for (int q = 0; q < 32; ++q) {
+                m2 = min(m2, (int)(unsigned)wlo[q]);
+                b2 |= (int)whi[q];
+            }
+            s_minl = m2;
+            s_bad = b2;
+            s_sel = -1;
+            s_blk = -1;
+            s_tlo = carry.lo;
+            s_thi = carry.hi;
+        }
     }
     __syncthreads();
     const u128 total{s_tlo, s_thi};
@@ -303,16 +400,10 @@ __global__ void __launch_bounds__(1024) kpp_pick_kernel(Dev b, int c) {
         const double totd = u128_to_double_units(total);
         const double target = u * totd + 0.0;
         const u128 tgt = ceil_units(target);
-        if (tid == 0) {
-            int blk = b.NB - 1;
-            for (int q = 0; q < b.NB; ++q) {
-                if (u128_ge(u128{plo[q], phi[q]}, tgt)) {
-                    blk = q;
-                    break;
-                }
-            }
-            s_blk = blk;
-        }
+        if (tid == 0) s_blk = b.NB - 1;
+        __syncthreads();
+        for (int q = tid; q < b.NB; q += blockDim.x)
+            if (u128_ge(u128{plo[q], phi[q]}, tgt)) atomicMin(&s_blk, q);  // the first block reaching the target
         __syncthreads();
         const int blk = s_blk;
         u128 base{0ull, 0ull};
@@ -394,25 +485,63 @@ __global__ void __launch_bounds__(BT) estep_kernel(Dev b) {
 }
 
 // Sequential fp32 inertia and the early-stop test (kmeans_core.cpp:216-262).
-__global__ void inertia_kernel(Dev b, int it, int max_iters, int min_iter, float tol, float rel_tol, int eval) {
+// The sum is one chain in sample order (thread 0); the other threads stage
+// the next 4096 distances in shared memory meanwhile, so the chain never
+// waits on memory.
+constexpr int IN_THREADS = 256;
+constexpr int IN_CHUNK = 4096;
+__global__ void __launch_bounds__(IN_THREADS) inertia_kernel(Dev b, int it, int max_iters, int min_iter, float tol,
+                                                             float rel_tol, int eval) {
     const int t = blockIdx.x;
-    if (threadIdx.x != 0 || b.done[t]) return;
+    if (b.done[t]) return;
+    __shared__ __align__(16) float buf[2][IN_CHUNK];
     float inertia = 0.0f;
     if (eval) {
         const float* md = b.md + (size_t)t * b.n;
-        // sequential sum in sample order; float4 loads only from a 16-byte
-        // boundary (the task's base offset t * n is not one when n is odd)
-        int i = 0;
-        for (; i < b.n && (reinterpret_cast<uintptr_t>(md + i) & 15) != 0; ++i) inertia = __fadd_rn(inertia, md[i]);
-        for (; i + 4 <= b.n; i += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(md + i);
-            inertia = __fadd_rn(inertia, v.x);
-            inertia = __fadd_rn(inertia, v.y);
-            inertia = __fadd_rn(inertia, v.z);
-            inertia = __fadd_rn(inertia, v.w);
+        const int nch = (b.n + IN_CHUNK - 1) / IN_CHUNK;
+        auto stage = [&](int ch) {
+            const int i0 = ch * IN_CHUNK;
+            float* dst = buf[ch & 1];
+            for (int e = threadIdx.x; e < IN_CHUNK; e += IN_THREADS) {
+                const int i = i0 + e;
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(
+                                 static_cast<uint32_t>(__cvta_generic_to_shared(dst + e))),
+                             "l"(md + (i < b.n ? i : 0)), "r"(i < b.n ? 4 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        stage(0);
+        for (int ch = 0; ch < nch; ++ch) {
+            if (ch + 1 < nch) {
+                stage(ch + 1);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                const float* v = buf[ch & 1];
+                const int cnt = min(IN_CHUNK, b.n - ch * IN_CHUNK);
+                int e = 0;
+                for (; e + 8 <= cnt; e += 8) {
+                    const float4 a = *reinterpret_cast<const float4*>(v + e);
+                    const float4 c = *reinterpret_cast<const float4*>(v + e + 4);
+                    inertia = __fadd_rn(inertia, a.x);
+                    inertia = __fadd_rn(inertia, a.y);
+                    inertia = __fadd_rn(inertia, a.z);
+                    inertia = __fadd_rn(inertia, a.w);
+                    inertia = __fadd_rn(inertia, c.x);
+                    inertia = __fadd_rn(inertia, c.y);
+                    inertia = __fadd_rn(inertia, c.z);
+                    inertia = __fadd_rn(inertia, c.w);
+                }
+                for (; e < cnt; ++e) inertia = __fadd_rn(inertia, v[e]);
+            }
+            __syncthreads();  // this buffer is refilled two chunks on
         }
-        for (; i < b.n; ++i) inertia = __fadd_rn(inertia, md[i]);
     }
+    if (threadIdx.x != 0) return;
     const int iters = it + 1;
     if (eval) {
         const float prev = b.prev_inertia[t];
@@ -926,79 +1055,106 @@ __global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix
 
 // centroid[c][d] = (sum over members in sample order) * (1 / size); empty cells
 // take the iteration's next reseed draw (kmeans_core.cpp:268-311).
-// One warp per cell: lane l owns the bf16 pair l of the row (dims 2l, 2l+1;
-// also pair l+32 when sub = 128; lanes 16..31 idle when sub = 32).  The member
-// list is read 32 indices at a time (one coalesced load, broadcast by
-// shuffle) and all 32 members' rows are requested before the adds, so each
-// warp keeps 32 row loads in flight; every dim's sum is still one chain of
-// fp32 adds in sample order.
-constexpr int MS_WARPS = 8;
+// One CTA per (centroid, task).  Each dim's sum is one chain of fp32 adds in
+// sample order, so a cell's time is its member count times one add; the
+// member rows are gathered by all four warps with 16-byte cp.async into a
+// ring of MS_STAGES chunks (MS_CHUNK bf16 each), far enough ahead that warp 0,
+// which owns the chains (lane l: bf16 pairs l and, for sub 128, l + 32),
+// never waits on DRAM.
+constexpr int MS_THREADS = 128;
+constexpr int MS_STAGES = 4;
+constexpr int MS_CHUNK = 8192;  // bf16 per stage: 256 / 128 / 64 rows of sub 32 / 64 / 128
 template <int SUB>
-__global__ void __launch_bounds__(MS_WARPS * 32) msum_kernel(Dev b, int it, const int32_t* perm) {
+__global__ void __launch_bounds__(MS_THREADS) msum_kernel(Dev b, int it, const int32_t* perm) {
     constexpr int NPAIR = SUB / 2;       // bf16 pairs per subvector (16, 32 or 64)
     constexpr bool TWO = NPAIR > 32;     // sub = 128: each lane owns pairs l and l + 32
-    const int t = blockIdx.y;
+    constexpr int ROWS = MS_CHUNK / SUB; // rows per stage
+    constexpr int CPR = SUB / 8;         // 16-byte pieces per row
+    const int t = blockIdx.y, c = blockIdx.x;
     if (b.done[t]) return;
     const int k = b.ks[task_s(b, t)];
-    const int lane = threadIdx.x & 31;
-    const int c = blockIdx.x * MS_WARPS + (threadIdx.x >> 5);
     if (c >= k) return;
-    const bool live = NPAIR >= 32 || lane < NPAIR;
+    extern __shared__ __align__(16) uint16_t mring[];  // [MS_STAGES][ROWS][SUB]
+    const int tid = threadIdx.x, lane = tid & 31;
     const int cnt = b.counts[(size_t)t * b.kst + c];
     float* out = b.cent + ((size_t)t * b.kmax + c) * SUB;
-    // this lane's first pair of sample 0; sample i is tstride elements further
-    const unsigned char* base = reinterpret_cast<const unsigned char*>(sample_ptr(b, t, 0)) + 4 * lane;
-    const long long tbytes = 2 * b.tstride;
-    if (cnt > 0) {
-        const int32_t* pm = perm + (size_t)t * b.n + b.offs[(size_t)t * (b.kst + 1) + c];
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        for (int m0 = 0; m0 < cnt; m0 += 32) {
-            const int nb = min(32, cnt - m0);
-            const int mine = lane < nb ? __ldg(pm + m0 + lane) : 0;
-            uint32_t v[32], w[32];
+    if (cnt == 0) {
+        if (tid < 32) {
+            const int r = b.erank[(size_t)t * b.kst + c];
+            const uint16_t* row = sample_ptr(b, t, b.reseed[(size_t)it * b.kst + r]);
+            for (int d = lane; d < SUB; d += 32) out[d] = bf16_bits_to_f32(row[d]);
+        }
+        return;
+    }
+    const int32_t* pm = perm + (size_t)t * b.n + b.offs[(size_t)t * (b.kst + 1) + c];
+    const int nch = (cnt + ROWS - 1) / ROWS;
+    auto stage = [&](int ch) {
+        uint16_t* dst = mring + (size_t)(ch % MS_STAGES) * MS_CHUNK;
+        const int m0 = ch * ROWS;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const unsigned char* row = base + (long long)__shfl_sync(0xffffffffu, mine, j) * tbytes;
-                v[j] = live ? __ldg(reinterpret_cast<const uint32_t*>(row)) : 0u;
-                w[j] = TWO ? __ldg(reinterpret_cast<const uint32_t*>(row + 128)) : 0u;
-            }
-            if (nb == 32) {
+        for (int q = 0; q < ROWS * CPR / MS_THREADS; ++q) {
+            const int e = tid + MS_THREADS * q;
+            const int r = e / CPR, j = e - r * CPR;
+            const bool live = m0 + r < cnt;
+            const uint16_t* src = sample_ptr(b, t, live ? __ldg(pm + m0 + r) : 0) + 8 * j;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                             static_cast<uint32_t>(__cvta_generic_to_shared(dst + r * SUB + 8 * j))),
+                         "l"(src), "r"(live ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // MS_STAGES - 1 chunks ahead; empty groups keep the group count uniform
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    s0 = __fadd_rn(s0, bf16lo(v[j]));
-                    s1 = __fadd_rn(s1, bf16hi(v[j]));
+    for (int ch = 0; ch < MS_STAGES - 1; ++ch) {
+        if (ch < nch) stage(ch);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    const bool own = tid < 32 && (NPAIR >= 32 || lane < NPAIR);
+    for (int ch = 0; ch < nch; ++ch) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(MS_STAGES - 2) : "memory");
+        __syncthreads();  // chunk ch landed for every thread; chunk ch - 1's slot is free
+        if (ch + MS_STAGES - 1 < nch) stage(ch + MS_STAGES - 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        if (own) {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(mring + (size_t)(ch % MS_STAGES) * MS_CHUNK) + lane;
+            const int nb = min(ROWS, cnt - ch * ROWS);
+            if (nb == ROWS) {
+#pragma unroll 16
+                for (int r = 0; r < ROWS; ++r) {
+                    const uint32_t v = src[r * NPAIR];
+                    s0 = __fadd_rn(s0, bf16lo(v));
+                    s1 = __fadd_rn(s1, bf16hi(v));
                     if (TWO) {
-                        s2 = __fadd_rn(s2, bf16lo(w[j]));
-                        s3 = __fadd_rn(s3, bf16hi(w[j]));
+                        const uint32_t w = src[r * NPAIR + 32];
+                        s2 = __fadd_rn(s2, bf16lo(w));
+                        s3 = __fadd_rn(s3, bf16hi(w));
                     }
                 }
             } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (j < nb) {
-                        s0 = __fadd_rn(s0, bf16lo(v[j]));
-                        s1 = __fadd_rn(s1, bf16hi(v[j]));
-                        if (TWO) {
-                            s2 = __fadd_rn(s2, bf16lo(w[j]));
-                            s3 = __fadd_rn(s3, bf16hi(w[j]));
-                        }
+                for (int r = 0; r < nb; ++r) {
+                    const uint32_t v = src[r * NPAIR];
+                    s0 = __fadd_rn(s0, bf16lo(v));
+                    s1 = __fadd_rn(s1, bf16hi(v));
+                    if (TWO) {
+                        const uint32_t w = src[r * NPAIR + 32];
+                        s2 = __fadd_rn(s2, bf16lo(w));
+                        s3 = __fadd_rn(s3, bf16hi(w));
                     }
                 }
             }
         }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (own) {
         const float inv = __fdiv_rn(1.0f, (float)cnt);
-        if (live) {
-            out[2 * lane] = __fmul_rn(s0, inv);
-            out[2 * lane + 1] = __fmul_rn(s1, inv);
-            if (TWO) {
-                out[64 + 2 * lane] = __fmul_rn(s2, inv);
-                out[65 + 2 * lane] = __fmul_rn(s3, inv);
-            }
+        out[2 * lane] = __fmul_rn(s0, inv);
+        out[2 * lane + 1] = __fmul_rn(s1, inv);
+        if (TWO) {
+            out[64 + 2 * lane] = __fmul_rn(s2, inv);
+            out[65 + 2 * lane] = __fmul_rn(s3, inv);
         }
-    } else {
-        const int r = b.erank[(size_t)t * b.kst + c];
-        const uint16_t* row = sample_ptr(b, t, b.reseed[(size_t)it * b.kst + r]);
-        for (int d = lane; d < SUB; d += 32) out[d] = bf16_bits_to_f32(row[d]);
     }
 }
 
@@ -1206,8 +1362,12 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
     if ((e = cudaFuncSetAttribute(kpp_pick_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pick_smem)) !=
         cudaSuccess)
         return e;
+    const size_t upd_smem = kpp_update_smem<SUB>();
+    if ((e = cudaFuncSetAttribute(kpp_update_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)upd_smem)) != cudaSuccess)
+        return e;
     for (int c = 1; c < kmax_all; ++c) {
-        kpp_update_kernel<SUB><<<dim3(d.NB, d.T), BT, 0, st>>>(d, c);
+        kpp_update_kernel<SUB><<<dim3(d.NB, d.T), BT, upd_smem, st>>>(d, c);
         kpp_pick_kernel<<<d.T, 1024, pick_smem, st>>>(d, c);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1237,6 +1397,10 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
         tc_tiles = (ntiles + tc_ctas - 1) / tc_ctas;
         tc_ctas = (ntiles + tc_tiles - 1) / tc_tiles;
     }
+    const size_t ms_smem = (size_t)MS_STAGES * MS_CHUNK * 2;
+    if ((e = cudaFuncSetAttribute(msum_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ms_smem)) !=
+        cudaSuccess)
+        return e;
     for (int it = 0; it < a.max_iters; ++it) {
         if (tc) {
             cent_split_kernel<SUB><<<dim3(d.npad, d.T), 32, 0, st>>>(d);
@@ -1245,7 +1409,7 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
             estep_kernel<SUB><<<dim3((d.n + BT - 1) / BT, d.T), BT, es_smem, st>>>(d);
         }
         const int eval = it >= std::max(0, a.early_stop_min_iter - 2) ? 1 : 0;
-        inertia_kernel<<<d.T, 32, 0, st>>>(d, it, a.max_iters, a.early_stop_min_iter, a.tol, a.early_stop_rel_tol,
+        inertia_kernel<<<d.T, IN_THREADS, 0, st>>>(d, it, a.max_iters, a.early_stop_min_iter, a.tol, a.early_stop_rel_tol,
                                             eval);
         Radix r{};
         r.T = d.T;
@@ -1276,7 +1440,7 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
             label_count_kernel<<<dim3(std::min(d.NB, 64), d.T), BT, 0, st>>>(d);
         }
         cell_prefix_kernel<<<d.T, 1024, 0, st>>>(d, two_pass ? 0 : 1);
-        msum_kernel<SUB><<<dim3((kmax_all + MS_WARPS - 1) / MS_WARPS, d.T), MS_WARPS * 32, 0, st>>>(d, it, perm);
+        msum_kernel<SUB><<<dim3(kmax_all, d.T), MS_THREADS, ms_smem, st>>>(d, it, perm);
     }
     return cudaGetLastError();
 }
