@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "imi_internal.h"
 
+#include <cuda.h>
 #include <float.h>
 #include <limits.h>
 
@@ -68,6 +69,8 @@ struct Dev {
     uint16_t* chi;         // [T][npad][sub]
     uint16_t* clo;         // [T][npad][sub]
     float* cn;             // [T][npad]
+    float* xn;             // [T][nx] squared norms of the samples (the error band's scale)
+    int nx;                // n rounded up to a whole tile of 128
     int npad;              // centroids rounded up to 16 (0 when the tensor-core E-step is not used)
     int32_t* status;       // [1] or null
 };
@@ -571,17 +574,15 @@ __global__ void __launch_bounds__(IN_THREADS) inertia_kernel(Dev b, int it, int 
 // with d~ within 2^-11 (||x||^2 + max ||c||^2) of the minimum d~ is
 // recomputed with the exact 8-lane routine and the exact minimum wins (the
 // lowest index on ties): labels and minimum distances are those of the exact
-// E-step.  Usually the second-smallest d~ is outside that band and only the
-// approximate winner is recomputed.
+// E-step.  Usually only one centroid lies in that band: it is the winner, and
+// its exact distance is only needed when the inertia is evaluated.
 //
 // Operands sit in shared memory in the K-major, no-swizzle core-matrix
-// layout: 8 rows x 16 bytes per core matrix, core matrices 128 B apart along
-// K, 8-row groups KC*16 B apart (KC = SUB + 16 columns).  Sample tiles are
-// double-buffered: the next tile's rows stream in (cp.async) during the
-// current tile's MMAs and epilogue.
+// layout (8 rows x 16 bytes per core matrix).  Centroid rows: core matrices
+// 128 B apart along K, 8-row groups KC*16 B apart (KC = SUB + 16 columns).
+// Sample tiles: chunk-major as the TMA writes them (below).
 // ---------------------------------------------------------------------------
 constexpr int TC_M = 128;                 // samples per tile = TMEM lanes
-constexpr int TC_THREADS = 128;           // warp w owns TMEM lanes 32w .. 32w+31
 constexpr int TC_WAIT_LIMIT = 1 << 20;    // polls of the MMA-done barrier before giving up
 constexpr float TC_PAD_NORM = 3.0e38f;    // ||c||^2 of a padding row: never the minimum, still finite
 
@@ -633,6 +634,62 @@ IMI_DEV void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "memory");
 }
 
+IMI_DEV void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// minimum of W accumulator words (a tree, so the compares overlap)
+template <int W>
+IMI_DEV float tc_min(const uint32_t (&r)[W]) {
+    float v[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) v[j] = __uint_as_float(r[j]);
+#pragma unroll
+    for (int h = W / 2; h > 0; h >>= 1)
+#pragma unroll
+        for (int j = 0; j < h; ++j) v[j] = fminf(v[j], v[j + h]);
+    return v[0];
+}
+
+// bit j set where word j is at most thr
+template <int W>
+IMI_DEV uint32_t tc_le(const uint32_t (&r)[W], float thr) {
+    uint32_t m = 0u;
+#pragma unroll
+    for (int j = 0; j < W; ++j) m |= (__uint_as_float(r[j]) <= thr) ? (1u << j) : 0u;
+    return m;
+}
+
+// the low `live` bits (all 32 when live >= 32, none when live <= 0): the
+// columns below k; padding columns never win, even when the band is infinite
+IMI_DEV uint32_t col_mask(int live) { return live >= 32 ? 0xffffffffu : (live <= 0 ? 0u : (1u << live) - 1u); }
+
+// squared norm of every sample of every task (fp32; it only scales the error
+// band of the tensor-core E-step), rows padded to whole tiles
+template <int SUB>
+__global__ void __launch_bounds__(BT) xnorm_kernel(Dev b) {
+    const int t = blockIdx.y;
+    const int i = blockIdx.x * BT + threadIdx.x;
+    if (i >= b.nx) return;
+    float s = 0.0f;
+    if (i < b.n) {
+        float x[SUB];
+        load_sample<SUB>(b, t, i, x);
+#pragma unroll
+        for (int d = 0; d < SUB; ++d) s = fmaf(x[d], x[d], s);
+    }
+    b.xn[(size_t)t * b.nx + i] = s;
+}
+
 IMI_DEV uint16_t bf16_bits_rn(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 
 // centroid c of task t -> B rows of the two MMA chains (core-matrix layout,
@@ -669,205 +726,403 @@ __global__ void cent_split_kernel(Dev b) {
     }
 }
 
+// Lloyd E-step on the tensor cores, warp-specialised.  One CTA per SM walks
+// a run of 128-sample tiles of one task:
+//  * a control thread keeps up to `stages` tiles in flight with TMA (a 4-D
+//    tensor map over the keys writes each tile chunk-major: 16-byte column
+//    chunk c of row r at c * 2 KB + r * 16 B, the no-swizzle K-major
+//    core-matrix layout with LBO = 2 KB, SBO = 128 B) plus the tile's 128
+//    sample norms, and issues the hi, norm and lo MMA chains of tile j into
+//    TMEM accumulator j % 4 (npad fp32 columns, d~(c) = ||c||^2 - 2 x.c);
+//  * two groups of eight epilogue warps take alternate tiles; sample r (TMEM
+//    lane r) of a tile is shared by two warps of the group, each scanning one
+//    half of the columns: the minimum m1, then the centroids with
+//    d~ <= m1 + band, band = 2^-11 (||x||^2 + max ||c||^2) bounding the
+//    bf16-split error.  One centroid in that set is the exact first-min
+//    argmin; otherwise every centroid of the set is re-measured exactly and
+//    the lowest distance (then the lowest index) wins.  The exact distance of
+//    the winner is only computed for iterations whose inertia is evaluated.
+// Stages and accumulators are handed over with mbarriers (full / empty per
+// stage, full / empty per accumulator); every wait is bounded and a timeout
+// sets the status flag and drains the copies and MMAs in flight.
+constexpr int TC_MAX_STAGES = 8;
+constexpr int TC_GROUP = 256;                       // eight epilogue warps
+constexpr int TC_CTA_THREADS = 2 * TC_GROUP + 32;   // two groups and the control warp (17 warps: at most
+                                                    // 96 registers, five warps share one SM quarter)
+constexpr long long TC_SPIN_LIMIT = 1ll << 24;      // control polls without progress before giving up
+
+// element (r, d) of a staged sample tile (chunk-major, see above)
+IMI_DEV int a_off(int r, int d) { return (d >> 3) * (TC_M * 8) + r * 8 + (d & 7); }
+
+IMI_DEV void mb_init(uint32_t bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+IMI_DEV bool mb_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+IMI_DEV void mb_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+IMI_DEV void mb_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+IMI_DEV void group_sync(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(TC_GROUP) : "memory"); }
+IMI_DEV bool group_any(int id, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(TC_GROUP)
+        : "memory");
+    return r != 0;
+}
+
+// Exact squared distance between sample row `row` of a staged tile and an
+// fp32 centroid: the same eight-lane accumulation order as dist_lanes8.
 template <int SUB>
-__global__ void __launch_bounds__(TC_THREADS) estep_tc_kernel(Dev b, int tiles_per_cta, int ncols) {
-    constexpr int KC = SUB + 16;        // K columns of the hi chain (the lo chain uses the first SUB)
-    constexpr int CPR = SUB / 8;        // 16-byte chunks per sample row
-    constexpr int CFLD = SUB + 4;       // row stride of the exact centroids (breaks bank conflicts)
+IMI_DEV float dist_tile(const uint16_t* A, int row, const float* __restrict__ c) {
+    float lane[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) lane[l] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < SUB; i += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(A + a_off(row, i));
+        const float4 c0 = *reinterpret_cast<const float4*>(c + i);
+        const float4 c1 = *reinterpret_cast<const float4*>(c + i + 4);
+        float d;
+        d = __fsub_rn(bf16lo(v.x), c0.x); lane[0] = __fmaf_rn(d, d, lane[0]);
+        d = __fsub_rn(bf16hi(v.x), c0.y); lane[1] = __fmaf_rn(d, d, lane[1]);
+        d = __fsub_rn(bf16lo(v.y), c0.z); lane[2] = __fmaf_rn(d, d, lane[2]);
+        d = __fsub_rn(bf16hi(v.y), c0.w); lane[3] = __fmaf_rn(d, d, lane[3]);
+        d = __fsub_rn(bf16lo(v.z), c1.x); lane[4] = __fmaf_rn(d, d, lane[4]);
+        d = __fsub_rn(bf16hi(v.z), c1.y); lane[5] = __fmaf_rn(d, d, lane[5]);
+        d = __fsub_rn(bf16lo(v.w), c1.z); lane[6] = __fmaf_rn(d, d, lane[6]);
+        d = __fsub_rn(bf16hi(v.w), c1.w); lane[7] = __fmaf_rn(d, d, lane[7]);
+    }
+    float t = __fadd_rn(lane[0], lane[1]);
+#pragma unroll
+    for (int l = 2; l < 8; ++l) t = __fadd_rn(t, lane[l]);
+    return t;
+}
+
+template <int SUB>
+__global__ void __launch_bounds__(TC_CTA_THREADS, 1)
+    estep_tc_kernel(Dev b, const __grid_constant__ CUtensorMap tmap, int tiles_per_cta, int acc_cols, int stages,
+                    int want_md) {
+    constexpr int KC = SUB + 16;   // K columns of the hi chain of B (the lo chain uses the first SUB)
+    constexpr int CPR = SUB / 8;   // 16-byte chunks per sample row
+    constexpr int CFLD = SUB + 4;  // row stride of the exact centroids (spreads the banks)
     const int t = blockIdx.y;
     if (b.done[t]) return;  // the whole CTA, before any TMEM is allocated
-    extern __shared__ __align__(1024) unsigned char tsm[];
     const int k = b.ks[task_s(b, t)], npad = b.npad;
-    const int tid = threadIdx.x, warp = tid >> 5;
-    uint16_t* As0 = reinterpret_cast<uint16_t*>(tsm);  // two [TC_M][KC] sample tiles
-    uint16_t* As1 = As0 + TC_M * KC;
-    uint16_t* Bh = As1 + TC_M * KC;                    // [npad][KC]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ntiles = (b.n + TC_M - 1) / TC_M;
+    const int tile0 = blockIdx.x * tiles_per_cta;
+    const int nt = max(0, min(ntiles, tile0 + tiles_per_cta) - tile0);
+
+    extern __shared__ __align__(1024) unsigned char tsm[];
+    uint16_t* As = reinterpret_cast<uint16_t*>(tsm);  // [stages][CPR][TC_M][8] sample tiles
+    uint16_t* Ae = As + stages * TC_M * SUB;           // [TC_M][16] constant norm columns
+    uint16_t* Bh = Ae + TC_M * 16;                     // [npad][KC]
     uint16_t* Bl = Bh + npad * KC;
-    float* cf = reinterpret_cast<float*>(Bl + npad * KC);  // [k][CFLD] exact centroids
-    unsigned long long* mbar = reinterpret_cast<unsigned long long*>(cf + (size_t)npad * CFLD);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
+    float* xs = reinterpret_cast<float*>(Bl + npad * KC);  // [stages][TC_M] sample norms
+    unsigned long long* bars = reinterpret_cast<unsigned long long*>(xs + stages * TC_M);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 24);
+    float* cf = reinterpret_cast<float*>(bars + 64);   // [k][CFLD] exact centroids
+    const uint32_t full0 = tc_smem(bars), empty0 = tc_smem(bars + 8);
+    const uint32_t accf0 = tc_smem(bars + 16), acce0 = tc_smem(bars + 20);
+    __shared__ float xm[2][2][TC_M];  // per group and half: partial minimum, then partial exact best
+    __shared__ int xc[2][2][TC_M];    // per group and half: candidates in the band, then best index
+    __shared__ int xf[2][2][TC_M];    // per group and half: first candidate
+    __shared__ float red[TC_CTA_THREADS / 32];
+    __shared__ volatile int s_fail;
+    __shared__ int s_issued, s_mma;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_smem(tslot)),
-                     "r"(ncols)
+                     "r"(4 * acc_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    const int ntiles = (b.n + TC_M - 1) / TC_M;
-    const int tile0 = blockIdx.x * tiles_per_cta, tile1 = min(ntiles, tile0 + tiles_per_cta);
-    // the sample rows of a tile into a buffer: thread tid takes chunks tid, tid + 128, ...;
-    // 8..16 consecutive threads cover one row (coalesced); rows past n are zero
-    auto load_tile = [&](int tile, uint16_t* dst) {
-#pragma unroll
-        for (int q = 0; q < CPR; ++q) {
-            const int e = tid + TC_THREADS * q;
-            const int r = e / CPR, j = e - r * CPR;
-            const int i = tile * TC_M + r;
-            const uint16_t* src = sample_ptr(b, t, i < b.n ? i : 0) + 8 * j;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(tc_smem(dst + core_off<KC>(r, 8 * j))),
-                         "l"(src), "r"(i < b.n ? 16 : 0)
-                         : "memory");
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    if (tile0 < tile1) load_tile(tile0, As0);
-    {  // the constant [1, 1, 0, ..] columns of both sample buffers
-        const int r = tid;
-        for (int d = SUB; d < KC; ++d) {
-            const uint16_t v = d < SUB + 2 ? (uint16_t)0x3F80u : (uint16_t)0;  // bf16 1.0
-            As0[core_off<KC>(r, d)] = v;
-            As1[core_off<KC>(r, d)] = v;
-        }
-    }
-    {  // this task's B rows (both chains) and the exact centroids
+    for (int e = tid; e < TC_M * 16; e += TC_CTA_THREADS)  // bf16 1.0 in columns 0 and 1
+        Ae[core_off<16>(e >> 4, e & 15)] = (e & 15) < 2 ? (uint16_t)0x3F80u : (uint16_t)0;
+    {  // this task's B rows (both chains) and its exact centroids
         const uint4* sh = reinterpret_cast<const uint4*>(b.chi + (size_t)t * npad * KC);
         const uint4* sl = reinterpret_cast<const uint4*>(b.clo + (size_t)t * npad * KC);
         uint4* dh = reinterpret_cast<uint4*>(Bh);
         uint4* dl = reinterpret_cast<uint4*>(Bl);
-        for (int e = tid; e < npad * KC / 8; e += TC_THREADS) {
+        for (int e = tid; e < npad * KC / 8; e += TC_CTA_THREADS) {
             dh[e] = sh[e];
             dl[e] = sl[e];
         }
         const float* sc = b.cent + (size_t)t * b.kmax * SUB;
-        for (int e = tid; e < k * SUB / 4; e += TC_THREADS) {
+        for (int e = tid; e < k * SUB / 4; e += TC_CTA_THREADS) {
             const int c = e / (SUB / 4), q = e - c * (SUB / 4);
             *reinterpret_cast<float4*>(cf + c * CFLD + 4 * q) = *reinterpret_cast<const float4*>(sc + 4 * e);
         }
+        float cm = 0.0f;  // max ||c||^2 of the task's centroids (the band's scale)
+        for (int c = tid; c < k; c += TC_CTA_THREADS) cm = fmaxf(cm, __ldg(b.cn + (size_t)t * npad + c));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+        if (lane == 0) red[warp] = cm;
     }
     if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_smem(mbar)) : "memory");
+        for (int q = 0; q < stages; ++q) {
+            mb_init(full0 + 8 * q, 1);   // the control thread's expect_tx; the copies complete it
+            mb_init(empty0 + 8 * q, 2);  // the MMAs' commit and the epilogue group
+        }
+        for (int q = 0; q < 4; ++q) {
+            mb_init(accf0 + 8 * q, 1);   // the MMAs' commit
+            mb_init(acce0 + 8 * q, 1);   // the epilogue group
+        }
+        s_fail = 0;
+        s_issued = 0;
+        s_mma = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    float cmax = 0.0f;  // max ||c||^2 of the task's centroids (the band's scale)
-    for (int c = 0; c < k; ++c) cmax = fmaxf(cmax, __ldg(b.cn + (size_t)t * npad + c));
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes above -> MMA operand reads
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tslot;
+    float cmax = red[0];
+#pragma unroll
+    for (int w = 1; w < TC_CTA_THREADS / 32; ++w) cmax = fmaxf(cmax, red[w]);
 
-    // instruction descriptor: fp32 accumulator, bf16 A and B, both K-major,
-    // N = npad, M = 128
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(npad >> 3) << 17) |
-                           ((uint32_t)(TC_M >> 4) << 24);
-    const uint32_t bh0 = tc_smem(Bh), bl0 = tc_smem(Bl);
-    constexpr uint32_t LBO = 128, SBO = KC * 16;
-    const uint32_t bar = tc_smem(mbar);
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    uint32_t phase = 0;
-    int failed = 0;
-    for (int tile = tile0; tile < tile1; ++tile) {
-        uint16_t* As = ((tile - tile0) & 1) ? As1 : As0;
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            const uint32_t a0 = tc_smem(As);
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-            for (int kk = 0; kk < KC / 16; ++kk)
-                umma_bf16(tmem, umma_desc(a0 + kk * 2 * LBO, LBO, SBO), umma_desc(bh0 + kk * 2 * LBO, LBO, SBO), idesc,
-                          kk > 0 ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < SUB / 16; ++kk)
-                umma_bf16(tmem, umma_desc(a0 + kk * 2 * LBO, LBO, SBO), umma_desc(bl0 + kk * 2 * LBO, LBO, SBO), idesc,
-                          1u);
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                         : "memory");
-        }
-        if (tile + 1 < tile1) load_tile(tile + 1, As == As0 ? As1 : As0);  // overlaps the MMAs and the epilogue
-        const bool ok = tc_wait(bar, phase);
-        if (__syncthreads_or(!ok)) {
-            failed = 1;
-            break;
-        }
-        phase ^= 1u;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // epilogue: sample row tid of the tile
-        float m1 = INFINITY, m2 = INFINITY;
-        int i1 = 0;
-        for (int c0 = 0; c0 < npad; c0 += 16) {
-            uint32_t r[16];
-            tc_ld16(taddr + (uint32_t)c0, r);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float v = __uint_as_float(r[j]);
-                if (v < m1) {
-                    m2 = m1;
-                    m1 = v;
-                    i1 = c0 + j;
-                } else if (v < m2) {
-                    m2 = v;
-                }
-            }
-        }
-        float x[SUB];
-#pragma unroll
-        for (int j = 0; j < CPR; ++j) {
-            const uint4 v = *reinterpret_cast<const uint4*>(As + core_off<KC>(tid, 8 * j));
-            x[8 * j + 0] = bf16lo(v.x);
-            x[8 * j + 1] = bf16hi(v.x);
-            x[8 * j + 2] = bf16lo(v.y);
-            x[8 * j + 3] = bf16hi(v.y);
-            x[8 * j + 4] = bf16lo(v.z);
-            x[8 * j + 5] = bf16hi(v.z);
-            x[8 * j + 6] = bf16lo(v.w);
-            x[8 * j + 7] = bf16hi(v.w);
-        }
-        float xn = 0.0f;
-#pragma unroll
-        for (int d = 0; d < SUB; ++d) xn = fmaf(x[d], x[d], xn);
-        const float band = ldexpf(xn + cmax, -11);
-        float best;
-        int bi;
-        const bool single = m2 > m1 + band;  // one candidate: the approximate winner
-        if (single) {
-            bi = i1;
-            best = dist_lanes8<SUB>(x, cf + i1 * CFLD);
-        } else {
-            best = FLT_MAX;
-            bi = 0;
-        }
-        // several within the band: recompute them all, in index order; the
-        // TMEM loads are warp-wide, so the whole warp walks the chunks when
-        // any lane needs them
-        if (__any_sync(0xffffffffu, !single)) {
-            const float thr = single ? -INFINITY : m1 + band;
-            for (int c0 = 0; c0 < npad; c0 += 16) {
-                uint32_t r[16];
-                tc_ld16(taddr + (uint32_t)c0, r);
-                unsigned cand = 0u;
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    if (c0 + j < k && __uint_as_float(r[j]) <= thr) cand |= 1u << j;
-                while (cand) {
-                    const int c = c0 + __ffs(cand) - 1;
-                    cand &= cand - 1u;
-                    const float dd = dist_lanes8<SUB>(x, cf + c * CFLD);
-                    if (dd < best) {
-                        best = dd;
-                        bi = c;
+    if (warp == 2 * TC_GROUP / 32) {
+        // ---- control: TMA producer and MMA issuer (one thread)
+        if (lane == 0) {
+            // instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = npad, M = 128
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(npad >> 3) << 17) |
+                                   ((uint32_t)(TC_M >> 4) << 24);
+            const uint32_t bh0 = tc_smem(Bh), bl0 = tc_smem(Bl);
+            constexpr uint32_t LBO_A = TC_M * 16, SBO_A = 128, LBO_B = 128, SBO_B = KC * 16;
+            const uint64_t ext_desc = umma_desc(tc_smem(Ae), 128, 256);
+            const uint32_t stage_bytes = TC_M * SUB * 2;
+            const int h = task_h(b, t), s0 = task_s(b, t) * CPR;
+            const float* xn_t = b.xn + (size_t)t * b.nx;
+            int issued = 0, jm = 0;
+            long long idle = 0;
+            while (jm < nt) {
+                bool prog = false;
+                if (issued < nt && issued < jm + stages) {
+                    const int q = issued % stages;
+                    if (issued < stages || mb_test(empty0 + 8 * q, (uint32_t)((issued / stages) - 1) & 1u)) {
+                        const uint32_t fb = full0 + 8 * q;
+                        const int row0 = (tile0 + issued) * TC_M;
+                        mb_expect(fb, stage_bytes + TC_M * 4);
+                        asm volatile(
+                            "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                            "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(tc_smem(As + q * TC_M * SUB)),
+                            "l"(reinterpret_cast<uint64_t>(&tmap)), "r"(0), "r"(row0), "r"(s0), "r"(h), "r"(fb)
+                            : "memory");
+                        asm volatile(
+                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                tc_smem(xs + q * TC_M)),
+                            "l"(xn_t + row0), "r"(TC_M * 4), "r"(fb)
+                            : "memory");
+                        ++issued;
+                        prog = true;
                     }
                 }
+                if (jm < issued) {
+                    const int q = jm % stages, ac = jm & 3;
+                    if (mb_test(full0 + 8 * q, (uint32_t)(jm / stages) & 1u) &&
+                        (jm < 4 || mb_test(acce0 + 8 * ac, (uint32_t)((jm >> 2) - 1) & 1u))) {
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const uint32_t acc = tmem + (uint32_t)(ac * acc_cols);
+                        const uint32_t a0 = tc_smem(As + q * TC_M * SUB);
+#pragma unroll
+                        for (int kk = 0; kk < SUB / 16; ++kk)
+                            umma_bf16(acc, umma_desc(a0 + kk * 2 * LBO_A, LBO_A, SBO_A),
+                                      umma_desc(bh0 + kk * 2 * LBO_B, LBO_B, SBO_B), idesc, kk > 0 ? 1u : 0u);
+                        umma_bf16(acc, ext_desc, umma_desc(bh0 + (SUB / 16) * 2 * LBO_B, LBO_B, SBO_B), idesc, 1u);
+#pragma unroll
+                        for (int kk = 0; kk < SUB / 16; ++kk)
+                            umma_bf16(acc, umma_desc(a0 + kk * 2 * LBO_A, LBO_A, SBO_A),
+                                      umma_desc(bl0 + kk * 2 * LBO_B, LBO_B, SBO_B), idesc, 1u);
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                accf0 + 8 * ac)
+                            : "memory");
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                empty0 + 8 * q)
+                            : "memory");
+                        ++jm;
+                        prog = true;
+                    }
+                }
+                if (prog) {
+                    idle = 0;
+                } else if (++idle > TC_SPIN_LIMIT || s_fail) {
+                    s_fail = 1;
+                    break;
+                }
+            }
+            s_issued = issued;
+            s_mma = jm;
+        }
+    } else {
+        // ---- epilogue: group g takes tiles g, g + 2, ...
+        const int g = warp >> 3, lw = warp & 7, half = lw >> 2;
+        const int row = (lw & 3) * 32 + lane;            // this thread's sample (TMEM lane) in a tile
+        const int gid = 1 + g;                           // the group's named barrier
+        const int hsplit = ((npad / 2 + 15) / 16) * 16;  // columns [0, hsplit) and [hsplit, npad)
+        const int cbeg = half ? hsplit : 0, cend = half ? npad : hsplit;
+        const uint32_t lane_base = (uint32_t)((lw & 3) * 32) << 16;
+        for (int j = g; j < nt; j += 2) {
+            const int q = j % stages, ac = j & 3;
+            const bool ok = tc_wait(accf0 + 8 * ac, (uint32_t)(j >> 2) & 1u) &&
+                            tc_wait(full0 + 8 * q, (uint32_t)(j / stages) & 1u);
+            if (group_any(gid, !ok)) {
+                s_fail = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t taddr = tmem + lane_base + (uint32_t)(ac * acc_cols);
+            const uint16_t* Ap = As + q * TC_M * SUB;
+            const float xn = xs[q * TC_M + row];
+            const int i = (tile0 + j) * TC_M + row;
+            // pass 1: the approximate minimum over this half of the row
+            float m1 = INFINITY;
+            int c0 = cbeg;
+            for (; c0 + 32 <= cend; c0 += 32) {
+                uint32_t r[32];
+                tc_ld32(taddr + (uint32_t)c0, r);
+                m1 = fminf(m1, tc_min<32>(r));
+            }
+            if (c0 < cend) {
+                uint32_t r[16];
+                tc_ld16(taddr + (uint32_t)c0, r);
+                m1 = fminf(m1, tc_min<16>(r));
+            }
+            xm[g][half][row] = m1;
+            group_sync(gid);
+            m1 = fminf(xm[g][0][row], xm[g][1][row]);
+            // pass 2: the real centroids of this half within the band
+            const float thr = m1 + ldexpf(xn + cmax, -11);
+            int cnt = 0, first = 0;
+            for (c0 = cbeg; c0 + 32 <= cend; c0 += 32) {
+                uint32_t r[32];
+                tc_ld32(taddr + (uint32_t)c0, r);
+                const uint32_t m = tc_le<32>(r, thr) & col_mask(k - c0);
+                if (cnt == 0 && m) first = c0 + __ffs(m) - 1;
+                cnt += __popc(m);
+            }
+            if (c0 < cend) {
+                uint32_t r[16];
+                tc_ld16(taddr + (uint32_t)c0, r);
+                const uint32_t m = tc_le<16>(r, thr) & col_mask(k - c0);
+                if (cnt == 0 && m) first = c0 + __ffs(m) - 1;
+                cnt += __popc(m);
+            }
+            xc[g][half][row] = cnt;
+            xf[g][half][row] = first;
+            group_sync(gid);
+            const int c_lo = xc[g][0][row];
+            const bool single = c_lo + xc[g][1][row] <= 1;
+            int bi = c_lo ? xf[g][0][row] : xf[g][1][row];
+            float best = 0.0f;
+            // several within the band: each half re-measures its own, in index
+            // order; the TMEM loads are warp-wide, so a warp walks its chunks
+            // when any of its lanes needs them
+            if (group_any(gid, !single)) {
+                float pb = FLT_MAX;
+                int pi = 0;
+                if (__any_sync(0xffffffffu, !single)) {
+                    const float th2 = single ? -INFINITY : thr;
+                    for (c0 = cbeg; c0 < cend; c0 += 16) {
+                        uint32_t r[16];
+                        tc_ld16(taddr + (uint32_t)c0, r);
+                        uint32_t cand = tc_le<16>(r, th2) & col_mask(k - c0);
+                        while (cand) {
+                            const int c = c0 + __ffs(cand) - 1;
+                            cand &= cand - 1u;
+                            const float dd = dist_tile<SUB>(Ap, row, cf + c * CFLD);
+                            if (dd < pb) {
+                                pb = dd;
+                                pi = c;
+                            }
+                        }
+                    }
+                }
+                xm[g][half][row] = pb;  // (the partials of pass 2 were read before the vote)
+                xc[g][half][row] = pi;
+                group_sync(gid);
+                if (!single) {
+                    const bool lo_wins = xm[g][0][row] <= xm[g][1][row];  // ties: the lower index
+                    best = lo_wins ? xm[g][0][row] : xm[g][1][row];
+                    bi = lo_wins ? xc[g][0][row] : xc[g][1][row];
+                }
+            }
+            if (half == 0) {
+                if (single && want_md) best = dist_tile<SUB>(Ap, row, cf + bi * CFLD);
+                if (i < b.n) {
+                    b.labels[(size_t)t * b.n + i] = bi;
+                    if (want_md) b.md[(size_t)t * b.n + i] = best;
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            group_sync(gid);  // the accumulator, the tile and the exchange arrays are free again
+            if ((tid & (TC_GROUP - 1)) == 0) {
+                mb_arrive(acce0 + 8 * ac);
+                mb_arrive(empty0 + 8 * q);
             }
         }
-        const int i = tile * TC_M + tid;
-        if (i < b.n) {
-            b.labels[(size_t)t * b.n + i] = bi;
-            b.md[(size_t)t * b.n + i] = best;
-        }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();  // TMEM and this sample buffer are free again
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    if (failed) {
-        // report, then let the MMAs in flight finish (bounded) before TMEM goes
-        if (tid == 0 && b.status) atomicOr(b.status, 1);
-        (void)tc_wait(bar, phase);
+    __syncthreads();
+    if (tid == 2 * TC_GROUP && s_fail) {
+        // report, then let the copies and MMAs in flight finish (bounded) before TMEM and shared memory go
+        if (b.status) atomicOr(b.status, 1);
+        const int issued = s_issued, jm = s_mma;
+        for (int j = max(0, jm - 4); j < jm; ++j) (void)tc_wait(accf0 + 8 * (j & 3), (uint32_t)(j >> 2) & 1u);
+        for (int j = jm; j < issued; ++j) (void)tc_wait(full0 + 8 * (j % stages), (uint32_t)(j / stages) & 1u);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * acc_cols) : "memory");
+}
+
+// The keys as a 4-D TMA tensor: (8 bf16 of a chunk, token, chunk of the head
+// dim, head), so that a box of (8, 128, sub / 8, 1) lands chunk-major.  False
+// when the driver entry point is missing or the strides do not qualify.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static bool encode_sample_map(const Dev& d, CUtensorMap* m) {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            (void)cudaGetLastError();
+    }
+    if (!fn) return false;
+    const unsigned long long tb = (unsigned long long)d.tstride * 2;
+    const unsigned long long hb = d.heads > 1 ? (unsigned long long)d.hstride * 2 : tb * (unsigned long long)d.n;
+    if ((reinterpret_cast<uintptr_t>(d.keys) & 15) || (tb & 15) || (hb & 15) || d.dim % 8 || d.sub % 16) return false;
+    const cuuint64_t dims[4] = {8, (cuuint64_t)d.n, (cuuint64_t)(d.dim / 8), (cuuint64_t)d.heads};
+    const cuuint64_t strides[3] = {tb, 16, hb};
+    const cuuint32_t box[4] = {8, (cuuint32_t)TC_M, (cuuint32_t)(d.sub / 8), 1};
+    const cuuint32_t elem[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(d.keys), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // ---------------------------------------------------------------------------
@@ -1288,7 +1543,7 @@ namespace {
 
 struct Layout {
     size_t labels, md, perm_a, perm_b, part_lo, part_hi, part_minl, part_bad, hist, dig_off, dig_tot, counts, offs,
-        erank, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, total;
+        erank, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, xn, total;
     int npad;
 };
 
@@ -1340,6 +1595,7 @@ Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters
     L.chi = take((size_t)T * L.npad * (sub + 16) * 2);
     L.clo = take((size_t)T * L.npad * (sub + 16) * 2);
     L.cn = take((size_t)T * L.npad * 4);
+    L.xn = take(L.npad > 0 ? (size_t)T * ((n + 127) / 128 * 128) * 4 : 0);
     L.total = o;
     return L;
 }
@@ -1379,36 +1635,50 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
         return e;
     const int two_pass = kmax_all > 256;
     // tensor-core E-step when every task's k fits one MMA (N <= 256)
-    const bool tc = d.npad > 0;
-    int tc_ncols = 32, tc_ctas = 1, tc_tiles = 1;
+    // tensor-core E-step when every task's k fits one MMA (N <= 256), the
+    // operands fit shared memory and the keys can be described to the TMA unit
+    int tc_acc = 32, tc_ctas = 1, tc_tiles = 1, tc_stages = 0;
     size_t tc_smem_bytes = 0;
+    CUtensorMap tmap;
+    bool tc = d.npad > 0 && encode_sample_map(d, &tmap);
     if (tc) {
-        while (tc_ncols < d.npad) tc_ncols <<= 1;
-        const size_t need = 2 * (size_t)TC_M * (SUB + 16) * 2 + 2 * (size_t)d.npad * (SUB + 16) * 2 +
-                            (size_t)d.npad * (SUB + 4) * 4 + 16 + 1024;
-        // at most 512 / ncols resident CTAs per SM, so their TMEM always fits
-        const size_t cap = 232448 / (512 / tc_ncols) - 3072;
-        tc_smem_bytes = std::max(need, std::min(cap, (size_t)232448));
-        if ((e = cudaFuncSetAttribute(estep_tc_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)tc_smem_bytes)) != cudaSuccess)
-            return e;
-        const int ntiles = (d.n + TC_M - 1) / TC_M;
-        tc_ctas = std::max(1, std::min(ntiles, (148 * (512 / tc_ncols) + d.T - 1) / d.T));
-        tc_tiles = (ntiles + tc_ctas - 1) / tc_ctas;
-        tc_ctas = (ntiles + tc_tiles - 1) / tc_tiles;
+        while (tc_acc < d.npad) tc_acc <<= 1;  // four accumulators of tc_acc columns
+        const size_t fixed = (size_t)TC_M * 16 * 2 + 2 * (size_t)d.npad * (SUB + 16) * 2 + 64 * 8 +
+                             (size_t)kmax_all * (SUB + 4) * 4;
+        const size_t per_stage = (size_t)TC_M * SUB * 2 + TC_M * 4;
+        const size_t room = 232448 - 8192;  // less the static exchange arrays
+        tc_stages = (int)std::min<size_t>(TC_MAX_STAGES, room > fixed ? (room - fixed) / per_stage : 0);
+        tc = tc_acc * 4 <= 512 && tc_stages >= 2;
+        if (tc) {
+            tc_smem_bytes = fixed + (size_t)tc_stages * per_stage + 1024;
+            // more than half the SM's shared memory: one CTA (and its 512
+            // TMEM columns) per SM
+            tc_smem_bytes = std::max(tc_smem_bytes, (size_t)120 * 1024);
+            if ((e = cudaFuncSetAttribute(estep_tc_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)tc_smem_bytes)) != cudaSuccess)
+                return e;
+            const int ntiles = (d.n + TC_M - 1) / TC_M;
+            tc_ctas = std::max(1, std::min(ntiles, 148 / d.T));
+            tc_tiles = (ntiles + tc_ctas - 1) / tc_ctas;
+            tc_ctas = (ntiles + tc_tiles - 1) / tc_tiles;
+        }
     }
     const size_t ms_smem = (size_t)MS_STAGES * MS_CHUNK * 2;
     if ((e = cudaFuncSetAttribute(msum_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ms_smem)) !=
         cudaSuccess)
         return e;
+    if (tc) xnorm_kernel<SUB><<<dim3((d.nx + BT - 1) / BT, d.T), BT, 0, st>>>(d);
     for (int it = 0; it < a.max_iters; ++it) {
+        // the inertia (and so the exact min distances) is only needed from
+        // two iterations before the first one allowed to stop
+        const int eval = it >= std::max(0, a.early_stop_min_iter - 2) ? 1 : 0;
         if (tc) {
             cent_split_kernel<SUB><<<dim3(d.npad, d.T), 32, 0, st>>>(d);
-            estep_tc_kernel<SUB><<<dim3(tc_ctas, d.T), TC_THREADS, tc_smem_bytes, st>>>(d, tc_tiles, tc_ncols);
+            estep_tc_kernel<SUB><<<dim3(tc_ctas, d.T), TC_CTA_THREADS, tc_smem_bytes, st>>>(d, tmap, tc_tiles, tc_acc,
+                                                                                            tc_stages, eval);
         } else {
             estep_kernel<SUB><<<dim3((d.n + BT - 1) / BT, d.T), BT, es_smem, st>>>(d);
         }
-        const int eval = it >= std::max(0, a.early_stop_min_iter - 2) ? 1 : 0;
         inertia_kernel<<<d.T, IN_THREADS, 0, st>>>(d, it, a.max_iters, a.early_stop_min_iter, a.tol, a.early_stop_rel_tol,
                                             eval);
         Radix r{};
@@ -1535,6 +1805,8 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
     d.chi = reinterpret_cast<uint16_t*>(ws + L.chi);
     d.clo = reinterpret_cast<uint16_t*>(ws + L.clo);
     d.cn = reinterpret_cast<float*>(ws + L.cn);
+    d.xn = reinterpret_cast<float*>(ws + L.xn);
+    d.nx = (d.n + 127) / 128 * 128;
     d.status = a.status;
     d.G = (int)G;
     // per-cell work arrays use stride d.kst (max k); sub-centroids use a.kmax
