@@ -904,6 +904,8 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
             const uint32_t bh0 = tc_smem(Bh), bl0 = tc_smem(Bl);
             constexpr uint32_t LBO_A = TC_M * 16, SBO_A = 128, LBO_B = 128, SBO_B = KC * 16;
             const uint64_t ext_desc = umma_desc(tc_smem(Ae), 128, 256);
+            const uint64_t a_desc0 = umma_desc(tc_smem(As), LBO_A, SBO_A);
+            const uint64_t bh_desc = umma_desc(bh0, LBO_B, SBO_B), bl_desc = umma_desc(bl0, LBO_B, SBO_B);
             const uint32_t stage_bytes = TC_M * SUB * 2;
             const int h = task_h(b, t), s0 = task_s(b, t) * CPR;
             const float* xn_t = b.xn + (size_t)t * b.nx;
@@ -937,16 +939,18 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
                         (jm < 4 || mb_test(acce0 + 8 * ac, (uint32_t)((jm >> 2) - 1) & 1u))) {
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                         const uint32_t acc = tmem + (uint32_t)(ac * acc_cols);
-                        const uint32_t a0 = tc_smem(As + q * TC_M * SUB);
+                        // descriptor start addresses sit in the low bits (16-byte units):
+                        // a K step is a plain add
+                        const uint64_t ad = a_desc0 + (uint64_t)(q * (TC_M * SUB * 2 / 16));
 #pragma unroll
                         for (int kk = 0; kk < SUB / 16; ++kk)
-                            umma_bf16(acc, umma_desc(a0 + kk * 2 * LBO_A, LBO_A, SBO_A),
-                                      umma_desc(bh0 + kk * 2 * LBO_B, LBO_B, SBO_B), idesc, kk > 0 ? 1u : 0u);
-                        umma_bf16(acc, ext_desc, umma_desc(bh0 + (SUB / 16) * 2 * LBO_B, LBO_B, SBO_B), idesc, 1u);
+                            umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bh_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
+                                      idesc, kk > 0 ? 1u : 0u);
+                        umma_bf16(acc, ext_desc, bh_desc + (uint64_t)((SUB / 16) * (2 * LBO_B / 16)), idesc, 1u);
 #pragma unroll
                         for (int kk = 0; kk < SUB / 16; ++kk)
-                            umma_bf16(acc, umma_desc(a0 + kk * 2 * LBO_A, LBO_A, SBO_A),
-                                      umma_desc(bl0 + kk * 2 * LBO_B, LBO_B, SBO_B), idesc, 1u);
+                            umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bl_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
+                                      idesc, 1u);
                         asm volatile(
                             "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                 accf0 + 8 * ac)
@@ -979,8 +983,10 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
         const uint32_t lane_base = (uint32_t)((lw & 3) * 32) << 16;
         for (int j = g; j < nt; j += 2) {
             const int q = j % stages, ac = j & 3;
-            const bool ok = tc_wait(accf0 + 8 * ac, (uint32_t)(j >> 2) & 1u) &&
-                            tc_wait(full0 + 8 * q, (uint32_t)(j / stages) & 1u);
+            // one thread polls the barriers; the group waits at its named barrier
+            bool ok = true;
+            if ((tid & (TC_GROUP - 1)) == 0)
+                ok = tc_wait(accf0 + 8 * ac, (uint32_t)(j >> 2) & 1u) && tc_wait(full0 + 8 * q, (uint32_t)(j / stages) & 1u);
             if (group_any(gid, !ok)) {
                 s_fail = 1;
                 break;
