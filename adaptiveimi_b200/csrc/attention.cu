@@ -7,18 +7,17 @@
 //
 // Grid (splits, groups); 8 warps per CTA, one CTA per SM.  A CTA owns a
 // contiguous range of the group's rows and stages their row-list entries in
-// shared memory.  Each warp streams 16-row tiles through a 3-deep ring: one
-// lane per row issues a 256-byte cp.async.bulk (K rows from lanes 0-15, V rows
-// from lanes 16-31) that completes on the stage's mbarrier, so one warp
-// instruction moves a whole tile.  Rows sit at a 272-byte pitch so the eight
-// rows of an ldmatrix fall on distinct banks.  The warp computes S = Q K^T and
+// shared memory.  Each warp streams 16-row tiles (K and V, 8 KB) through a
+// 3-deep ring of 16-byte cp.async pieces, half a warp per 256-byte row, so
+// the copies ride the ordinary load path (per-row bulk copies were bound by
+// the copy engine's request rate at about 33 GB/s per SM).  Rows sit at a
+// 272-byte pitch so the eight rows of an ldmatrix fall on distinct banks.  The warp computes S = Q K^T and
 // O += P V with mma.sync m16n8k16 (query heads on M: G <= 8 of the 16 rows are
 // live) and keeps an online softmax in exp2 space.  The warps merge through
 // shared memory; the CTA writes one (m, l, o) partial; the last CTA of a group
 // (an atomic counter that it re-zeroes) merges the partials into the bf16
 // output, or a separate merge kernel does when no counter buffer is given.
-// Every mbarrier wait is bounded: a wait that gives up sets bit 0 of
-// `status` and the kernel finishes without hanging.
+// The kernel has no spin-waits (cp.async groups complete in hardware).
 //
 // The kernel is launched as a programmatic dependent (PDL) of the kernel
 // before it in the stream: its CTAs set up their barriers while that kernel
@@ -44,39 +43,10 @@ constexpr int AT_PITCH = 272;                            // bytes per row in sha
                                                          // puts the 8 rows of an ldmatrix on distinct banks
 constexpr int AT_STAGE_BYTES = 2 * AT_TILE * AT_PITCH;   // K tile + V tile
 constexpr int AT_RING_BYTES = AT_WARPS * AT_STAGES * AT_STAGE_BYTES;
-constexpr int AT_BAR_BYTES = AT_WARPS * AT_STAGES * 8;   // one mbarrier per stage per warp
-constexpr int AT_WAIT_LIMIT = 1 << 20;                   // polls of an mbarrier before the kernel gives up
+constexpr int AT_BAR_BYTES = AT_WARPS * AT_STAGES * 8;   // (reserved; the row list follows it)
 
 IMI_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
-IMI_DEV void mbar_init(uint32_t bar, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-IMI_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
-IMI_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// The whole warp polls until every lane sees the phase complete, at most
-// AT_WAIT_LIMIT times; false when it gave up.
-IMI_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
-    for (int i = 0; i < AT_WAIT_LIMIT; ++i)
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-    return false;
-}
-// One row, global -> shared, completing on `bar`; a plain load into this CTA only.
-IMI_DEV void bulk_row(uint32_t dst, const void* src, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-                 "l"(src), "r"((uint32_t)AT_ROWB), "r"(bar)
-                 : "memory");
-}
 IMI_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -130,10 +100,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const uint32_t ring = smem_u32(att_smem);
-    const uint32_t bars = ring + AT_RING_BYTES;
     int32_t* ridx_s = reinterpret_cast<int32_t*>(att_smem + AT_RING_BYTES + AT_BAR_BYTES);
-    if (threadIdx.x < AT_WARPS * AT_STAGES) mbar_init(bars + 8 * threadIdx.x, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     // Launched as a programmatic dependent of the select kernel: everything
     // above overlaps its tail; every global read comes after this wait.
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -175,45 +142,49 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     for (int u = 0; u < 16; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
     const int my_tiles = ntiles > warp ? (ntiles - warp + AT_WARPS - 1) / AT_WARPS : 0;
     const uint32_t wring = ring + warp * AT_STAGES * AT_STAGE_BYTES;
-    const uint32_t wbars = bars + warp * AT_STAGES * 8;
 
-    // Tile `it` of this warp: lane l brings row (l & 15) of the tile's K
-    // (l < 16) or V (l >= 16) with one bulk copy.  Rows past the range or
-    // without a source buffer are zero-filled instead (a past-the-range row is
-    // also masked out of the softmax; a sourceless one counts as a zero row).
+    // Tile `it` of this warp.  Lane l resolves the source of row l of the
+    // tile's 32 rows (K rows 0-15, V rows 16-31); the rows are then copied in
+    // 16-byte cp.async pieces, half a warp per row (256 contiguous bytes), two
+    // rows per warp instruction.  Rows past the range or without a source
+    // buffer are zero-filled (a past-the-range row is also masked out of the
+    // softmax; a sourceless one counts as a zero row).
     auto issue = [&](int it) {
         const int t = warp + it * AT_WARPS;
         const int st = it % AT_STAGES;
-        const uint32_t bar = wbars + 8 * st;
-        const int i = lane & 15, kv = lane >> 4;
-        const int r = t * AT_TILE + i;
-        const unsigned char* src = r < nrows ? row_src(a, h, ridx_s[r], kv) : nullptr;
-        const unsigned live = __ballot_sync(0xffffffffu, src != nullptr);
-        if (lane == 0) mbar_expect_tx(bar, (uint32_t)__popc(live) * AT_ROWB);
-        __syncwarp();
-        const uint32_t dst = wring + st * AT_STAGE_BYTES + (kv * AT_TILE + i) * AT_PITCH;
-        if (src) {
-            bulk_row(dst, src, bar);
-        } else {
+        {
+            const int i = lane & 15, kv = lane >> 4;
+            const int r = t * AT_TILE + i;
+            const unsigned char* src = r < nrows ? row_src(a, h, ridx_s[r], kv) : nullptr;
+            const unsigned long long sp = reinterpret_cast<unsigned long long>(src);
+            const uint32_t base = wring + st * AT_STAGE_BYTES;
+            const int piece = lane & 15;
 #pragma unroll
-            for (int q = 0; q < AT_ROWB / 16; ++q)
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(dst + 16 * q), "r"(0u) : "memory");
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            for (int q = 0; q < 16; ++q) {
+                const int R = 2 * q + (lane >> 4);  // tile row (K: 0-15, V: 16-31) = the lane holding its source
+                const unsigned long long rp = __shfl_sync(0xffffffffu, sp, R);
+                const unsigned char* g = rp ? reinterpret_cast<const unsigned char*>(rp) + 16 * piece
+                                            : reinterpret_cast<const unsigned char*>(a.q);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(base + R * AT_PITCH + 16 * piece),
+                             "l"(g), "r"(rp ? 16 : 0)
+                             : "memory");
+            }
         }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
     };
 
-    int issued = 0, waited = 0;
-    bool failed = false;
-    for (; issued < AT_STAGES - 1 && issued < my_tiles; ++issued) issue(issued);
+    // AT_STAGES - 1 tiles ahead; empty groups keep the per-thread group count
+    // uniform so that wait_group names the right tile
+    for (int j = 0; j < AT_STAGES - 1; ++j) {
+        if (j < my_tiles) issue(j);
+        else asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
     for (int it = 0; it < my_tiles; ++it) {
-        if (issued < my_tiles) issue(issued++);
+        if (it + AT_STAGES - 1 < my_tiles) issue(it + AT_STAGES - 1);
+        else asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(AT_STAGES - 1) : "memory");
+        __syncwarp();  // every lane's pieces of tile `it` have landed
         const int st = it % AT_STAGES;
-        if (!mbar_wait_warp(wbars + 8 * st, (uint32_t)((it / AT_STAGES) & 1))) {
-            failed = true;
-            break;
-        }
-        ++waited;
-        __syncwarp();
         const int t = warp + it * AT_WARPS;
         const uint32_t kb = wring + st * AT_STAGE_BYTES;
         const uint32_t vb = kb + AT_TILE * AT_PITCH;
@@ -265,15 +236,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             mma_bf16(o[u], pa0, 0u, pa2, 0u, b0, b1);
             mma_bf16(o[u + 1], pa0, 0u, pa2, 0u, b2, b3);
         }
-        __syncwarp();
+        __syncwarp();  // the stage is refilled two tiles on
     }
-    if (failed) {
-        // a wait gave up: report it, then let the copies still in flight land
-        // (bounded again) before the ring is reused by the merge below
-        if (lane == 0 && a.status) atomicOr(a.status, 1);
-        for (int it = waited; it < issued; ++it)
-            (void)mbar_wait_warp(wbars + 8 * (it % AT_STAGES), (uint32_t)((it / AT_STAGES) & 1));
-    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     __syncthreads();
@@ -329,72 +294,81 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     }
     __syncthreads();
     if (!s_last) return;
-    // Parallel merge.  Warp g reduces query head g's (m, l) over the splits
-    // (lanes stride the splits, loads independent) and leaves one weight
-    // 2^(m_q - M) per split in shared memory; then every thread sums float4
-    // columns of the partial outputs over a share of the splits, so the loads
-    // of different splits are in flight together instead of one L2 round trip
-    // per split.  The ring is free by now: red[] / sL[] / wsm[] reuse it.
+    // Parallel merge in one round trip: every thread first puts its loads of
+    // the partial outputs (a float4 column of the [G][128] output, for its
+    // share of the splits) in flight, next to the (m, l) loads of all splits;
+    // after one barrier the weights 2^(m_q - M) come from shared memory and
+    // the loaded columns are summed.  The ring is free by now: red[] and the
+    // (m, l) copy reuse it.
     const size_t hb = (size_t)h * a.splits * a.G;
-    float4* red = reinterpret_cast<float4*>(att_smem);                   // [P][G*32]
-    float* sL = reinterpret_cast<float*>(att_smem + 256 * sizeof(float4));  // [8]
-    float* wsm = sL + 8;                                                    // [splits][G]
-    if (warp < a.G) {
-        float M = -INFINITY;
-        for (int q = lane; q < a.splits; q += 32) M = fmaxf(M, __ldcg(&a.part_ml[(hb + (size_t)q * a.G + warp) * 2]));
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-        float L = 0.0f;
-        for (int q = lane; q < a.splits; q += 32) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2*>(&a.part_ml[(hb + (size_t)q * a.G + warp) * 2]));
-            const float f = M == -INFINITY ? 0.0f : exp2f(ml.x - M);
-            wsm[q * a.G + warp] = f;
-            L += ml.y * f;
-        }
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
-        if (lane == 0) {
-            sL[warp] = L;
-            if (a.ml_part) {  // sequence sharding: the group's (max, sum) for the cross-shard combine
-                a.ml_part[((size_t)h * a.G + warp) * 2 + 0] = M;
-                a.ml_part[((size_t)h * a.G + warp) * 2 + 1] = L;
-            }
-        }
-    }
-    __syncthreads();
     const int cols = a.G * 32;  // float4 columns of the [G][128] output
     const int P = (AT_WARPS * 32) / cols;
-    if ((int)threadIdx.x < P * cols) {
-        const int col = threadIdx.x % cols, ph = threadIdx.x / cols;
-        const int gg = col >> 5, d4 = col & 31;
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 4
-        for (int q = ph; q < a.splits; q += P) {
-            const size_t pb = hb + (size_t)q * a.G + gg;
-            const float f = wsm[q * a.G + gg];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.part_o + pb * 128) + d4);
-            acc.x += v.x * f;
-            acc.y += v.y * f;
-            acc.z += v.z * f;
-            acc.w += v.w * f;
+    constexpr int MB = 8;  // splits per thread per batch of loads
+    float4* red = reinterpret_cast<float4*>(att_smem);                      // [P][G*32]
+    float2* sml = reinterpret_cast<float2*>(att_smem + 256 * sizeof(float4));  // [splits][G]
+    const bool active = (int)threadIdx.x < P * cols;
+    const int col = threadIdx.x % cols, ph = threadIdx.x / cols;
+    const int gg = col >> 5, d4 = col & 31;
+    const float4* po = reinterpret_cast<const float4*>(a.part_o);
+    float4 v[MB];
+#pragma unroll
+    for (int k = 0; k < MB; ++k) {
+        const int q = ph + k * P;
+        v[k] = (active && q < a.splits) ? __ldcg(po + (hb + (size_t)q * a.G + gg) * 32 + d4)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    const float2* pml = reinterpret_cast<const float2*>(a.part_ml);
+    for (int t2 = threadIdx.x; t2 < a.splits * a.G; t2 += blockDim.x) sml[t2] = __ldcg(pml + hb + t2);
+    __syncthreads();
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float M = -INFINITY;
+    if (active) {
+        for (int q = 0; q < a.splits; ++q) M = fmaxf(M, sml[q * a.G + gg].x);
+        auto add = [&](int q, const float4& x) {
+            const float f = M == -INFINITY ? 0.0f : exp2f(sml[q * a.G + gg].x - M);
+            acc.x += x.x * f;
+            acc.y += x.y * f;
+            acc.z += x.z * f;
+            acc.w += x.w * f;
+        };
+#pragma unroll
+        for (int k = 0; k < MB; ++k)
+            if (ph + k * P < a.splits) add(ph + k * P, v[k]);
+        for (int q0 = ph + MB * P; q0 < a.splits; q0 += MB * P) {  // more splits than one batch
+#pragma unroll
+            for (int k = 0; k < MB; ++k) {
+                const int q = q0 + k * P;
+                v[k] = q < a.splits ? __ldcg(po + (hb + (size_t)q * a.G + gg) * 32 + d4)
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int k = 0; k < MB; ++k)
+                if (q0 + k * P < a.splits) add(q0 + k * P, v[k]);
         }
         red[ph * cols + col] = acc;
     }
     __syncthreads();
     if ((int)threadIdx.x < cols) {
-        const int col = threadIdx.x, gg = col >> 5, d4 = col & 31;
-        float4 acc = red[col];
-        for (int ph = 1; ph < P; ++ph) {
-            const float4 v = red[ph * cols + col];
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+        float L = 0.0f;
+        for (int q = 0; q < a.splits; ++q) {
+            const float2 ml = sml[q * a.G + gg];
+            L += ml.y * (M == -INFINITY ? 0.0f : exp2f(ml.x - M));
+        }
+        if (a.ml_part && d4 == 0) {  // sequence sharding: the group's (max, sum) for the cross-shard combine
+            a.ml_part[((size_t)h * a.G + gg) * 2 + 0] = M;
+            a.ml_part[((size_t)h * a.G + gg) * 2 + 1] = L;
+        }
+        acc = red[col];
+        for (int p2 = 1; p2 < P; ++p2) {
+            const float4 w = red[p2 * cols + col];
+            acc.x += w.x;
+            acc.y += w.y;
+            acc.z += w.z;
+            acc.w += w.w;
         }
         if (a.o_part)  // sequence sharding: unnormalised, combined across shards later
             *reinterpret_cast<float4*>(a.o_part + ((size_t)h * a.G + gg) * 128 + 4 * d4) = acc;
         if (a.out) {
-            const float L = sL[gg];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
             uint2 packed;
             packed.x = pack_bf16(acc.x * inv, acc.y * inv);

@@ -119,8 +119,8 @@ static int check_select(const imi_select_desc* d) {
 
 static int check_attention(const imi_attn_desc* d) {
     if (!d) return fail(IMI_ERR_INVALID, "imi_sparse_attention: null descriptor");
-    if (d->bg <= 0 || d->G <= 0 || d->G > 8 || d->splits <= 0 || d->splits > 4096)
-        return fail(IMI_ERR_INVALID, "imi_sparse_attention: need 1 <= G <= 8 and 1 <= splits <= 4096");
+    if (d->bg <= 0 || d->G <= 0 || d->G > 8 || d->splits <= 0 || d->splits > 4096 || d->splits * d->G > 16384)
+        return fail(IMI_ERR_INVALID, "imi_sparse_attention: need 1 <= G <= 8, 1 <= splits <= 4096, splits * G <= 16384");
     if (!d->q || !d->row_index || !d->row_count || !d->list_keys || !d->list_values || !d->static_keys ||
         !d->static_values || !d->part_o || !d->part_ml || (!d->out && !d->o_part))
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: null pointer in descriptor");

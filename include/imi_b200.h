@@ -138,7 +138,7 @@ typedef struct imi_select_desc {
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
-    int32_t bg, G, splits, exec_capacity;  /* dim is 128 */
+    int32_t bg, G, splits, exec_capacity;  /* dim is 128; G <= 8, splits <= 4096, splits * G <= 16384 */
     float scale;
     const uint16_t* q;                     /* [bg, G, 128] */
     const int32_t* row_index;              /* [bg, exec_capacity] */
