@@ -6,8 +6,8 @@
 // selected rows are read once, straight from the HBM-resident lists.
 //
 // Grid (splits, groups); 8 warps per CTA, one CTA per SM.  A CTA owns a
-// contiguous range of the group's rows and stages their row-list entries in
-// shared memory.  Each warp streams 16-row tiles (K and V, 8 KB) through a
+// contiguous share of the group's 16-row tiles; its warps read the tiles'
+// row-list entries two tiles ahead.  Each warp streams 16-row tiles (K and V, 8 KB) through a
 // 3-deep ring of 16-byte cp.async pieces, half a warp per 256-byte row, so
 // the copies ride the ordinary load path (per-row bulk copies were bound by
 // the copy engine's request rate at about 33 GB/s per SM).  Rows sit at a
@@ -100,7 +100,6 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const uint32_t ring = smem_u32(att_smem);
-    int32_t* ridx_s = reinterpret_cast<int32_t*>(att_smem + AT_RING_BYTES + AT_BAR_BYTES);
     // Launched as a programmatic dependent of the select kernel: everything
     // above overlaps its tail; every global read comes after this wait.
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -108,16 +107,18 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     const int rows_total = a.row_count[h];
-    int chunk = (rows_total + a.splits - 1) / a.splits;
-    chunk = (chunk + AT_TILE - 1) & ~(AT_TILE - 1);
-    const int r0 = split * chunk;
-    const int r1 = min(rows_total, r0 + chunk);
-    const int nrows = max(0, r1 - r0);
-    const int ntiles = (nrows + AT_TILE - 1) / AT_TILE;
+    const int gtiles = (rows_total + AT_TILE - 1) / AT_TILE;  // the group's 16-row tiles
+    // CTA `split` owns a contiguous share of the group's tiles; its warps take
+    // every AT_WARPS-th tile of it.  (Taking tiles from a per-group atomic
+    // counter instead balanced the CTAs but cost more in contention than it
+    // saved.)
+    int ct0, ct1;
     {
-        const int32_t* ridx = a.row_index + (size_t)h * a.exec_capacity + r0;
-        for (int r = threadIdx.x; r < nrows; r += blockDim.x) ridx_s[r] = ridx[r];
+        const int per = (gtiles + a.splits - 1) / a.splits;
+        ct0 = min(gtiles, split * per);
+        ct1 = min(gtiles, ct0 + per);
     }
+    const int32_t* rlist = a.row_index + (size_t)h * a.exec_capacity;
     uint32_t qa[8][2];
     {
         const uint16_t* qh = a.q + (size_t)h * a.G * 128;
@@ -133,59 +134,58 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             }
         }
     }
-    __syncthreads();
 
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY, l_run = 0.0f;
     float o[16][4];
 #pragma unroll
     for (int u = 0; u < 16; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
-    const int my_tiles = ntiles > warp ? (ntiles - warp + AT_WARPS - 1) / AT_WARPS : 0;
     const uint32_t wring = ring + warp * AT_STAGES * AT_STAGE_BYTES;
+    const int tlimit = ct1;  // tiles at or past this are not this CTA's
+    // the row-list entry of this lane's row of tile t (-1: no row)
+    auto entry = [&](int t) -> int {
+        const int r = t * AT_TILE + (lane & 15);
+        return (t < tlimit && r < rows_total) ? rlist[r] : -1;
+    };
 
-    // Tile `it` of this warp.  Lane l resolves the source of row l of the
-    // tile's 32 rows (K rows 0-15, V rows 16-31); the rows are then copied in
-    // 16-byte cp.async pieces, half a warp per row (256 contiguous bytes), two
-    // rows per warp instruction.  Rows past the range or without a source
-    // buffer are zero-filled (a past-the-range row is also masked out of the
-    // softmax; a sourceless one counts as a zero row).
-    auto issue = [&](int it) {
-        const int t = warp + it * AT_WARPS;
-        const int st = it % AT_STAGES;
-        {
-            const int i = lane & 15, kv = lane >> 4;
-            const int r = t * AT_TILE + i;
-            const unsigned char* src = r < nrows ? row_src(a, h, ridx_s[r], kv) : nullptr;
-            const unsigned long long sp = reinterpret_cast<unsigned long long>(src);
-            const uint32_t base = wring + st * AT_STAGE_BYTES;
-            const int piece = lane & 15;
+    // Issue tile t into stage st.  Lane l holds the row-list entry of row
+    // (l & 15) of the tile; lanes 0-15 resolve the K rows, 16-31 the V rows.
+    // The rows are copied in 16-byte cp.async pieces, half a warp per row
+    // (256 contiguous bytes), two rows per warp instruction.  Rows past the
+    // range or without a source buffer are zero-filled (a past-the-range row
+    // is also masked out of the softmax; a sourceless one counts as a zero row).
+    auto issue = [&](int ent, int st) {
+        const unsigned char* src = row_src(a, h, ent, lane >> 4);  // -1 (source bits 3): no row
+        const unsigned long long sp = reinterpret_cast<unsigned long long>(src);
+        const uint32_t base = wring + st * AT_STAGE_BYTES;
+        const int piece = lane & 15;
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int R = 2 * q + (lane >> 4);  // tile row (K: 0-15, V: 16-31) = the lane holding its source
-                const unsigned long long rp = __shfl_sync(0xffffffffu, sp, R);
-                const unsigned char* g = rp ? reinterpret_cast<const unsigned char*>(rp) + 16 * piece
-                                            : reinterpret_cast<const unsigned char*>(a.q);
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(base + R * AT_PITCH + 16 * piece),
-                             "l"(g), "r"(rp ? 16 : 0)
-                             : "memory");
-            }
+        for (int q = 0; q < 16; ++q) {
+            const int R = 2 * q + (lane >> 4);  // tile row (K: 0-15, V: 16-31) = the lane holding its source
+            const unsigned long long rp = __shfl_sync(0xffffffffu, sp, R);
+            const unsigned char* gp = rp ? reinterpret_cast<const unsigned char*>(rp) + 16 * piece
+                                         : reinterpret_cast<const unsigned char*>(a.q);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(base + R * AT_PITCH + 16 * piece),
+                         "l"(gp), "r"(rp ? 16 : 0)
+                         : "memory");
         }
         asm volatile("cp.async.commit_group;\n" ::: "memory");
     };
 
-    // AT_STAGES - 1 tiles ahead; empty groups keep the per-thread group count
-    // uniform so that wait_group names the right tile
-    for (int j = 0; j < AT_STAGES - 1; ++j) {
-        if (j < my_tiles) issue(j);
-        else asm volatile("cp.async.commit_group;\n" ::: "memory");
-    }
-    for (int it = 0; it < my_tiles; ++it) {
-        if (it + AT_STAGES - 1 < my_tiles) issue(it + AT_STAGES - 1);
-        else asm volatile("cp.async.commit_group;\n" ::: "memory");
+    // Software pipeline, per warp: tile q0 is computed while q1 is in flight
+    // and the row-list entries of tB are loaded (tB is issued next).
+    int q0 = ct0 + warp, q1 = q0 + AT_WARPS, tB = q0 + 2 * AT_WARPS;
+    int eB = entry(tB);
+    issue(entry(q0), 0);
+    issue(entry(q1), 1);
+    for (int it = 0; q0 < tlimit; ++it) {
+        issue(eB, (it + 2) % AT_STAGES);  // tile tB into the stage freed by the tile before q0
+        const int tN = tB;
+        tB += AT_WARPS;
+        eB = entry(tB);
         asm volatile("cp.async.wait_group %0;\n" ::"n"(AT_STAGES - 1) : "memory");
-        __syncwarp();  // every lane's pieces of tile `it` have landed
+        __syncwarp();  // every lane's pieces of tile q0 have landed
         const int st = it % AT_STAGES;
-        const int t = warp + it * AT_WARPS;
         const uint32_t kb = wring + st * AT_STAGE_BYTES;
         const uint32_t vb = kb + AT_TILE * AT_PITCH;
         float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
@@ -198,12 +198,12 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             mma_bf16(s0, qa[j][0], 0u, qa[j][1], 0u, b0, b1);
             mma_bf16(s1, qa[j][0], 0u, qa[j][1], 0u, b2, b3);
         }
-        const int rb = t * AT_TILE;  // relative to r0
+        const int rb = q0 * AT_TILE;
         float x[4];
-        x[0] = (rb + 2 * c < nrows) ? s0[0] * sl2 : -INFINITY;
-        x[1] = (rb + 2 * c + 1 < nrows) ? s0[1] * sl2 : -INFINITY;
-        x[2] = (rb + 8 + 2 * c < nrows) ? s1[0] * sl2 : -INFINITY;
-        x[3] = (rb + 9 + 2 * c < nrows) ? s1[1] * sl2 : -INFINITY;
+        x[0] = (rb + 2 * c < rows_total) ? s0[0] * sl2 : -INFINITY;
+        x[1] = (rb + 2 * c + 1 < rows_total) ? s0[1] * sl2 : -INFINITY;
+        x[2] = (rb + 8 + 2 * c < rows_total) ? s1[0] * sl2 : -INFINITY;
+        x[3] = (rb + 9 + 2 * c < rows_total) ? s1[1] * sl2 : -INFINITY;
         float tmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
@@ -237,6 +237,8 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
             mma_bf16(o[u + 1], pa0, 0u, pa2, 0u, b2, b3);
         }
         __syncwarp();  // the stage is refilled two tiles on
+        q0 = q1;
+        q1 = tN;
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -437,11 +439,7 @@ cudaError_t launch_combine_shards(const CombineArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-size_t attn_smem_bytes(const AttnArgs& a) {
-    int chunk = (a.exec_capacity + a.splits - 1) / a.splits;
-    chunk = (chunk + AT_TILE - 1) & ~(AT_TILE - 1);
-    return (size_t)AT_RING_BYTES + AT_BAR_BYTES + (size_t)chunk * 4;
-}
+size_t attn_smem_bytes(const AttnArgs&) { return (size_t)AT_RING_BYTES + AT_BAR_BYTES; }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     const size_t sm = attn_smem_bytes(a);
