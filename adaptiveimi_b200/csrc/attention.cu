@@ -299,15 +299,18 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     // Parallel merge in one round trip: every thread first puts its loads of
     // the partial outputs (a float4 column of the [G][128] output, for its
     // share of the splits) in flight, next to the (m, l) loads of all splits;
-    // after one barrier the weights 2^(m_q - M) come from shared memory and
-    // the loaded columns are summed.  The ring is free by now: red[] and the
-    // (m, l) copy reuse it.
+    // after one barrier warp g turns head g's (m, l) into M, L and one weight
+    // 2^(m_q - M) per split, and after a second the loaded columns are summed
+    // with those weights.  The ring is free by now: red[], the (m, l) copy and
+    // the weights reuse it.
     const size_t hb = (size_t)h * a.splits * a.G;
     const int cols = a.G * 32;  // float4 columns of the [G][128] output
     const int P = (AT_WARPS * 32) / cols;
-    constexpr int MB = 8;  // splits per thread per batch of loads
+    constexpr int MB = 20;  // splits per thread per batch of loads
     float4* red = reinterpret_cast<float4*>(att_smem);                      // [P][G*32]
-    float2* sml = reinterpret_cast<float2*>(att_smem + 256 * sizeof(float4));  // [splits][G]
+    float* sL = reinterpret_cast<float*>(att_smem + 256 * sizeof(float4));  // [8]
+    float2* sml = reinterpret_cast<float2*>(sL + 8);                        // [splits][G]
+    float* wsm = reinterpret_cast<float*>(sml + a.splits * a.G);            // [splits][G]
     const bool active = (int)threadIdx.x < P * cols;
     const int col = threadIdx.x % cols, ph = threadIdx.x / cols;
     const int gg = col >> 5, d4 = col & 31;
@@ -322,12 +325,33 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const float2* pml = reinterpret_cast<const float2*>(a.part_ml);
     for (int t2 = threadIdx.x; t2 < a.splits * a.G; t2 += blockDim.x) sml[t2] = __ldcg(pml + hb + t2);
     __syncthreads();
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float M = -INFINITY;
+    if (warp < a.G) {
+        float M = -INFINITY;
+        for (int q = lane; q < a.splits; q += 32) M = fmaxf(M, sml[q * a.G + warp].x);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+        float L = 0.0f;
+        for (int q = lane; q < a.splits; q += 32) {
+            const float2 ml = sml[q * a.G + warp];
+            const float f = M == -INFINITY ? 0.0f : exp2f(ml.x - M);
+            wsm[q * a.G + warp] = f;
+            L += ml.y * f;
+        }
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        if (lane == 0) {
+            sL[warp] = L;
+            if (a.ml_part) {  // sequence sharding: the group's (max, sum) for the cross-shard combine
+                a.ml_part[((size_t)h * a.G + warp) * 2 + 0] = M;
+                a.ml_part[((size_t)h * a.G + warp) * 2 + 1] = L;
+            }
+        }
+    }
+    __syncthreads();
     if (active) {
-        for (int q = 0; q < a.splits; ++q) M = fmaxf(M, sml[q * a.G + gg].x);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         auto add = [&](int q, const float4& x) {
-            const float f = M == -INFINITY ? 0.0f : exp2f(sml[q * a.G + gg].x - M);
+            const float f = wsm[q * a.G + gg];
             acc.x += x.x * f;
             acc.y += x.y * f;
             acc.z += x.z * f;
@@ -351,16 +375,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     }
     __syncthreads();
     if ((int)threadIdx.x < cols) {
-        float L = 0.0f;
-        for (int q = 0; q < a.splits; ++q) {
-            const float2 ml = sml[q * a.G + gg];
-            L += ml.y * (M == -INFINITY ? 0.0f : exp2f(ml.x - M));
-        }
-        if (a.ml_part && d4 == 0) {  // sequence sharding: the group's (max, sum) for the cross-shard combine
-            a.ml_part[((size_t)h * a.G + gg) * 2 + 0] = M;
-            a.ml_part[((size_t)h * a.G + gg) * 2 + 1] = L;
-        }
-        acc = red[col];
+        float4 acc = red[col];
         for (int p2 = 1; p2 < P; ++p2) {
             const float4 w = red[p2 * cols + col];
             acc.x += w.x;
@@ -371,6 +386,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
         if (a.o_part)  // sequence sharding: unnormalised, combined across shards later
             *reinterpret_cast<float4*>(a.o_part + ((size_t)h * a.G + gg) * 128 + 4 * d4) = acc;
         if (a.out) {
+            const float L = sL[gg];
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
             uint2 packed;
             packed.x = pack_bf16(acc.x * inv, acc.y * inv);
