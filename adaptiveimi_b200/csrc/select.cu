@@ -87,6 +87,11 @@ struct SelHdr {
     long long pre2[3];
     unsigned long long T2, flags2;
     int wsel[SL_WARPS], wkept[SL_WARPS];
+    // cluster-wide emission: the thresholds (leader -> every CTA), then each
+    // CTA's selected / kept counts, selected rows and stop-marker candidate
+    unsigned long long cthrA, cthrB;
+    int pc_sel[SL_CL], pc_rows[SL_CL], pc_kept[SL_CL];
+    unsigned long long pc_nx[SL_CL];
     unsigned long long rscr[2][48];  // resolve scratch per warp: 32 keys, then 32 sizes
 };
 
@@ -613,8 +618,9 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     const int chunk = (ne + SL_CL - 1) / SL_CL;
     const int c0 = rank * chunk;
     const int c1 = min(ne, c0 + chunk);
-    int ccv[SL_CPT], szv[SL_CPT];
+    int ccv[SL_CPT], szv[SL_CPT], ofv[SL_CPT];
     bool mkv[SL_CPT], dkv[SL_CPT];
+    const int32_t* offs = a.cell_offsets + hs * (n + 1);
 #pragma unroll
     for (int j = 0; j < SL_CPT; ++j) {
         const int c = c0 + tid + j * SL_THREADS;
@@ -623,7 +629,12 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         mkv[j] = in ? mask[c] != 0 : true;
         szv[j] = in ? sizes[c] : 0;
         dkv[j] = in && dirty ? dirty[c] != 0 : false;
+        ofv[j] = in && a.row_index ? offs[c] : 0;  // used by the emission, loaded with the rest
     }
+    // the leader's delta-ring inputs, loaded with the rest as well
+    const int32_t* dids = a.delta_count ? a.delta_cell_ids + hs * a.delta_capacity : nullptr;
+    const int dcount0 = (rank == 0 && a.delta_count) ? a.delta_count[h] : 0;
+    const int did0 = (rank == 0 && dids && tid < a.delta_capacity) ? dids[tid] : -1;
     if (tid < a.dim) {
         float acc = 0.0f;
         for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bf16_bits_to_f32(a.q[(hs * a.G + g) * a.dim + tid]));
@@ -683,6 +694,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             score_chains<SL_CPT>(acc, sep, il, q2, cT, ldT, sub);
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+    unsigned long long mykey[SL_CPT];  // this thread's slots' keys (0: not a candidate), kept for the emission
     {
         SelHdr* lead = cluster.map_shared_rank(&sm, 0);
         unsigned long long* lkey = cluster.map_shared_rank(skey, 0);
@@ -691,6 +703,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < SL_CPT; ++j) {
             const int c = c0 + tid + j * SL_THREADS;
+            mykey[j] = 0ull;
             if (c >= c1) continue;
             unsigned long long key = 0ull;
             float s = -INFINITY;
@@ -714,6 +727,7 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
             }
             lkey[c] = key;
             lsz[c] = key ? szv[j] : 0;
+            mykey[j] = key;
             if (a.scores_out) a.scores_out[hs * n + c] = s;
         }
 #pragma unroll
@@ -743,67 +757,156 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     if (a.scores_out)
         for (int c = ne + rank * SL_THREADS + tid; c < n; c += SL_CL * SL_THREADS) a.scores_out[hs * n + c] = -INFINITY;
     cluster.sync();  // every score is in the leader
-    if (rank != 0) return;
-    SL_STAMP(2);
-    unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
-    for (int r = 0; r < SL_CL; ++r) {
-        key_lo0 = min(key_lo0, sm.rmin[r]);
-        key_hi0 = max(key_hi0, sm.rmax[r]);
-    }
-
-    // ---------------- leader: the two boundaries ----------------
     unsigned long long thrA = ~0ull, thrB = ~0ull;  // no candidates: nothing selected
-    if (key_hi0 != 0ull) {
-        if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
-            thrA = sm.T;
-            thrB = sm.T2;
-        } else {
-            search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
-            thrA = sm.T;
-            const bool token_or_rank = sm.flags != 0ull;
-            __syncthreads();
-            if (token_or_rank) {
-                thrB = thrA;
-            } else {
-                search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 0, rules);
-                thrB = sm.T;
-            }
+    if (rank == 0) {
+        SL_STAMP(2);
+        unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
+        for (int r = 0; r < SL_CL; ++r) {
+            key_lo0 = min(key_lo0, sm.rmin[r]);
+            key_hi0 = max(key_hi0, sm.rmax[r]);
         }
-        __syncthreads();
-    }
-    SL_STAMP(3);
 
-    // ---------------- leader: emission in slot order ----------------
-    // warp w owns the contiguous slot range [w*R, (w+1)*R); lanes take
-    // consecutive slots (conflict-free); ballots count and rank
-    const int R = ((ne + SL_WARPS - 1) / SL_WARPS + 31) & ~31;
-    const int w0 = wid * R, w1 = min(ne, w0 + R);
+        // ---------------- leader: the two boundaries ----------------
+        if (key_hi0 != 0ull) {
+            if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
+                thrA = sm.T;
+                thrB = sm.T2;
+            } else {
+                search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
+                thrA = sm.T;
+                const bool token_or_rank = sm.flags != 0ull;
+                __syncthreads();
+                if (token_or_rank) {
+                    thrB = thrA;
+                } else {
+                    search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 0, rules);
+                    thrB = sm.T;
+                }
+            }
+            __syncthreads();
+        }
+        SL_STAMP(3);
+        if (tid < SL_CL) {  // the thresholds into every CTA
+            SelHdr* dst = cluster.map_shared_rank(&sm, tid);
+            dst->cthrA = thrA;
+            dst->cthrB = thrB;
+        }
+    }
+    cluster.sync();  // the thresholds are everywhere
+    thrA = sm.cthrA;
+    thrB = sm.cthrB;
+
+    // ---------------- every CTA: its slice's part of the emission ----------------
+    // Slot order within the slice is (j, tid).  One block scan of the
+    // per-j selected flags (16-bit fields of one word) ranks this thread's
+    // slots among the slice's selected cells; the selected cells' sizes then
+    // go into a compact list in that order and a second scan places their rows.
+    int lsel[SL_CPT];  // slice-local rank of a selected slot (-1: not selected)
+    int csel = 0, ckept = 0;
+    unsigned long long nxl = 0ull;  // highest-ranked candidate left out in this slice
     {
-        int wsel = 0, wkept = 0;
-        unsigned long long nx = 0ull;  // highest-ranked candidate left out (the stop marker)
-        for (int base = w0; base < w1; base += 32) {
-            const int c = base + lid;
-            const unsigned long long k = c < w1 ? skey[c] : 0ull;
-            wsel += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrA));
-            wkept += __popc(__ballot_sync(0xffffffffu, k != 0ull && k > thrB));
-            if (k != 0ull && k <= thrA) nx = max(nx, k);
-        }
+        unsigned long long x = 0ull;
+        unsigned int y = 0u;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) nx = max(nx, (unsigned long long)__shfl_xor_sync(0xffffffffu, nx, o));
-        if (lid == 0) {
-            sm.wsel[wid] = wsel;
-            sm.wkept[wid] = wkept;
-            sm.rscr[0][wid] = nx;
+        for (int j = 0; j < SL_CPT; ++j) {
+            const unsigned long long k = mykey[j];
+            if (k != 0ull && k > thrA) x |= 1ull << (16 * j);
+            if (k != 0ull && k > thrB) ++y;
+            if (k != 0ull && k <= thrA) nxl = max(nxl, k);
         }
+        const unsigned long long mine = x;
+        sl_scan_pair(x, y, sm);  // inclusive; the fields never carry (at most 512 per field)
+        const unsigned long long tot = sm.red64[SL_WARPS - 1];
+        ckept = (int)sm.red32[SL_WARPS - 1];
+        int before = 0;  // selected slots of the earlier j
+#pragma unroll
+        for (int j = 0; j < SL_CPT; ++j) {
+            const int fj = (int)((x >> (16 * j)) & 0xffff), mj = (int)((mine >> (16 * j)) & 1);
+            lsel[j] = mj ? before + fj - 1 : -1;
+            before += (int)((tot >> (16 * j)) & 0xffff);
+        }
+        csel = before;
+    }
+    int* l_start = sel_start;
+    int* l_off = sel_off;
+    int* l_sz = sel_slot;
+#pragma unroll
+    for (int j = 0; j < SL_CPT; ++j) {
+        if (lsel[j] < 0) continue;
+        l_sz[lsel[j]] = szv[j];
+        l_off[lsel[j]] = ofv[j];
     }
     __syncthreads();
-    if (tid == 0 && a.cand_out) {  // the stop marker after the selected cells, then the count
+    int crow = 0;
+    {  // row starts of the compact list (slice-local), thread t owns entries 4t .. 4t+3
+        int szs[4], loc = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int i = 4 * tid + q;
+            szs[q] = i < csel ? l_sz[i] : 0;
+            loc += szs[q];
+        }
+        int run = sl_scan(loc, sm.redi, &crow) - loc;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int i = 4 * tid + q;
+            if (i < csel) l_start[i] = run;
+            run += szs[q];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nxl = max(nxl, (unsigned long long)__shfl_xor_sync(0xffffffffu, nxl, o));
+    if (lid == 0) sm.rscr[0][wid] = nxl;
+    __syncthreads();
+    if (tid < SL_CL) {  // this slice's counts into every CTA
         unsigned long long nx = 0ull;
         for (int q = 0; q < SL_WARPS; ++q) nx = max(nx, sm.rscr[0][q]);
-        int ns = 0;
-        for (int q = 0; q < SL_WARPS; ++q) ns += sm.wsel[q];
-        ns = min(ns, a.nprobe);
-        unsigned long long* rec = a.cand_out + hs * (2 * (size_t)(a.nprobe + 1) + 1);
+        SelHdr* dst = cluster.map_shared_rank(&sm, tid);
+        dst->pc_sel[rank] = csel;
+        dst->pc_rows[rank] = crow;
+        dst->pc_kept[rank] = ckept;
+        dst->pc_nx[rank] = nx;
+    }
+    cluster.sync();
+    int sel_base = 0, row_base = a.static_len, nsel = 0, nkept = 0, sel_rows = 0;
+    unsigned long long nx = 0ull;
+    for (int r = 0; r < SL_CL; ++r) {
+        if (r < rank) {
+            sel_base += sm.pc_sel[r];
+            row_base += sm.pc_rows[r];
+        }
+        nsel += sm.pc_sel[r];
+        sel_rows += sm.pc_rows[r];
+        nkept += sm.pc_kept[r];
+        nx = max(nx, sm.pc_nx[r]);
+    }
+    SL_STAMP(4);
+    unsigned long long* rec = a.cand_out ? a.cand_out + hs * (2 * (size_t)(a.nprobe + 1) + 1) : nullptr;
+    int32_t* rows = a.row_index ? a.row_index + hs * (size_t)a.exec_capacity : nullptr;
+#pragma unroll
+    for (int j = 0; j < SL_CPT; ++j) {
+        if (lsel[j] < 0) continue;
+        const int my = sel_base + lsel[j];
+        if (my < a.nprobe) {
+            a.sel_cells[hs * a.nprobe + my] = c0 + tid + j * SL_THREADS;
+            if (rec) {
+                rec[my] = mykey[j];
+                rec[a.nprobe + 1 + my] = (unsigned long long)szv[j];
+            }
+        }
+    }
+    if (rows) {
+        for (int i = wid; i < csel; i += SL_WARPS) {
+            const int s0 = row_base + l_start[i], off = l_off[i], sz = l_sz[i];
+            for (int jj = lid; jj < sz; jj += 32)
+                if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
+        }
+    }
+    if (rank != 0) return;
+
+    // ---------------- leader: stop marker, static and delta rows, counts ----------------
+    if (tid == 0 && rec) {  // the stop marker after the selected cells, then the count
+        const int ns = min(nsel, a.nprobe);
         if (nx) {
             const int slot = (int)(0xffffffffu - (uint32_t)nx) - a.key_base;
             rec[ns] = nx;
@@ -811,93 +914,25 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
         }
         rec[2 * (a.nprobe + 1)] = (unsigned long long)(ns + (nx ? 1 : 0));
     }
-    int sel_base = 0, nsel = 0, nkept = 0;
-    for (int q = 0; q < SL_WARPS; ++q) {
-        const int ws = sm.wsel[q];
-        if (q < wid) sel_base += ws;
-        nsel += ws;
-        nkept += sm.wkept[q];
-    }
-    {
-        int si = sel_base;
-        const unsigned lt = (1u << lid) - 1u;
-        for (int base = w0; base < w1; base += 32) {
-            const int c = base + lid;
-            const unsigned long long k = c < w1 ? skey[c] : 0ull;
-            const bool fin = k != 0ull && k > thrA;
-            const unsigned fm = __ballot_sync(0xffffffffu, fin);
-            if (fin) {
-                const int my = si + __popc(fm & lt);
-                if (my < a.nprobe) {
-                    a.sel_cells[hs * a.nprobe + my] = c;
-                    if (a.cand_out) {
-                        unsigned long long* rec = a.cand_out + hs * (2 * (size_t)(a.nprobe + 1) + 1);
-                        rec[my] = k;
-                        rec[a.nprobe + 1 + my] = (unsigned long long)ssz[c];
-                    }
-                }
-                if (my < SL_SEL_MAX) sel_slot[my] = c;
-            }
-            si += __popc(fm);
-        }
-    }
-    __syncthreads();
-    SL_STAMP(4);
-    if (a.row_index == nullptr) {  // candidates only (the sharded merge writes the rows)
+    if (!rows) {  // candidates only (the sharded merge writes the rows)
         if (tid == 0) {
             a.sel_count[h] = min(nsel, a.nprobe);
             if (a.kept_count) a.kept_count[h] = nkept;
         }
         return;
     }
-    // row offsets of the selected cells (slot order) by one block scan;
-    // thread t owns entries 4t .. 4t+3
-    const int ns = min(nsel, SL_SEL_MAX);
-    const int32_t* offs = a.cell_offsets + hs * (n + 1);
     const int static_len = a.static_len;
-    int sel_rows = 0;
-    {
-        int szs[4], ofv[4], loc = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {  // the offset loads are in flight during the scan
-            const int i = 4 * tid + q;
-            const int slot = i < ns ? sel_slot[i] : 0;
-            szs[q] = i < ns ? ssz[slot] : 0;
-            ofv[q] = i < ns ? offs[slot] : 0;
-            loc += szs[q];
-        }
-        int tot;
-        int run = sl_scan(loc, sm.redi, &tot) - loc + static_len;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int i = 4 * tid + q;
-            if (i < ns) {
-                sel_start[i] = run;
-                sel_off[i] = ofv[q];
-            }
-            run += szs[q];
-        }
-        sel_rows = tot;
-    }
-    __syncthreads();
-    int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
     for (int r = tid; r < static_len; r += SL_THREADS) rows[r] = (1 << 30) | r;
-    for (int i = wid; i < ns; i += SL_WARPS) {
-        const int s0 = sel_start[i], off = sel_off[i], sz = ssz[sel_slot[i]];
-        for (int jj = lid; jj < sz; jj += 32)
-            if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
-    }
     int total = min(static_len + sel_rows, a.exec_capacity);
     if (a.delta_count) {
-        const int dcount = min(a.delta_count[h], a.delta_capacity);
+        const int dcount = min(dcount0, a.delta_capacity);
         const bool has_pad = nkept < a.nprobe;
-        const int32_t* dids = a.delta_cell_ids + hs * a.delta_capacity;
         int appended = 0;
         for (int base = 0; base < dcount; base += SL_THREADS) {
             const int pidx = base + tid;
             int f = 0;
             if (pidx < dcount) {
-                const int cid = dids[pidx];
+                const int cid = base == 0 ? did0 : dids[pidx];
                 if (cid >= 0 && cid < ne) {
                     const unsigned long long k = skey[cid];
                     f = (k != 0ull && k > thrB) ? 1 : 0;
