@@ -53,7 +53,7 @@ KMEANS = {"max_iters": 20, "tol": 0.0005, "early_stop_min_iter": 20, "early_stop
 # `python bench.py --layers 2 --steps 2 --warmup 3 --no-cpu-baseline` with
 # --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 # -k regex:imi_attn_kernel -s 4 -c 3 (each launch is one full layer).
-ATTN_TRAFFIC_BYTES = 50_226_539
+ATTN_TRAFFIC_BYTES = 50_290_518
 ASYNC = {"enabled": True, "batch": 16, "threshold": 16, "delta_tokens": 512}
 
 
