@@ -197,13 +197,14 @@ static int check_decode_attend(const imi_select_desc* sel, const imi_attn_desc* 
     return IMI_OK;
 }
 
+// app: a steady-zone append that the select kernel performs itself
 static int launch_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
-                                void* stream) {
+                                void* stream, const imi_append_desc* app = nullptr) {
     if (apply) {
         cudaError_t e = imi::launch_apply(*apply, S(stream));
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
     }
-    cudaError_t e = imi::launch_select(*sel, S(stream));
+    cudaError_t e = imi::launch_select(*sel, S(stream), app);
     if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
     return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");
 }
@@ -229,7 +230,12 @@ int imi_decode_layer(const imi_append_desc* app, const imi_async_desc* as, const
         const int st = check_decode_attend(sel, attn, apply);
         if (st != IMI_OK) return st;
     }
-    if (app) {
+    // Without an async assignment in this step nothing reads the appended
+    // rows before the attention, so the select kernel does the append (one
+    // launch and one programmatic hand-off fewer); the assignment reads the
+    // batch slot that the append writes, so with it the append goes first.
+    const bool fuse = app && !as && app->bg == sel->bg;
+    if (app && !fuse) {
         cudaError_t e = imi::launch_append(*app, S(stream));
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_layer(append)");
     }
@@ -237,7 +243,7 @@ int imi_decode_layer(const imi_append_desc* app, const imi_async_desc* as, const
         cudaError_t e = imi::launch_async_assign(*as, S(stream));
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_layer(async assignment)");
     }
-    return launch_decode_attend(sel, attn, apply, stream);
+    return launch_decode_attend(sel, attn, apply, stream, fuse ? app : nullptr);
 }
 
 int imi_merge_candidates(const imi_merge_desc* d, void* stream) {

@@ -53,24 +53,9 @@ __global__ void imi_append_kernel(const __grid_constant__ AppendArgs a) {
     // next one (the selection) start its launch
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    const int h = blockIdx.x;
     const int t = threadIdx.x >> 5;  // 0 = keys, 1 = values
-    const int lane = threadIdx.x & 31;
     if (t > 1) return;
-    const uint4* src = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const unsigned char*>(t ? a.new_values : a.new_keys) + (size_t)h * a.src_head_stride * 2);
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(t ? a.zone_values : a.zone_keys) +
-                                          ((size_t)h * a.zone_rows + a.pos) * a.dim * 2);
-    const int n16 = a.dim * 2 / 16;
-    for (int i = lane; i < n16; i += 32) {
-        const uint4 v = src[i];
-        dst[i] = v;
-        if (a.batch_keys) {
-            uint4* bd = reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(t ? a.batch_values : a.batch_keys) +
-                                                 ((size_t)h * a.batch_cap + a.batch_slot) * a.dim * 2);
-            bd[i] = v;
-        }
-    }
+    append_group(a, blockIdx.x, t, threadIdx.x & 31);
 }
 
 // ----------------------------------------------------------------------------

@@ -524,7 +524,7 @@ IMI_DEV int prefix_table_offset(const SelectArgs& a, int s, int sub) {
 }
 
 __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
-    imi_select_kernel(const __grid_constant__ SelectArgs a) {
+    imi_select_kernel(const __grid_constant__ SelectArgs a, const __grid_constant__ AppendArgs ap) {
     extern __shared__ __align__(16) unsigned char dyn[];
     SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
     cg::cluster_group cluster = cg::this_cluster();
@@ -594,6 +594,9 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     // launched as a programmatic dependent (of the append): everything above
     // overlapped the previous kernel; every global read comes after this
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    // the fused steady-zone append of this group (ap.new_keys set): two warps
+    // of the last CTA, which has nothing else to do until the scores
+    if (ap.new_keys && rank == SL_CL - 1 && wid < 2) append_group(ap, h, wid, lid);
 
     const int32_t* sizes = a.cell_sizes + hs * n;
     const uint8_t* mask = a.cell_mask + hs * n;
@@ -1124,12 +1127,13 @@ size_t select_smem_bytes(const SelectArgs& a) {
 
 int select_max_slots() { return SL_MAX_SLOTS; }
 
-cudaError_t launch_select(const SelectArgs& a, cudaStream_t st) {
+cudaError_t launch_select(const SelectArgs& a, cudaStream_t st, const AppendArgs* app) {
     const size_t sm = select_smem_bytes(a);
     static int smem_set[64] = {};
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_select_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
-    return launch_pdl(imi_select_kernel, dim3(SL_CL, a.bg), dim3(SL_THREADS), sm, st, a);
+    AppendArgs none{};
+    return launch_pdl(imi_select_kernel, dim3(SL_CL, a.bg), dim3(SL_THREADS), sm, st, a, app ? *app : none);
 }
 
 }  // namespace imi
