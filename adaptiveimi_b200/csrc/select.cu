@@ -591,6 +591,33 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
     // first half of the cluster barrier that guards the DSMEM stores: every
     // CTA is running
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    // While the previous kernel drains, warm L2 (and the address translations)
+    // for every input line this CTA will read.  A prefetch returns no data,
+    // so it cannot observe anything the previous kernel writes; the loads
+    // proper come after the wait below.
+    {
+        const int chunk0 = (((a.slot_bound > 0 && a.slot_bound < a.n_slots) ? a.slot_bound : a.n_slots) + SL_CL - 1) / SL_CL;
+        const int p0 = rank * chunk0;
+        const size_t base = (size_t)h * a.n_slots;
+        auto pf = [](const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); };
+        // 32 slots per line of the 4-byte arrays, 128 of the byte arrays
+        for (int i = tid * 32; i < chunk0; i += SL_THREADS * 32) {
+            pf(a.cell_code + base + p0 + i);
+            pf(a.cell_sizes + base + p0 + i);
+            if (a.row_index) pf(a.cell_offsets + (size_t)h * (a.n_slots + 1) + p0 + i);
+            if ((i & 127) == 0) {
+                pf(a.cell_mask + base + p0 + i);
+                if (a.cell_dirty) pf(a.cell_dirty + base + p0 + i);
+            }
+        }
+        const int S0 = a.parts == 0 ? 1 : a.parts;
+        if (S0 > 1) {  // the sub-centroid tables, one line per thread step
+            const char* sc = reinterpret_cast<const char*>(a.sub_centroids + (size_t)h * S0 * a.kmax * (a.dim / S0));
+            const size_t bytes = (size_t)S0 * a.kmax * (a.dim / S0) * 4;
+            for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)SL_THREADS * 128) pf(sc + o);
+        }
+        if (tid < (a.G * a.dim * 2 + 127) / 128) pf(reinterpret_cast<const char*>(a.q + (size_t)h * a.G * a.dim) + tid * 128);
+    }
     // launched as a programmatic dependent (of the append): everything above
     // overlapped the previous kernel; every global read comes after this
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
