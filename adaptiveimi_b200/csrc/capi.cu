@@ -94,7 +94,8 @@ static int check_select(const imi_select_desc* d) {
     if (!d->q || !d->cell_code || !d->cell_sizes || !d->cell_offsets || !d->cell_mask || !d->centroids ||
         !d->sub_centroids || !d->sel_cells || !d->sel_count || (!d->row_index != !d->row_count))
         return fail(IMI_ERR_INVALID, "imi_select_cells: null pointer in descriptor");
-    if (d->nprobe > 2048) return fail(IMI_ERR_INVALID, "imi_select_cells: nprobe > 2048 is not supported");
+    if (d->nprobe > imi::select_max_slots())
+        return fail(IMI_ERR_INVALID, "imi_select_cells: nprobe > " + std::to_string(imi::select_max_slots()) + " is not supported");
     if (d->key_base < 0 || (int64_t)d->key_base + d->n_slots > 0x7fffffffLL)
         return fail(IMI_ERR_INVALID, "imi_select_cells: key_base + n_slots must fit in 31 bits");
     if (d->static_len < 0 || d->static_len + (int64_t)d->buffer_pages * d->page_size > d->exec_capacity)
@@ -251,9 +252,10 @@ int imi_merge_candidates(const imi_merge_desc* d, void* stream) {
         !d->row_index || !d->row_count)
         return fail(IMI_ERR_INVALID, "imi_merge_candidates: null pointer");
     if (d->bg <= 0 || d->shards <= 0 || d->cap <= 0 || d->rank < 0 || d->rank >= d->shards || d->n_slots <= 0 ||
-        d->nprobe <= 0 || d->nprobe > 2048 || d->page_size <= 0 || d->static_len < 0 || d->key_base < 0)
+        d->nprobe <= 0 || d->nprobe > imi::select_max_slots() || d->page_size <= 0 || d->static_len < 0 || d->key_base < 0)
         return fail(IMI_ERR_INVALID, "imi_merge_candidates: bad sizes");
-    if (d->cap > 2049) return fail(IMI_ERR_INVALID, "imi_merge_candidates: cap (nprobe + 1) > 2049");
+    if (d->cap > imi::select_max_slots() + 1)
+        return fail(IMI_ERR_INVALID, "imi_merge_candidates: cap (nprobe + 1) too large");
     if (d->static_len + (int64_t)d->buffer_pages * d->page_size > d->exec_capacity)
         return fail(IMI_ERR_INVALID, "imi_merge_candidates: exec_capacity < static_len + buffer_pages*page_size");
     if (imi::merge_smem_bytes(*d) > 227 * 1024)

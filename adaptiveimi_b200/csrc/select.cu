@@ -313,10 +313,38 @@ __device__ __noinline__ void resolve_boundary(const unsigned long long* bk, cons
     __syncwarp();
 }
 
+// The candidates a boundary search walks: candidate c (0 <= c < ne) has key
+// key(c) (0: not a candidate) and size size(c).  DenseKeys: arrays (shared
+// memory).  RecordKeys: the shards' candidate records in global memory, as
+// the sequence-sharded merge receives them (candidate s * cap + j is entry j
+// of shard s's record; entries at or past the record's count are not
+// candidates).
+struct DenseKeys {
+    const unsigned long long* k;
+    const int* s;
+    IMI_DEV unsigned long long key(int c) const { return k[c]; }
+    IMI_DEV int size(int c) const { return s[c]; }
+};
+struct RecordKeys {
+    const unsigned long long* cand;  // shard s's record of this group at cand + s * shard_stride
+    size_t shard_stride;
+    int cap;
+    const int* counts;  // [shards] record counts (shared memory)
+    IMI_DEV unsigned long long key(int c) const {
+        const int sh = c / cap, j = c - sh * cap;
+        return j < counts[sh] ? __ldcg(cand + sh * shard_stride + j) : 0ull;
+    }
+    IMI_DEV int size(int c) const {
+        const int sh = c / cap, j = c - sh * cap;
+        return (int)__ldcg(cand + sh * shard_stride + cap + j);
+    }
+};
+
 // Refinement search for one boundary over power-of-two key ranges (the rare
 // path: a first-round boundary bucket with more than 32 elements).  All
 // threads call it; the result is left in sm.T / sm.flags.
-__device__ __noinline__ void search_one(SelHdr& sm, const unsigned long long* skey, const int* ssz, int ne,
+template <class Keys>
+__device__ __noinline__ void search_one(SelHdr& sm, const Keys& keys, int ne,
                                         unsigned long long lo, unsigned long long hi, int use_pages, SelRules r) {
     const int tid = threadIdx.x;
     long long C = 0, Sz = 0, Pg = 0;  // totals of candidates with key > hi
@@ -326,9 +354,9 @@ __device__ __noinline__ void search_one(SelHdr& sm, const unsigned long long* sk
         const int shift = bits > SL_NB_BITS ? bits - SL_NB_BITS : 0;
         hist_clear(sm);
         for (int c = tid; c < ne; c += SL_THREADS) {
-            const unsigned long long k = skey[c];
+            const unsigned long long k = keys.key(c);
             if (k == 0ull || k < lo || k > hi) continue;
-            hist_add(sm, (int)((k - lo) >> shift), ssz[c], r);
+            hist_add(sm, (int)((k - lo) >> shift), keys.size(c), r);
         }
         __syncthreads();
         BucketView v;
@@ -368,12 +396,12 @@ __device__ __noinline__ void search_one(SelHdr& sm, const unsigned long long* sk
         const unsigned long long bhi = (bend < blo || bend > hi) ? hi : bend;
         if (cnt <= 32) {
             for (int c = tid; c < ne; c += SL_THREADS) {
-                const unsigned long long k = skey[c];
+                const unsigned long long k = keys.key(c);
                 if (k == 0ull || k < blo || k > bhi) continue;
                 const int at = atomicAdd(&sm.nb, 1);
                 if (at < 32) {
                     sm.bkeys[at] = k;
-                    sm.bsz[at] = ssz[c];
+                    sm.bsz[at] = keys.size(c);
                 }
             }
             __syncthreads();
@@ -397,17 +425,18 @@ __device__ __noinline__ void search_one(SelHdr& sm, const unsigned long long* sk
 // truncation), over buckets linear in the score (equal scores share a bucket
 // and are ordered by the warp rank).  Returns false when a boundary bucket
 // holds more than 32 elements.  Results in sm.T / sm.T2.
-IMI_DEV bool search_both(SelHdr& sm, const unsigned long long* skey, const int* ssz, int ne,
+template <class Keys>
+IMI_DEV bool search_both(SelHdr& sm, const Keys& keys, int ne,
                          unsigned long long key_lo0, unsigned long long key_hi0, const SelRules& r) {
     const int tid = threadIdx.x, wid = tid >> 5;
     const float smin = sl_key_score(key_lo0), smax = sl_key_score(key_hi0);
     const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
     hist_clear(sm);
     for (int c = tid; c < ne; c += SL_THREADS) {
-        const unsigned long long k = skey[c];
+        const unsigned long long k = keys.key(c);
         if (k == 0ull) continue;
         const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
-        hist_add(sm, b, ssz[c], r);
+        hist_add(sm, b, keys.size(c), r);
     }
     __syncthreads();
     BucketView v;
@@ -446,21 +475,21 @@ IMI_DEV bool search_both(SelHdr& sm, const unsigned long long* skey, const int* 
     const int bA = hasA ? sm.bucket : -1, bB = hasB ? sm.bucket2 : -1;
     if (hasA || hasB) {
         for (int c = tid; c < ne; c += SL_THREADS) {
-            const unsigned long long k = skey[c];
+            const unsigned long long k = keys.key(c);
             if (k == 0ull) continue;
             const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
             if (b == bA) {
                 const int at = atomicAdd(&sm.nb, 1);
                 if (at < 32) {
                     sm.bkeys[at] = k;
-                    sm.bsz[at] = ssz[c];
+                    sm.bsz[at] = keys.size(c);
                 }
             }
             if (b == bB) {
                 const int at = atomicAdd(&sm.nb2, 1);
                 if (at < 32) {
                     sm.bkeys2[at] = k;
-                    sm.bsz2[at] = ssz[c];
+                    sm.bsz2[at] = keys.size(c);
                 }
             }
         }
@@ -798,18 +827,19 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 
         // ---------------- leader: the two boundaries ----------------
         if (key_hi0 != 0ull) {
-            if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
+            const DenseKeys dk{skey, ssz};
+            if (search_both(sm, dk, ne, key_lo0, key_hi0, rules)) {
                 thrA = sm.T;
                 thrB = sm.T2;
             } else {
-                search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
+                search_one(sm, dk, ne, key_lo0, key_hi0, 1, rules);
                 thrA = sm.T;
                 const bool token_or_rank = sm.flags != 0ull;
                 __syncthreads();
                 if (token_or_rank) {
                     thrB = thrA;
                 } else {
-                    search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 0, rules);
+                    search_one(sm, dk, ne, key_lo0, key_hi0, 0, rules);
                     thrB = sm.T;
                 }
             }
@@ -998,39 +1028,21 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 // part of the global selection is a prefix of its own order, so its local
 // selection under the global rules plus its stop marker cover it.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_constant__ MergeArgs a) {
-    extern __shared__ __align__(16) unsigned char dyn[];
-    SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
+// Whether the merge copies every candidate into shared memory (otherwise it
+// searches the records in global memory, where they arrived).
+__host__ __device__ inline bool merge_dense(const MergeArgs& a) {
+    return (size_t)a.shards * a.cap <= 8192;
+}
+
+template <class Keys>
+IMI_DEV void merge_select(const MergeArgs& a, SelHdr& sm, const Keys& keys, int ne, int* sel_start, int* sel_off,
+                          const SelRules& rules) {
     const int h = blockIdx.x;
     const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
     const size_t hs = h;
-    const int ne = a.shards * a.cap;
-    const int npad = (ne + 1) & ~1;
-    unsigned char* p = dyn + ((sizeof(SelHdr) + 15) & ~size_t(15));
-    unsigned long long* skey = reinterpret_cast<unsigned long long*>(p);
-    p += sizeof(unsigned long long) * npad;
-    int* ssz = reinterpret_cast<int*>(p);
-    p += sizeof(int) * npad;
-    int* sel_slot = reinterpret_cast<int*>(p);
-    int* sel_start = sel_slot + SL_SEL_MAX;
-    int* sel_off = sel_start + SL_SEL_MAX;
-    SelRules rules;
-    rules.nprobe = a.nprobe;
-    rules.max_tokens = a.max_tokens;
-    rules.buffer_pages = a.buffer_pages;
-    rules.page_size = a.page_size;
-    rules.pg_shift = __ffs(a.page_size) - 1;
-    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
-
-    const size_t rec_len = 2 * (size_t)a.cap + 1;
     unsigned long long kmn = ~0ull, kmx = 0ull;
     for (int e = tid; e < ne; e += SL_THREADS) {
-        const int s = e / a.cap, j = e - s * a.cap;
-        const unsigned long long* rec = a.cand + ((size_t)s * a.bg + hs) * rec_len;
-        const bool valid = j < (int)rec[2 * a.cap];
-        const unsigned long long k = valid ? rec[j] : 0ull;
-        skey[e] = k;
-        ssz[e] = valid && k ? (int)rec[a.cap + j] : 0;
+        const unsigned long long k = keys.key(e);
         if (k) {
             kmn = min(kmn, k);
             kmx = max(kmx, k);
@@ -1054,26 +1066,27 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
     __syncthreads();
     unsigned long long thrA = ~0ull;
     if (key_hi0 != 0ull) {
-        if (search_both(sm, skey, ssz, ne, key_lo0, key_hi0, rules)) {
+        if (search_both(sm, keys, ne, key_lo0, key_hi0, rules)) {
             thrA = sm.T;
         } else {
-            search_one(sm, skey, ssz, ne, key_lo0, key_hi0, 1, rules);
+            search_one(sm, keys, ne, key_lo0, key_hi0, 1, rules);
             thrA = sm.T;
         }
         __syncthreads();
     }
 
     // this shard's candidates sit in slot order at [rank * cap, rank * cap + count)
+    const size_t rec_len = 2 * (size_t)a.cap + 1;
     const int base = a.rank * a.cap;
     const int cnt = (int)a.cand[((size_t)a.rank * a.bg + hs) * rec_len + 2 * a.cap];
-    const int per = (cnt + SL_THREADS - 1) / SL_THREADS;  // contiguous entries per thread (<= 5)
+    const int per = (cnt + SL_THREADS - 1) / SL_THREADS;  // contiguous entries per thread
     const int e0 = min(cnt, tid * per), e1 = min(cnt, e0 + per);
     unsigned int nloc = 0, sloc = 0;
     for (int e = e0; e < e1; ++e) {
-        const unsigned long long k = skey[base + e];
+        const unsigned long long k = keys.key(base + e);
         if (k != 0ull && k > thrA) {
             ++nloc;
-            sloc += (unsigned)ssz[base + e];
+            sloc += (unsigned)keys.size(base + e);
         }
     }
     unsigned long long ix = nloc;
@@ -1088,17 +1101,14 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
         int my = (int)(ix - nloc);
         int run = a.static_len + (int)(iy - sloc);
         for (int e = e0; e < e1; ++e) {
-            const unsigned long long k = skey[base + e];
+            const unsigned long long k = keys.key(base + e);
             if (k != 0ull && k > thrA) {
                 const int slot = (int)(0xffffffffu - (uint32_t)k) - a.key_base;
                 if (my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = slot;
-                if (my < SL_SEL_MAX) {
-                    sel_slot[my] = slot;
-                    sel_start[my] = run;
-                    sel_off[my] = offs[slot];
-                }
+                sel_start[my] = run;  // my < cnt <= cap: the lists hold cap entries
+                sel_off[my] = offs[slot];
                 ++my;
-                run += ssz[base + e];
+                run += keys.size(base + e);
             }
         }
     }
@@ -1106,10 +1116,9 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
     const int ntot = sm.wsel[0], rows_sel = sm.wkept[0];
     int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
     for (int r = tid; r < a.static_len; r += SL_THREADS) rows[r] = (1 << 30) | r;
-    const int ns = min(ntot, SL_SEL_MAX);
-    for (int i = wid; i < ns; i += SL_WARPS) {
+    for (int i = wid; i < ntot; i += SL_WARPS) {
         const int s0 = sel_start[i], off = sel_off[i];
-        const int sz = (i + 1 < ns ? sel_start[i + 1] : a.static_len + rows_sel) - s0;
+        const int sz = (i + 1 < ntot ? sel_start[i + 1] : a.static_len + rows_sel) - s0;
         for (int jj = lid; jj < sz; jj += 32)
             if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
     }
@@ -1119,10 +1128,55 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
     }
 }
 
+__global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_constant__ MergeArgs a) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
+    const int h = blockIdx.x;
+    const int tid = threadIdx.x;
+    const size_t hs = h;
+    const int ne = a.shards * a.cap;
+    const bool dense = merge_dense(a);
+    const int npad = dense ? (ne + 1) & ~1 : 0;
+    unsigned char* p = dyn + ((sizeof(SelHdr) + 15) & ~size_t(15));
+    unsigned long long* skey = reinterpret_cast<unsigned long long*>(p);
+    p += sizeof(unsigned long long) * npad;
+    int* ssz = reinterpret_cast<int*>(p);
+    p += sizeof(int) * npad;
+    int* counts = reinterpret_cast<int*>(p);  // [shards]
+    p += sizeof(int) * ((a.shards + 3) & ~3);
+    int* sel_start = reinterpret_cast<int*>(p);  // [cap]
+    int* sel_off = sel_start + a.cap;            // [cap]
+    SelRules rules;
+    rules.nprobe = a.nprobe;
+    rules.max_tokens = a.max_tokens;
+    rules.buffer_pages = a.buffer_pages;
+    rules.page_size = a.page_size;
+    rules.pg_shift = __ffs(a.page_size) - 1;
+    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
+
+    const size_t rec_len = 2 * (size_t)a.cap + 1;
+    for (int sh = tid; sh < a.shards; sh += SL_THREADS)
+        counts[sh] = min(a.cap, (int)a.cand[((size_t)sh * a.bg + hs) * rec_len + 2 * a.cap]);
+    __syncthreads();
+    const RecordKeys rk{a.cand + hs * rec_len, (size_t)a.bg * rec_len, a.cap, counts};
+    if (dense) {
+        for (int e = tid; e < ne; e += SL_THREADS) {
+            const unsigned long long k = rk.key(e);
+            skey[e] = k;
+            ssz[e] = k ? rk.size(e) : 0;
+        }
+        __syncthreads();
+        merge_select(a, sm, DenseKeys{skey, ssz}, ne, sel_start, sel_off, rules);
+    } else {
+        merge_select(a, sm, rk, ne, sel_start, sel_off, rules);
+    }
+}
+
 size_t merge_smem_bytes(const MergeArgs& a) {
     const size_t ne = (size_t)a.shards * a.cap;
-    const size_t npad = (ne + 1) & ~size_t(1);
-    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + 3 * (size_t)SL_SEL_MAX * sizeof(int) + 16;
+    const size_t npad = merge_dense(a) ? (ne + 1) & ~size_t(1) : 0;
+    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + 4 * (((size_t)a.shards + 3) & ~size_t(3)) +
+           2 * (size_t)a.cap * sizeof(int) + 16;
 }
 
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {

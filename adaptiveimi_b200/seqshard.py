@@ -30,8 +30,9 @@ would need a global argmax across shards.
 ``decode_step`` runs either with one shard per process (``torch.distributed``
 initialised, NCCL all-gathers) or with every shard in one process (the
 exchange is a tensor that all shards write into), which the single-GPU tests
-use.  Limits of the on-chip selection apply: nprobe <= 2048, shard slots <=
-16384, and shards * (nprobe + 1) candidates must fit one CTA's shared memory.
+use.  Limits of the on-chip selection apply: nprobe <= 16384 and shard slots
+<= 16384.  The merge keeps up to 8192 candidates (shards * (nprobe + 1)) in
+shared memory and searches larger sets in the gathered records directly.
 """
 from __future__ import annotations
 
@@ -86,8 +87,8 @@ def plan_shards(n_total: int, shards: int, parts: int, retrieval_budget: float, 
         slots.append(RetrievalSizes.from_capacity(n, parts, retrieval_budget, buffer_cluster_num, 0,
                                                   page_size).n_centroids)
     key_base = [sum(slots[:r]) for r in range(shards)]
-    if glob.nprobe > 2048:
-        raise ValueError(f"global nprobe {glob.nprobe} > 2048 is beyond the on-chip selection")
+    if glob.nprobe > 16384:
+        raise ValueError(f"global nprobe {glob.nprobe} > 16384 is beyond the on-chip selection")
     if max(slots) > 16384:
         raise ValueError(f"{max(slots)} slots per shard > 16384: use more shards")
     return ShardPlan(shards=shards, n_total=n_total, starts=tuple(starts), lengths=tuple(lengths), ks=tuple(ks),

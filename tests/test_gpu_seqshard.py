@@ -2,6 +2,7 @@
 selection over the shards' candidates must equal the oracle's selection over
 the union of the shards' cells, and the combined attention must match an fp64
 softmax over every selected row plus the steady zone."""
+import dataclasses
 import math
 
 import numpy as np
@@ -16,11 +17,13 @@ pytestmark = pytest.mark.gpu
 ATOL_MAX, ATOL_MEAN = 2e-2, 2e-3
 
 
-def _setup(shards, heads=4, G=4, ctx=8192, seed=5):
+def _setup(shards, heads=4, G=4, ctx=8192, seed=5, nprobe=None):
     K, V, Q = make_layer(heads, heads * G, ctx, 128, 64, seed, 500000.0, n_queries=6)
     mid_k, mid_v = K[:, 32:ctx - 64], V[:, 32:ctx - 64]
     n = mid_k.shape[1]
     plan = seqshard.plan_shards(n, shards, 2, 0.1, 32)
+    if nprobe is not None:  # a rank-bound selection: every token and page allowed
+        plan = dataclasses.replace(plan, nprobe=nprobe, max_tokens=n, buffer_pages=n)
     zone_k = torch.cat([K[:, :32], K[:, ctx - 64:]], 1).contiguous()  # [heads, 96, 128]
     zone_v = torch.cat([V[:, :32], V[:, ctx - 64:]], 1).contiguous()
     local = []
@@ -34,10 +37,14 @@ def _setup(shards, heads=4, G=4, ctx=8192, seed=5):
     return K, V, Q, plan, local, zone_k, zone_v
 
 
-@pytest.mark.parametrize("shards", [1, 2, 3])
-def test_sharded_selection_and_attention_match_the_union(shards):
+@pytest.mark.parametrize("shards,nprobe", [(1, None), (2, None), (3, None), (4, 2100)])
+def test_sharded_selection_and_attention_match_the_union(shards, nprobe):
+    # (4, 2100): nprobe above 2048, and 4 * 2101 candidates, more than the
+    # merge keeps in shared memory, so it searches the gathered records
     heads, G = 4, 4
-    K, V, Q, plan, local, zone_k, zone_v = _setup(shards)
+    K, V, Q, plan, local, zone_k, zone_v = _setup(shards, nprobe=nprobe)
+    if nprobe is not None:
+        assert plan.shards * plan.cap > 8192
     zkd, zvd = zone_k.cuda(), zone_v.cuda()
     cents = [s.index.centroids.cpu().numpy() for s in local]
     masks = [s.index.cell_mask.cpu().numpy() for s in local]
