@@ -515,6 +515,132 @@ def run_reference(args):
     return res
 
 
+# ----------------------------------------------------------------------------
+# 1M context, sequence-sharded over the ranks
+# ----------------------------------------------------------------------------
+METRIC_1M = "sparse_decode_us_per_layer_step@1M"
+
+
+def run_1m(args):
+    """Every rank holds one contiguous shard of the 1M-token middle of every
+    layer, builds its IMI, and each decode step runs, per layer: local
+    selection under the global rules, an NCCL all-gather of the candidate
+    records, the global merge, attention over this shard's rows (rank 0 also
+    the steady zone, which receives the step's appended token), an NCCL
+    all-gather of the (o, m, l) partials and the log-sum-exp combine.  Each
+    timed step (all layers) is replayed from a CUDA graph captured before the
+    timed region, so the host's per-layer calls are not what is measured."""
+    import torch.distributed as dist
+
+    from adaptiveimi_b200 import seqshard
+    from adaptiveimi_b200.sharding import max_over_ranks
+    from adaptiveimi_b200.synthetic import rope
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        dist.init_process_group("nccl", init_method="env://")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    L, kvh, G, D = args.layers, CFG["kv_heads"], CFG["q_heads"] // CFG["kv_heads"], CFG["head_dim"]
+    ctx = args.context
+    static0 = CFG["static_start"] + CFG["static_end"]
+    n = ctx - static0
+    budget = 0.05
+    try:
+        plan = seqshard.plan_shards(n, ws, CFG["subspace_parts"], budget, CFG["buffer_cluster_num"])
+    except ValueError as e:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC_1M, "unavailable": f"{ctx} tokens over {ws} shard(s): {e}"}),
+                  flush=True)
+        return None
+    steps_total = args.warmup + args.steps
+    cap = static0 + steps_total + 1
+    th, C = CFG["theta"], CFG["components"]
+    shards, zk, zv, qs, nk, nv = [], [], [], [], [], []
+    t0 = time.perf_counter()
+    for l in range(L):
+        means = torch.randn(kvh, C, D, generator=torch.Generator(device=dev).manual_seed(1000 * l), device=dev)
+
+        def mix(count, positions, seed):
+            g = torch.Generator(device=dev).manual_seed(seed)
+            comp = torch.randint(0, C, (kvh, count), generator=g, device=dev)
+            x = torch.gather(means, 1, comp[..., None].expand(-1, -1, D)) + \
+                0.3 * torch.randn(kvh, count, D, generator=g, device=dev)
+            return rope(x, positions, th), torch.randn(kvh, count, D, generator=g, device=dev)
+
+        a0, ln = plan.starts[rank], plan.lengths[rank]
+        k, v = mix(ln, torch.arange(CFG["static_start"] + a0, CFG["static_start"] + a0 + ln, device=dev),
+                   1000 * l + 17 + rank)
+        s = seqshard.SeqShard(plan, rank, kvh, G, cap, dev)
+        s.build(k.to(torch.bfloat16).contiguous(), v.to(torch.bfloat16).contiguous(), **KMEANS)
+        shards.append(s)
+        del k, v
+        zpos = torch.cat([torch.arange(0, CFG["static_start"], device=dev),
+                          torch.arange(ctx - CFG["static_end"], ctx, device=dev)])
+        zkk, zvv = mix(static0, zpos, 1000 * l + 5)
+        zk.append(torch.zeros((kvh, cap, D), dtype=torch.bfloat16, device=dev))
+        zv.append(torch.zeros((kvh, cap, D), dtype=torch.bfloat16, device=dev))
+        zk[-1][:, :static0] = zkk.to(torch.bfloat16)
+        zv[-1][:, :static0] = zvv.to(torch.bfloat16)
+        qq, _ = mix(steps_total * (G + 1), torch.arange(ctx, ctx + steps_total, device=dev).repeat_interleave(G + 1),
+                    1000 * l + 9)
+        qq = qq.reshape(kvh, steps_total, G + 1, D).permute(1, 0, 2, 3).to(torch.bfloat16).contiguous()
+        qs.append(qq[:, :, :G].contiguous())                # [steps, kv, G, D]
+        nk.append(qq[:, :, G].contiguous())                 # [steps, kv, D]: the appended key
+        nv.append(torch.randn(steps_total, kvh, D, device=dev).to(torch.bfloat16))
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+
+    def step(t):
+        for l in range(L):
+            if rank == 0:  # decode append into the steady zone
+                zk[l][:, static0 + t] = nk[l][t]
+                zv[l][:, static0 + t] = nv[l][t]
+            seqshard.decode_step([shards[l]], qs[l][t], zk[l], zv[l], static0 + t + 1)
+
+    for t in range(args.warmup):
+        step(t)
+    torch.cuda.synchronize()
+    graphs = []
+    for t in range(args.warmup, steps_total):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(t)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for g in graphs:
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ms, build_s = max_over_ranks([ms, build_s], dev)
+    if rank != 0:
+        return None
+    us = ms * 1000.0 / (args.steps * L)
+    return {
+        "metric": METRIC_1M, "value": round(us, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (Gaussian-mixture keys + RoPE, N(0,1) values; seeded per layer and shard)",
+        "config": {"workload": f"BASELINE configs[2]: {ctx} tokens sequence-sharded {ws}-way, per-shard IMI S=2, "
+                               f"global budget {budget}, {L} layers, one append per step",
+                   "context": ctx, "layers": L, "kv_heads": kvh, "q_heads": CFG["q_heads"], "shards": ws,
+                   "nprobe": plan.nprobe, "budget_tokens": plan.max_tokens, "slots_per_shard": list(plan.n_slots),
+                   "parallelism": f"sequence shards x{ws}, NCCL all-gathers of candidates and partials",
+                   "timing": "CUDA-graph replay of each whole step, device events, max over ranks"},
+        "build_s_max": round(build_s, 3),
+        "clocks": clk.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -522,9 +648,27 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=CFG["layers"])
-    ap.add_argument("--context", type=int, default=CFG["context"])
+    ap.add_argument("--context", type=int, default=None, help="default: 131072 (128k) or 1048576 (1m)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="128k", choices=["128k", "1m"],
+                    help="1m: BASELINE configs[2], the 1M context sequence-sharded over the ranks")
     args = ap.parse_args()
+    if args.context is None:
+        args.context = 1_048_576 if args.workload == "1m" else CFG["context"]
+    if args.workload == "1m":
+        if args.impl == "reference":
+            ws, rank, _ = dist_env()
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "metric": METRIC_1M,
+                                  "unavailable": "the reference's CPU decode path at 1M context is not sampled"}),
+                      flush=True)
+            return
+        if args.warmup < 3:
+            args.warmup = 3
+        res = run_1m(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.steps + args.warmup + 8 > CFG["max_new_length"] - 1:
