@@ -80,6 +80,11 @@ class CombineDesc(ctypes.Structure):
                 ("out", P)]
 
 
+class PeerGatherDesc(ctypes.Structure):
+    _fields_ = [("world", i32), ("rank", i32), ("bytes", i64), ("src_peers", P), ("flag_peers", P), ("epoch", P),
+                ("ticket", P), ("dst", P), ("status", P)]
+
+
 class AppendDesc(ctypes.Structure):
     _fields_ = [
         ("bg", i32), ("dim", i32),
@@ -114,7 +119,7 @@ EXPORTS = (
     "imi_abi_version", "imi_last_error", "imi_build_workspace_size", "imi_build_index",
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
     "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_decode_layer",
-    "imi_merge_candidates", "imi_combine_partials", "imi_sparse_attention_noalloc",
+    "imi_merge_candidates", "imi_combine_partials", "imi_sparse_attention_noalloc", "imi_peer_allgather",
 )
 
 _lib = None
@@ -152,6 +157,7 @@ def load():
                                         ctypes.POINTER(ApplyDesc), P]
         L.imi_merge_candidates.argtypes = [ctypes.POINTER(MergeDesc), P]
         L.imi_combine_partials.argtypes = [ctypes.POINTER(CombineDesc), P]
+        L.imi_peer_allgather.argtypes = [ctypes.POINTER(PeerGatherDesc), P]
         L.imi_decode_layer.argtypes = [ctypes.POINTER(AppendDesc), ctypes.POINTER(AsyncDesc),
                                        ctypes.POINTER(ApplyDesc), ctypes.POINTER(SelectDesc),
                                        ctypes.POINTER(AttnDesc), P]

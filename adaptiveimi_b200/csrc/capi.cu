@@ -272,6 +272,16 @@ int imi_combine_partials(const imi_combine_desc* d, void* stream) {
     return cuda_status(imi::launch_combine_shards(*d, S(stream)), "imi_combine_partials");
 }
 
+int imi_peer_allgather(const imi_peer_gather_desc* d, void* stream) {
+    if (!d || !d->src_peers || !d->flag_peers || !d->epoch || !d->ticket || !d->dst)
+        return fail(IMI_ERR_INVALID, "imi_peer_allgather: null pointer");
+    if (d->world <= 0 || d->world > 64 || d->rank < 0 || d->rank >= d->world || d->bytes <= 0 || d->bytes % 16 != 0 ||
+        !aligned16(d->dst))
+        return fail(IMI_ERR_INVALID, "imi_peer_allgather: need 0 <= rank < world <= 64, bytes a positive multiple of 16, "
+                                     "dst 16-byte aligned");
+    return cuda_status(imi::launch_peer_allgather(*d, S(stream)), "imi_peer_allgather");
+}
+
 int imi_decode_append(const imi_append_desc* d, void* stream) {
     const int st = check_append(d);
     if (st != IMI_OK) return st;

@@ -20,6 +20,7 @@ using ApplyArgs = imi_apply_desc;
 using BuildArgs = imi_build_desc;
 using MergeArgs = imi_merge_desc;
 using CombineArgs = imi_combine_desc;
+using PeerGatherArgs = imi_peer_gather_desc;
 
 cudaError_t launch_similarity(const uint16_t* q, const float* cent, float* out, int bg, int G, int n_cells, int dim,
                               long long out_stride, cudaStream_t st);
@@ -33,6 +34,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
 size_t merge_smem_bytes(const MergeArgs& a);
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
 cudaError_t launch_combine_shards(const CombineArgs& a, cudaStream_t st);
+cudaError_t launch_peer_allgather(const PeerGatherArgs& a, cudaStream_t st);
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t st);
 size_t async_smem_bytes(const AsyncArgs& a);
 cudaError_t launch_async_assign(const AsyncArgs& a, cudaStream_t st);

@@ -137,6 +137,55 @@ class SeqShard:
                                      early_stop_rel_tol=early_stop_rel_tol)
         self.slot_bound = int(self.index.n_active.max().item())
 
+    # -- exchange over NVLink peer memory ---------------------------------------
+    def enable_peer_exchange(self, group=None) -> bool:
+        """Put this shard's candidate record and partials block in symmetric
+        memory (mapped by every rank of `group`, one shard per rank) and
+        exchange them with imi_peer_allgather instead of NCCL all-gathers.
+        Collective over the group; returns False (NCCL stays) when the block
+        sizes do not allow it."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        g = group if group is not None else dist.group.WORLD
+        world, rank = dist.get_world_size(g), dist.get_rank(g)
+        if world != self.plan.shards or rank != self.rank or (self.cand.numel() * 8) % 16 != 0:
+            return False
+        name = g.group_name
+        symm.enable_symm_mem_for_group(name)
+        cand = symm.empty(tuple(self.cand.shape), dtype=torch.int64, device=self.dev)
+        part = symm.empty(tuple(self.partials.shape), dtype=torch.float32, device=self.dev)
+        flags = symm.empty((2, world), dtype=torch.int32, device=self.dev)
+        cand.zero_()
+        flags.zero_()
+        hc, hp, hf = symm.rendezvous(cand, name), symm.rendezvous(part, name), symm.rendezvous(flags, name)
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=g)  # every rank's flags are zero before any exchange
+        i64 = torch.int64
+        fp = [int(x) for x in hf.buffer_ptrs]
+        self.cand, self.partials = cand, part
+        self._peer = dict(
+            world=world, handles=(hc, hp, hf), keep=(cand, part, flags),
+            src=(torch.tensor([int(x) for x in hc.buffer_ptrs], dtype=i64, device=self.dev),
+                 torch.tensor([int(x) for x in hp.buffer_ptrs], dtype=i64, device=self.dev)),
+            flags=(torch.tensor(fp, dtype=i64, device=self.dev),
+                   torch.tensor([x + 4 * world for x in fp], dtype=i64, device=self.dev)),
+            counters=torch.zeros((2, 2), dtype=torch.int32, device=self.dev),  # per channel: epoch, ticket
+            status=torch.zeros((1,), dtype=torch.int32, device=self.dev),
+            bytes=(self.cand.numel() * 8, self.partials.numel() * 4))
+        return True
+
+    def peer_allgather(self, channel: int, dst: torch.Tensor) -> None:
+        """Channel 0: the candidate records; 1: the partials block."""
+        pe = self._peer
+        d = _lib.PeerGatherDesc()
+        d.world, d.rank, d.bytes = pe["world"], self.rank, pe["bytes"][channel]
+        d.src_peers, d.flag_peers = pe["src"][channel].data_ptr(), pe["flags"][channel].data_ptr()
+        d.epoch = pe["counters"].data_ptr() + 8 * channel
+        d.ticket = d.epoch + 4
+        d.dst, d.status = dst.data_ptr(), pe["status"].data_ptr()
+        _lib.check(_lib.load().imi_peer_allgather(ctypes.byref(d), ops._stream(self.dev)), "imi_peer_allgather")
+
     # -- decode ---------------------------------------------------------------
     def select_local(self, q: torch.Tensor, cand_out: Optional[torch.Tensor] = None) -> None:
         """Local selection under the global rules; candidates into cand_out
@@ -230,11 +279,18 @@ def decode_step(local: Sequence[SeqShard], q: torch.Tensor, zone_keys: Optional[
     if len(local) != 1:
         raise ValueError("pass every shard, or this process's one shard")
     s = local[0]
+    peer = getattr(s, "_peer", None) is not None
     s.select_local(q)
     cand_all = torch.empty((plan.shards, bg, plan.record), dtype=torch.int64, device=dev)
-    torch.distributed.all_gather_into_tensor(cand_all, s.cand, group=group)
+    if peer:
+        s.peer_allgather(0, cand_all)
+    else:
+        torch.distributed.all_gather_into_tensor(cand_all, s.cand, group=group)
     s.merge(cand_all, static_len)
     s.attend(q, zone_keys, zone_values)
     parts_all = torch.empty((plan.shards, s.partials.numel()), dtype=torch.float32, device=dev)
-    torch.distributed.all_gather_into_tensor(parts_all, s.partials, group=group)
+    if peer:
+        s.peer_allgather(1, parts_all)
+    else:
+        torch.distributed.all_gather_into_tensor(parts_all, s.partials, group=group)
     return combine(parts_all, plan.shards, bg, G, out)

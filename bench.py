@@ -524,10 +524,10 @@ METRIC_1M = "sparse_decode_us_per_layer_step@1M"
 def run_1m(args):
     """Every rank holds one contiguous shard of the 1M-token middle of every
     layer, builds its IMI, and each decode step runs, per layer: local
-    selection under the global rules, an NCCL all-gather of the candidate
-    records, the global merge, attention over this shard's rows (rank 0 also
-    the steady zone, which receives the step's appended token), an NCCL
-    all-gather of the (o, m, l) partials and the log-sum-exp combine.  Each
+    selection under the global rules, an exchange of the candidate records
+    (imi_peer_allgather over NVLink peer memory), the global merge, attention over this shard's rows (rank 0 also
+    the steady zone, which receives the step's appended token), an exchange
+    of the (o, m, l) partials and the log-sum-exp combine.  Each
     timed step (all layers) is replayed from a CUDA graph captured before the
     timed region, so the host's per-layer calls are not what is measured."""
     import torch.distributed as dist
@@ -573,6 +573,8 @@ def run_1m(args):
                    1000 * l + 17 + rank)
         s = seqshard.SeqShard(plan, rank, kvh, G, cap, dev)
         s.build(k.to(torch.bfloat16).contiguous(), v.to(torch.bfloat16).contiguous(), **KMEANS)
+        if ws > 1 and not s.enable_peer_exchange():
+            raise SystemExit("peer-memory exchange unavailable for this geometry")
         shards.append(s)
         del k, v
         zpos = torch.cat([torch.arange(0, CFG["static_start"], device=dev),
@@ -621,6 +623,8 @@ def run_1m(args):
     if ws > 1:
         dist.barrier()
     ms = e0.elapsed_time(e1)
+    if ws > 1 and any(int(s._peer["status"].item()) for s in shards):
+        raise SystemExit("a peer exchange timed out")
     ms, build_s = max_over_ranks([ms, build_s], dev)
     if rank != 0:
         return None
@@ -634,7 +638,8 @@ def run_1m(args):
                                f"global budget {budget}, {L} layers, one append per step",
                    "context": ctx, "layers": L, "kv_heads": kvh, "q_heads": CFG["q_heads"], "shards": ws,
                    "nprobe": plan.nprobe, "budget_tokens": plan.max_tokens, "slots_per_shard": list(plan.n_slots),
-                   "parallelism": f"sequence shards x{ws}, NCCL all-gathers of candidates and partials",
+                   "parallelism": f"sequence shards x{ws}, candidates and partials exchanged over NVLink peer memory "
+                                  "(imi_peer_allgather)",
                    "timing": "CUDA-graph replay of each whole step, device events, max over ranks"},
         "build_s_max": round(build_s, 3),
         "clocks": clk.summary(),

@@ -199,6 +199,25 @@ typedef struct imi_combine_desc {
     void* out;                             /* [bg, G, 128] bf16 */
 } imi_combine_desc;
 
+/* Sequence sharding: all-gather of one block per rank over NVLink peer memory
+ * (no counterpart in the reference).  src_peers[r] is rank r's source block
+ * (bytes long, 16-byte aligned) as mapped on this GPU; flag_peers[r] is rank
+ * r's array of `world` flag words as mapped on this GPU (zero before the
+ * first call); epoch and ticket are this rank's own counters (zero before the
+ * first call, advanced by the kernel).  Both arrays live in device memory.
+ * dst receives [world][bytes].  A peer that does not arrive within about a
+ * second sets bit 0 of *status. */
+typedef struct imi_peer_gather_desc {
+    int32_t world, rank;
+    int64_t bytes;                         /* per rank, a multiple of 16 */
+    const void* const* src_peers;          /* [world] device array of peer pointers */
+    uint32_t* const* flag_peers;           /* [world] device array of peer pointers */
+    uint32_t* epoch;                       /* [1] this rank's exchange counter */
+    uint32_t* ticket;                      /* [1] scratch, zero between calls */
+    void* dst;                             /* [world, bytes] */
+    int32_t* status;                       /* [1] or NULL */
+} imi_peer_gather_desc;
+
 typedef struct imi_append_desc {
     int32_t bg, dim;
     const void* new_keys;                  /* group h at new_keys + h*src_head_stride elements */
@@ -286,6 +305,7 @@ IMI_API int imi_decode_append(const imi_append_desc* desc, void* stream);
  * the global candidate merge and the partial combine. */
 IMI_API int imi_merge_candidates(const imi_merge_desc* desc, void* stream);
 IMI_API int imi_combine_partials(const imi_combine_desc* desc, void* stream);
+IMI_API int imi_peer_allgather(const imi_peer_gather_desc* desc, void* stream);
 IMI_API int imi_async_assign(const imi_async_desc* desc, void* stream);
 IMI_API int imi_apply_updates(const imi_apply_desc* desc, void* stream);
 

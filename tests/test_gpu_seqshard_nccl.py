@@ -1,5 +1,6 @@
-"""Sequence sharding across real GPUs: one shard per process, NCCL
-all-gathers of the candidate records and the attention partials.  Every rank
+"""Sequence sharding across real GPUs: one shard per process, the candidate
+records and the attention partials exchanged by NCCL all-gathers or by
+imi_peer_allgather over NVLink peer memory.  Every rank
 also runs all the shards in-process (no collective) and must get the same
 output.  Needs at least two GPUs (skipped otherwise)."""
 import os
@@ -17,7 +18,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, ws, port, q):
+def _worker(rank, ws, port, q, peer):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
 
@@ -40,6 +41,8 @@ def _worker(rank, ws, port, q):
             s.build(mid_k[:, a:b].contiguous().to(dev), mid_v[:, a:b].contiguous().to(dev), max_iters=6,
                     early_stop_min_iter=6, tol=0.0, early_stop_rel_tol=0.0)
             shards.append(s)
+        if peer:
+            assert shards[rank].enable_peer_exchange()
         worst = 0.0
         for t in range(Q.shape[0]):
             qd = Q[t].reshape(heads, G, 128).contiguous().to(dev)
@@ -47,19 +50,22 @@ def _worker(rank, ws, port, q):
             ref = seqshard.decode_step(shards, qd, zk, zv, 96)
             torch.cuda.synchronize()
             worst = max(worst, float((got.float() - ref.float()).abs().max()))
+        if peer:
+            assert int(shards[rank]._peer["status"].item()) == 0
         q.put((rank, worst))
     finally:
         dist.destroy_process_group()
 
 
-def test_two_ranks_match_in_process_shards():
+@pytest.mark.parametrize("peer", [False, True])
+def test_two_ranks_match_in_process_shards(peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ws, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, ws, port, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, q, peer)) for r in range(ws)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(ws))
