@@ -320,12 +320,14 @@ __device__ __noinline__ void resolve_boundary(const unsigned long long* bk, cons
 // of shard s's record; entries at or past the record's count are not
 // candidates).
 struct DenseKeys {
+    static constexpr int kBatch = 1;  // shared memory: no latency to hide
     const unsigned long long* k;
     const int* s;
     IMI_DEV unsigned long long key(int c) const { return k[c]; }
     IMI_DEV int size(int c) const { return s[c]; }
 };
 struct RecordKeys {
+    static constexpr int kBatch = 8;  // global memory: loads in flight per thread
     const unsigned long long* cand;  // shard s's record of this group at cand + s * shard_stride
     size_t shard_stride;
     int cap;
@@ -340,6 +342,32 @@ struct RecordKeys {
     }
 };
 
+// Visit the candidates [0, ne) in batches of Keys::kBatch per thread: the
+// keys and sizes of a batch are loaded before f runs on any of them, so
+// passes over candidates in global memory keep that many loads in flight
+// instead of waiting for each one behind the shared-memory atomics.
+template <class Keys, class F>
+IMI_DEV void for_candidates(const Keys& keys, int ne, F&& f) {
+    constexpr int SL_BATCH = Keys::kBatch;
+    for (int c0 = threadIdx.x; c0 < ne; c0 += SL_BATCH * SL_THREADS) {
+        unsigned long long k[SL_BATCH];
+        int z[SL_BATCH];
+#pragma unroll
+        for (int u = 0; u < SL_BATCH; ++u) {
+            const int c = c0 + u * SL_THREADS;
+            k[u] = c < ne ? keys.key(c) : 0ull;
+        }
+#pragma unroll
+        for (int u = 0; u < SL_BATCH; ++u) {  // unconditional: one round of loads, not two
+            const int c = c0 + u * SL_THREADS;
+            z[u] = c < ne ? keys.size(c) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < SL_BATCH; ++u)
+            if (k[u]) f(k[u], z[u]);
+    }
+}
+
 // Refinement search for one boundary over power-of-two key ranges (the rare
 // path: a first-round boundary bucket with more than 32 elements).  All
 // threads call it; the result is left in sm.T / sm.flags.
@@ -353,11 +381,9 @@ __device__ __noinline__ void search_one(SelHdr& sm, const Keys& keys, int ne,
         const int bits = span ? 64 - __clzll(span) : 0;
         const int shift = bits > SL_NB_BITS ? bits - SL_NB_BITS : 0;
         hist_clear(sm);
-        for (int c = tid; c < ne; c += SL_THREADS) {
-            const unsigned long long k = keys.key(c);
-            if (k == 0ull || k < lo || k > hi) continue;
-            hist_add(sm, (int)((k - lo) >> shift), keys.size(c), r);
-        }
+        for_candidates(keys, ne, [&](unsigned long long k, int z) {
+            if (k >= lo && k <= hi) hist_add(sm, (int)((k - lo) >> shift), z, r);
+        });
         __syncthreads();
         BucketView v;
         hist_view(sm, C, Sz, Pg, v);
@@ -395,15 +421,14 @@ __device__ __noinline__ void search_one(SelHdr& sm, const Keys& keys, int ne,
         const unsigned long long bend = blo + ((1ull << shift) - 1ull);
         const unsigned long long bhi = (bend < blo || bend > hi) ? hi : bend;
         if (cnt <= 32) {
-            for (int c = tid; c < ne; c += SL_THREADS) {
-                const unsigned long long k = keys.key(c);
-                if (k == 0ull || k < blo || k > bhi) continue;
+            for_candidates(keys, ne, [&](unsigned long long k, int z) {
+                if (k < blo || k > bhi) return;
                 const int at = atomicAdd(&sm.nb, 1);
                 if (at < 32) {
                     sm.bkeys[at] = k;
-                    sm.bsz[at] = keys.size(c);
+                    sm.bsz[at] = z;
                 }
-            }
+            });
             __syncthreads();
             if ((tid >> 5) == 0)
                 resolve_boundary(sm.bkeys, sm.bsz, min(sm.nb, 32), qc, qsz, qp, use_pages, blo, sm.rscr[0], r,
@@ -432,12 +457,9 @@ IMI_DEV bool search_both(SelHdr& sm, const Keys& keys, int ne,
     const float smin = sl_key_score(key_lo0), smax = sl_key_score(key_hi0);
     const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
     hist_clear(sm);
-    for (int c = tid; c < ne; c += SL_THREADS) {
-        const unsigned long long k = keys.key(c);
-        if (k == 0ull) continue;
-        const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
-        hist_add(sm, b, keys.size(c), r);
-    }
+    for_candidates(keys, ne, [&](unsigned long long k, int z) {
+        hist_add(sm, min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale))), z, r);
+    });
     __syncthreads();
     BucketView v;
     hist_view(sm, 0, 0, 0, v);
@@ -474,25 +496,23 @@ IMI_DEV bool search_both(SelHdr& sm, const Keys& keys, int ne,
     }
     const int bA = hasA ? sm.bucket : -1, bB = hasB ? sm.bucket2 : -1;
     if (hasA || hasB) {
-        for (int c = tid; c < ne; c += SL_THREADS) {
-            const unsigned long long k = keys.key(c);
-            if (k == 0ull) continue;
+        for_candidates(keys, ne, [&](unsigned long long k, int z) {
             const int b = min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale)));
             if (b == bA) {
                 const int at = atomicAdd(&sm.nb, 1);
                 if (at < 32) {
                     sm.bkeys[at] = k;
-                    sm.bsz[at] = keys.size(c);
+                    sm.bsz[at] = z;
                 }
             }
             if (b == bB) {
                 const int at = atomicAdd(&sm.nb2, 1);
                 if (at < 32) {
                     sm.bkeys2[at] = k;
-                    sm.bsz2[at] = keys.size(c);
+                    sm.bsz2[at] = z;
                 }
             }
-        }
+        });
     }
     __syncthreads();
     // warp 0 resolves A, warp 1 resolves B (one shared copy of the code); a
@@ -1041,13 +1061,10 @@ IMI_DEV void merge_select(const MergeArgs& a, SelHdr& sm, const Keys& keys, int 
     const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
     const size_t hs = h;
     unsigned long long kmn = ~0ull, kmx = 0ull;
-    for (int e = tid; e < ne; e += SL_THREADS) {
-        const unsigned long long k = keys.key(e);
-        if (k) {
-            kmn = min(kmn, k);
-            kmx = max(kmx, k);
-        }
-    }
+    for_candidates(keys, ne, [&](unsigned long long k, int) {
+        kmn = min(kmn, k);
+        kmx = max(kmx, k);
+    });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         kmn = min(kmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmn, o));
