@@ -327,7 +327,7 @@ struct DenseKeys {
     IMI_DEV int size(int c) const { return s[c]; }
 };
 struct RecordKeys {
-    static constexpr int kBatch = 8;  // global memory: loads in flight per thread
+    static constexpr int kBatch = 1;  // (eight in flight measured slower on the 1M merge)
     const unsigned long long* cand;  // shard s's record of this group at cand + s * shard_stride
     size_t shard_stride;
     int cap;
@@ -373,9 +373,10 @@ IMI_DEV void for_candidates(const Keys& keys, int ne, F&& f) {
 // threads call it; the result is left in sm.T / sm.flags.
 template <class Keys>
 __device__ __noinline__ void search_one(SelHdr& sm, const Keys& keys, int ne,
-                                        unsigned long long lo, unsigned long long hi, int use_pages, SelRules r) {
+                                        unsigned long long lo, unsigned long long hi, int use_pages, SelRules r,
+                                        long long C0 = 0, long long S0 = 0, long long P0 = 0) {
     const int tid = threadIdx.x;
-    long long C = 0, Sz = 0, Pg = 0;  // totals of candidates with key > hi
+    long long C = C0, Sz = S0, Pg = P0;  // totals of candidates with key > hi (some may lie outside `keys`)
     while (true) {
         const unsigned long long span = hi - lo;
         const int bits = span ? 64 - __clzll(span) : 0;
@@ -1050,13 +1051,17 @@ __global__ void __cluster_dims__(SL_CL, 1, 1) __launch_bounds__(SL_THREADS, 1)
 // ---------------------------------------------------------------------------
 // Whether the merge copies every candidate into shared memory (otherwise it
 // searches the records in global memory, where they arrived).
+constexpr int MERGE_LIST = 8192;  // boundary-bucket candidates the non-dense merge refines in shared memory
 __host__ __device__ inline bool merge_dense(const MergeArgs& a) {
     return (size_t)a.shards * a.cap <= 8192;
 }
 
+// list_k / list_s (list_cap entries, shared memory, or null): room for the
+// boundary bucket's candidates when the first round cannot resolve it.
 template <class Keys>
 IMI_DEV void merge_select(const MergeArgs& a, SelHdr& sm, const Keys& keys, int ne, int* sel_start, int* sel_off,
-                          const SelRules& rules) {
+                          const SelRules& rules, unsigned long long* list_k = nullptr, int* list_s = nullptr,
+                          int list_cap = 0) {
     const int h = blockIdx.x;
     const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
     const size_t hs = h;
@@ -1084,6 +1089,46 @@ IMI_DEV void merge_select(const MergeArgs& a, SelHdr& sm, const Keys& keys, int 
     unsigned long long thrA = ~0ull;
     if (key_hi0 != 0ull) {
         if (search_both(sm, keys, ne, key_lo0, key_hi0, rules)) {
+            thrA = sm.T;
+        } else if (list_k != nullptr && sm.first < SL_NB && sm.bcnt <= list_cap) {
+            // Boundary A's first-round bucket is too full to resolve at once:
+            // copy its candidates into shared memory and refine there, from
+            // the first round's totals above that bucket, instead of passing
+            // over every record again per round.
+            const int bA = sm.bucket;
+            const long long qc = sm.pre[0], qs = sm.pre[1], qp = sm.pre[2];
+            __shared__ int s_nl;
+            if (tid == 0) s_nl = 0;
+            __syncthreads();
+            const float smin = sl_key_score(key_lo0), smax = sl_key_score(key_hi0);
+            const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
+            unsigned long long lmn = ~0ull, lmx = 0ull;
+            for_candidates(keys, ne, [&](unsigned long long k, int z) {
+                if (min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale))) != bA) return;
+                const int at = atomicAdd(&s_nl, 1);
+                list_k[at] = k;
+                list_s[at] = z;
+                lmn = min(lmn, k);
+                lmx = max(lmx, k);
+            });
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                lmn = min(lmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, lmn, o));
+                lmx = max(lmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, lmx, o));
+            }
+            if (lid == 0) {
+                sm.rscr[0][wid] = lmn;
+                sm.rscr[1][wid] = lmx;
+            }
+            __syncthreads();
+            unsigned long long llo = ~0ull, lhi = 0ull;
+            for (int q = 0; q < SL_WARPS; ++q) {
+                llo = min(llo, sm.rscr[0][q]);
+                lhi = max(lhi, sm.rscr[1][q]);
+            }
+            const int nl = s_nl;
+            __syncthreads();
+            search_one(sm, DenseKeys{list_k, list_s}, nl, llo, lhi, 1, rules, qc, qs, qp);
             thrA = sm.T;
         } else {
             search_one(sm, keys, ne, key_lo0, key_hi0, 1, rules);
@@ -1163,6 +1208,10 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
     p += sizeof(int) * ((a.shards + 3) & ~3);
     int* sel_start = reinterpret_cast<int*>(p);  // [cap]
     int* sel_off = sel_start + a.cap;            // [cap]
+    p += 2 * sizeof(int) * (((size_t)a.cap + 1) & ~size_t(1));
+    // non-dense: room for one first-round bucket's candidates
+    unsigned long long* list_k = dense ? nullptr : reinterpret_cast<unsigned long long*>(p);  // [MERGE_LIST]
+    int* list_s = dense ? nullptr : reinterpret_cast<int*>(list_k + MERGE_LIST);             // [MERGE_LIST]
     SelRules rules;
     rules.nprobe = a.nprobe;
     rules.max_tokens = a.max_tokens;
@@ -1185,7 +1234,273 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_kernel(const __grid_c
         __syncthreads();
         merge_select(a, sm, DenseKeys{skey, ssz}, ne, sel_start, sel_off, rules);
     } else {
-        merge_select(a, sm, rk, ne, sel_start, sel_off, rules);
+        merge_select(a, sm, rk, ne, sel_start, sel_off, rules, list_k, list_s, MERGE_LIST);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Cluster merge (shards <= 8): CTA r of a group's cluster holds shard r's
+// candidate record in its own shared memory.  Every CTA histograms its own
+// candidates over the common score range; the leader sums the histograms
+// through DSMEM and finds the bucket where a rule fires; the CTAs hand the
+// leader that bucket's candidates through DSMEM; the leader resolves the
+// boundary (refining in shared memory when the bucket is large) and the CTA
+// holding this rank's shard writes its selected cells and row list.  Each CTA
+// touches one shard's candidates, so the passes are 1/shards of a one-CTA
+// merge's.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int cmerge_list_cap(int cap) {
+    // what is left of 227 KB after the header, the shard's candidates and the emission lists
+    const long long used = ((long long)sizeof(SelHdr) + 15) / 16 * 16 + 12LL * cap + 8LL * cap + 256;
+    const long long room = (long long)(227 * 1024 - 1024) - used;
+    return (int)(room > 12 * 32 ? room / 12 : 32);
+}
+
+size_t cmerge_smem_bytes(const MergeArgs& a) {
+    return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * (size_t)a.cap + 8 * (size_t)a.cap + 256 +
+           12 * (size_t)cmerge_list_cap(a.cap);
+}
+
+__global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_cluster_kernel(const __grid_constant__ MergeArgs a) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    SelHdr& sm = *reinterpret_cast<SelHdr*>(dyn);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int r = (int)cluster.block_rank();  // = the shard this CTA holds
+    const int h = blockIdx.y;
+    const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
+    const size_t hs = h;
+    const int cap = a.cap, list_cap = cmerge_list_cap(cap);
+    unsigned char* p = dyn + ((sizeof(SelHdr) + 15) & ~size_t(15));
+    unsigned long long* ck = reinterpret_cast<unsigned long long*>(p);  // [cap] this shard's keys
+    p += 8 * (size_t)cap;
+    int* cs = reinterpret_cast<int*>(p);  // [cap] sizes
+    p += 4 * (size_t)cap;
+    int* sel_start = reinterpret_cast<int*>(p);  // [cap]
+    int* sel_off = sel_start + cap;              // [cap]
+    p += 8 * (size_t)cap;
+    p = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+    unsigned long long* list_k = reinterpret_cast<unsigned long long*>(p);  // [list_cap] leader
+    int* list_s = reinterpret_cast<int*>(list_k + list_cap);
+    __shared__ unsigned long long c_lo[SL_CL], c_hi[SL_CL];  // leader: every CTA's key range
+    __shared__ int c_bucket, c_nl, c_counts[SL_CL];
+    __shared__ unsigned long long c_thr;
+    SelRules rules;
+    rules.nprobe = a.nprobe;
+    rules.max_tokens = a.max_tokens;
+    rules.buffer_pages = a.buffer_pages;
+    rules.page_size = a.page_size;
+    rules.pg_shift = __ffs(a.page_size) - 1;
+    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
+
+    // ---- this shard's candidates (entries in slot order) and their key range
+    const size_t rec_len = 2 * (size_t)cap + 1;
+    const unsigned long long* rec = a.cand + ((size_t)r * a.bg + hs) * rec_len;
+    const int cnt = min(cap, (int)rec[2 * (size_t)cap]);
+    unsigned long long kmn = ~0ull, kmx = 0ull;
+    for (int j = tid; j < cnt; j += SL_THREADS) {
+        const unsigned long long k = __ldcg(rec + j);
+        ck[j] = k;
+        cs[j] = (int)__ldcg(rec + cap + j);
+        if (k) {
+            kmn = min(kmn, k);
+            kmx = max(kmx, k);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmn = min(kmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmn, o));
+        kmx = max(kmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    if (lid == 0) {
+        sm.rscr[0][wid] = kmn;
+        sm.rscr[1][wid] = kmx;
+    }
+    hist_clear(sm);  // (its barrier also publishes rscr)
+    if (tid == 0) {
+        unsigned long long lo = ~0ull, hi = 0ull;
+        for (int q = 0; q < SL_WARPS; ++q) {
+            lo = min(lo, sm.rscr[0][q]);
+            hi = max(hi, sm.rscr[1][q]);
+        }
+        unsigned long long* llo = cluster.map_shared_rank(c_lo, 0);
+        unsigned long long* lhi = cluster.map_shared_rank(c_hi, 0);
+        llo[r] = lo;
+        lhi[r] = hi;
+        cluster.map_shared_rank(c_counts, 0)[r] = cnt;
+        if (r == 0) c_nl = 0;
+    }
+    cluster.sync();  // #1: every range is in the leader
+    unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
+    {
+        const unsigned long long* llo = cluster.map_shared_rank(c_lo, 0);
+        const unsigned long long* lhi = cluster.map_shared_rank(c_hi, 0);
+        for (int q = 0; q < (int)cluster.num_blocks(); ++q) {
+            key_lo0 = min(key_lo0, llo[q]);
+            key_hi0 = max(key_hi0, lhi[q]);
+        }
+    }
+    const float smin = sl_key_score(key_lo0), smax = sl_key_score(key_hi0);
+    const float scale = smax > smin ? (float)(SL_NB - 1) / (smax - smin) : 0.0f;
+    auto bin = [&](unsigned long long k) { return min(SL_NB - 1, max(0, (int)((sl_key_score(k) - smin) * scale))); };
+    if (key_hi0 != 0ull) {
+        for (int j = tid; j < cnt; j += SL_THREADS)
+            if (ck[j]) hist_add(sm, bin(ck[j]), cs[j], rules);
+    }
+    cluster.sync();  // #2: every local histogram is complete
+    if (r == 0 && key_hi0 != 0ull) {
+        // the cluster's histogram into the leader's
+        for (int b = tid; b < SL_NB; b += SL_THREADS) {
+            unsigned long long x = sm.hcp[b];
+            unsigned int w = sm.hsz[b];
+            for (int q = 1; q < (int)cluster.num_blocks(); ++q) {
+                const SelHdr* o = cluster.map_shared_rank(&sm, q);
+                x += o->hcp[b];
+                w += o->hsz[b];
+            }
+            sm.hcp[b] = x;
+            sm.hsz[b] = w;
+        }
+        __syncthreads();
+        BucketView v;
+        hist_view(sm, 0, 0, 0, v);
+        {
+            long long ec = v.ec, es = v.es, ep = v.ep;
+            bool done = false;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (!done && v.cv[q] > 0 &&
+                    ((ec + v.cv[q] > rules.nprobe) || (es + v.sv[q] >= rules.max_tokens) ||
+                     (ep + v.pv[q] > rules.buffer_pages))) {
+                    atomicMin(&sm.first, 4 * tid + q);
+                    done = true;
+                }
+                ec += v.cv[q];
+                es += v.sv[q];
+                ep += v.pv[q];
+            }
+        }
+        __syncthreads();
+        const int fr = sm.first;
+        if (fr < SL_NB && (fr >> 2) == tid) view_publish(v, fr, &sm.bucket, &sm.bcnt, sm.pre);
+        __syncthreads();
+        if (tid < (int)cluster.num_blocks())
+            *cluster.map_shared_rank(&c_bucket, tid) = fr < SL_NB ? sm.bucket : -1;
+    }
+    if (r == 0 && key_hi0 == 0ull && tid < (int)cluster.num_blocks()) *cluster.map_shared_rank(&c_bucket, tid) = -1;
+    cluster.sync();  // #3: the boundary bucket is known everywhere
+    const int bA = c_bucket;
+    if (bA >= 0) {  // that bucket's candidates into the leader's list
+        int* lnl = cluster.map_shared_rank(&c_nl, 0);
+        unsigned long long* lk = cluster.map_shared_rank(list_k, 0);
+        int* ls = cluster.map_shared_rank(list_s, 0);
+        for (int j = tid; j < cnt; j += SL_THREADS) {
+            const unsigned long long k = ck[j];
+            if (k == 0ull || bin(k) != bA) continue;
+            const int at = atomicAdd(lnl, 1);
+            if (at < list_cap) {
+                lk[at] = k;
+                ls[at] = cs[j];
+            }
+        }
+    }
+    cluster.sync();  // #4: the list is complete
+    if (r == 0) {
+        unsigned long long thr = ~0ull;  // no candidates: nothing selected
+        if (key_hi0 != 0ull) {
+            if (bA < 0) {
+                thr = key_lo0 > 0 ? key_lo0 - 1 : 0ull;  // no rule fires: every candidate is selected
+            } else if (c_nl <= list_cap) {
+                const int nl = c_nl;
+                unsigned long long lmn = ~0ull, lmx = 0ull;
+                for (int i = tid; i < nl; i += SL_THREADS) {
+                    lmn = min(lmn, list_k[i]);
+                    lmx = max(lmx, list_k[i]);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    lmn = min(lmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, lmn, o));
+                    lmx = max(lmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, lmx, o));
+                }
+                if (lid == 0) {
+                    sm.rscr[0][wid] = lmn;
+                    sm.rscr[1][wid] = lmx;
+                }
+                __syncthreads();
+                unsigned long long llo = ~0ull, lhi = 0ull;
+                for (int q = 0; q < SL_WARPS; ++q) {
+                    llo = min(llo, sm.rscr[0][q]);
+                    lhi = max(lhi, sm.rscr[1][q]);
+                }
+                const long long qc = sm.pre[0], qs = sm.pre[1], qp = sm.pre[2];
+                __syncthreads();
+                if (nl <= 32) {
+                    if (wid == 0)
+                        resolve_boundary(list_k, list_s, nl, qc, qs, qp, 1, llo, sm.rscr[0], rules, &sm.T, &sm.flags);
+                } else {
+                    search_one(sm, DenseKeys{list_k, list_s}, nl, llo, lhi, 1, rules, qc, qs, qp);
+                }
+                __syncthreads();
+                thr = sm.T;
+            } else {  // a bucket larger than the list: search every record in global memory
+                const RecordKeys rk{a.cand + hs * rec_len, (size_t)a.bg * rec_len, cap, c_counts};
+                search_one(sm, rk, (int)cluster.num_blocks() * cap, key_lo0, key_hi0, 1, rules);
+                __syncthreads();
+                thr = sm.T;
+            }
+        }
+        if (tid == 0) *cluster.map_shared_rank(&c_thr, a.rank) = thr;
+    }
+    cluster.sync();  // #5: the threshold is with this rank's shard
+    if (r != a.rank) return;
+    const unsigned long long thrA = c_thr;
+
+    // ---- this rank's shard: its selected cells (slot order) and row list
+    const int per = (cnt + SL_THREADS - 1) / SL_THREADS;  // contiguous entries per thread
+    const int e0 = min(cnt, tid * per), e1 = min(cnt, e0 + per);
+    unsigned int nloc = 0, sloc = 0;
+    for (int e = e0; e < e1; ++e) {
+        const unsigned long long k = ck[e];
+        if (k != 0ull && k > thrA) {
+            ++nloc;
+            sloc += (unsigned)cs[e];
+        }
+    }
+    unsigned long long ix = nloc;
+    unsigned int iy = sloc;
+    sl_scan_pair(ix, iy, sm);
+    if (tid == SL_THREADS - 1) {
+        sm.wsel[0] = (int)ix;
+        sm.wkept[0] = (int)iy;
+    }
+    const int32_t* offs = a.cell_offsets + hs * (a.n_slots + 1);
+    {
+        int my = (int)(ix - nloc);
+        int run = a.static_len + (int)(iy - sloc);
+        for (int e = e0; e < e1; ++e) {
+            const unsigned long long k = ck[e];
+            if (k != 0ull && k > thrA) {
+                const int slot = (int)(0xffffffffu - (uint32_t)k) - a.key_base;
+                if (my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = slot;
+                sel_start[my] = run;
+                sel_off[my] = offs[slot];
+                ++my;
+                run += cs[e];
+            }
+        }
+    }
+    __syncthreads();
+    const int ntot = sm.wsel[0], rows_sel = sm.wkept[0];
+    int32_t* rows = a.row_index + hs * (size_t)a.exec_capacity;
+    for (int q = tid; q < a.static_len; q += SL_THREADS) rows[q] = (1 << 30) | q;
+    for (int i = wid; i < ntot; i += SL_WARPS) {
+        const int s0 = sel_start[i], off = sel_off[i];
+        const int sz = (i + 1 < ntot ? sel_start[i + 1] : a.static_len + rows_sel) - s0;
+        for (int jj = lid; jj < sz; jj += 32)
+            if (s0 + jj < a.exec_capacity) rows[s0 + jj] = off + jj;
+    }
+    if (tid == 0) {
+        a.sel_count[h] = min(ntot, a.nprobe);
+        a.row_count[h] = min(a.static_len + rows_sel, a.exec_capacity);
     }
 }
 
@@ -1193,10 +1508,29 @@ size_t merge_smem_bytes(const MergeArgs& a) {
     const size_t ne = (size_t)a.shards * a.cap;
     const size_t npad = merge_dense(a) ? (ne + 1) & ~size_t(1) : 0;
     return ((sizeof(SelHdr) + 15) & ~size_t(15)) + 12 * npad + 4 * (((size_t)a.shards + 3) & ~size_t(3)) +
-           2 * (size_t)a.cap * sizeof(int) + 16;
+           2 * sizeof(int) * (((size_t)a.cap + 1) & ~size_t(1)) + (merge_dense(a) ? 0 : 12 * (size_t)MERGE_LIST) + 16;
 }
 
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {
+    if (a.shards <= SL_CL && cmerge_smem_bytes(a) <= 227 * 1024) {  // the cluster merge
+        const size_t smc = cmerge_smem_bytes(a);
+        static int cset[64] = {};
+        cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_merge_cluster_kernel), smc, cset, 64);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.shards, a.bg);
+        cfg.blockDim = dim3(SL_THREADS);
+        cfg.dynamicSmemBytes = smc;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = a.shards;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, imi_merge_cluster_kernel, a);
+    }
     const size_t sm = merge_smem_bytes(a);
     static int smem_set[64] = {};
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_merge_kernel), sm, smem_set, 64);
