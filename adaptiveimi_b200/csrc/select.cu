@@ -1347,18 +1347,31 @@ __global__ void __launch_bounds__(SL_THREADS, 1) imi_merge_cluster_kernel(const 
             if (ck[j]) hist_add(sm, bin(ck[j]), cs[j], rules);
     }
     cluster.sync();  // #2: every local histogram is complete
-    if (r == 0 && key_hi0 != 0ull) {
-        // the cluster's histogram into the leader's
-        for (int b = tid; b < SL_NB; b += SL_THREADS) {
-            unsigned long long x = sm.hcp[b];
-            unsigned int w = sm.hsz[b];
-            for (int q = 1; q < (int)cluster.num_blocks(); ++q) {
+    if (key_hi0 != 0ull) {
+        // the cluster's histogram, each CTA summing a share of the buckets
+        // over every CTA into the leader's list area (free until #3)
+        const int nb = (int)cluster.num_blocks();
+        const int per = (SL_NB + nb - 1) / nb;
+        unsigned long long* lsum = cluster.map_shared_rank(list_k, 0);                      // [SL_NB]
+        unsigned int* lsz = reinterpret_cast<unsigned int*>(cluster.map_shared_rank(list_k, 0) + SL_NB);
+        for (int b = r * per + tid; b < min(SL_NB, (r + 1) * per); b += SL_THREADS) {
+            unsigned long long x = 0ull;
+            unsigned int w = 0u;
+            for (int q = 0; q < nb; ++q) {
                 const SelHdr* o = cluster.map_shared_rank(&sm, q);
                 x += o->hcp[b];
                 w += o->hsz[b];
             }
-            sm.hcp[b] = x;
-            sm.hsz[b] = w;
+            lsum[b] = x;
+            lsz[b] = w;
+        }
+    }
+    cluster.sync();  // #2b: the summed histogram is in the leader
+    if (r == 0 && key_hi0 != 0ull) {
+        const unsigned int* lsz = reinterpret_cast<const unsigned int*>(list_k + SL_NB);
+        for (int b = tid; b < SL_NB; b += SL_THREADS) {
+            sm.hcp[b] = list_k[b];
+            sm.hsz[b] = lsz[b];
         }
         __syncthreads();
         BucketView v;
@@ -1512,7 +1525,8 @@ size_t merge_smem_bytes(const MergeArgs& a) {
 }
 
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {
-    if (a.shards <= SL_CL && cmerge_smem_bytes(a) <= 227 * 1024) {  // the cluster merge
+    // the cluster merge (its list area also carries the summed histogram: at least SL_NB entries)
+    if (a.shards <= SL_CL && cmerge_list_cap(a.cap) >= SL_NB && cmerge_smem_bytes(a) <= 227 * 1024) {
         const size_t smc = cmerge_smem_bytes(a);
         static int cset[64] = {};
         cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_merge_cluster_kernel), smc, cset, 64);
