@@ -65,6 +65,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the burst figure (the build's kernels are timed as
+    one short burst per layer)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops)"
+    return 1590.0, "fallback"
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -282,6 +293,17 @@ def run_ours(args):
     hbm, src = peaks()
     achieved = attn["algo_bytes"] / (attn_avg_us * 1e-6) / 1e9 if attn_avg_us > 0 else 0.0
     keys_built = L * kvh * n_mid
+    # algorithmic k-means flops of the whole build, from each index's own iteration counts
+    build_flops = 0
+    for l in range(L):
+        idx = cache.index[l]
+        its = idx.iters_run.cpu().tolist()  # [heads, S]
+        S_ = len(idx.ks)
+        for row in its:
+            for s_, it in enumerate(row):
+                build_flops += (int(it) + 1) * 2 * n_mid * int(idx.ks[s_]) * (CFG["head_dim"] // S_)
+    build_flops *= ws  # every rank builds an equal share of the KV heads
+    tpk, tpk_src = tensor_peak()
     res = {
         "metric": METRIC, "value": round(us_per_layer_step, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": False,
@@ -308,7 +330,13 @@ def run_ours(args):
                      "rows_per_launch": attn["rows_per_launch"]},
         "build": {"metric": "IMI build Mkeys/s", "value": round(keys_built / (build_ms_max * 1e-3) / 1e6, 3),
                   "unit": "Mkeys/s", "build_ms_total": round(build_ms_max, 2), "keys": keys_built,
-                  "kmeans": KMEANS},
+                  "kmeans": KMEANS,
+                  "roofline": {"bound": "tensor", "achieved": round(build_flops / (build_ms_max * 1e-3) / 1e12, 2),
+                               "peak": tpk, "unit": "TFLOP/s",
+                               "frac": round(build_flops / (build_ms_max * 1e-3) / 1e12 / tpk, 4),
+                               "peak_source": tpk_src, "flops": build_flops,
+                               "flops_formula": "sum over (head, subspace) of (iters_run + 1) * 2 * n * k * D/S "
+                                                "(Lloyd distance passes plus the k-means++ pass), whole build time"}},
         "gpu_launches": None,
         "host_launch_us_per_layer_step": round(host_s * 1e6 / (args.steps * L), 2),
         "clocks": clk.summary(),
