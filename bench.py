@@ -341,9 +341,11 @@ def run_ours(args):
         "host_launch_us_per_layer_step": round(host_s * 1e6 / (args.steps * L), 2),
         "clocks": clk.summary(),
     }
-    # our kernels per layer-step: append + select + attention + combine, plus
-    # the async assignment every 16 steps and the centroid publish after it
-    res["gpu_launches"] = int(args.steps * L * 4 + (args.steps // ASYNC["batch"]) * L * 3)
+    # our kernels per layer-step: select (which also does the append) +
+    # attention (which also merges its splits); every ASYNC["batch"] steps a
+    # layer instead launches the append and the two assignment kernels before
+    # them (+3), and at its next visit the centroid publish (+1)
+    res["gpu_launches"] = int(args.steps * L * 2 + (args.steps // ASYNC["batch"]) * L * 4)
     if ws == 1 and not args.no_cpu_baseline:
         try:
             res["cpu_baseline"] = cpu_baseline(args, sample_layers=1, sample_steps=2)
