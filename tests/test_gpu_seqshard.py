@@ -37,10 +37,11 @@ def _setup(shards, heads=4, G=4, ctx=8192, seed=5, nprobe=None):
     return K, V, Q, plan, local, zone_k, zone_v
 
 
-@pytest.mark.parametrize("shards,nprobe", [(1, None), (2, None), (3, None), (4, 2100)])
+@pytest.mark.parametrize("shards,nprobe", [(1, None), (2, None), (3, None), (4, 2100), (10, None)])
 def test_sharded_selection_and_attention_match_the_union(shards, nprobe):
-    # (4, 2100): nprobe above 2048, and 4 * 2101 candidates, more than the
-    # merge keeps in shared memory, so it searches the gathered records
+    # (4, 2100): nprobe above 2048 and 4 * 2101 candidates (the cluster merge
+    # refines its boundary bucket in shared memory); (10, None): more shards
+    # than a cluster holds, so the one-CTA merge runs
     heads, G = 4, 4
     K, V, Q, plan, local, zone_k, zone_v = _setup(shards, nprobe=nprobe)
     if nprobe is not None:
