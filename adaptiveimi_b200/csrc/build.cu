@@ -55,6 +55,7 @@ struct Dev {
     int32_t* counts;       // [T][kmax]
     int32_t* offs;         // [T][kmax+1]
     int32_t* erank;        // [T][kmax]
+    int32_t* order;        // [T][kmax] cells by member count, largest first (the M-step's launch order)
     const double* draws_u; // [S][kmax]
     const int32_t* first;  // [S]
     const int32_t* reseed; // [iters][kmax]
@@ -1312,12 +1313,38 @@ __global__ void __launch_bounds__(1024) cell_prefix_kernel(Dev b, int from_radix
         __syncthreads();
     }
     if (threadIdx.x == 0) b.offs[(size_t)t * (b.kst + 1) + k] = carry_c;
+    // the M-step's launch order: cells by member count, largest first (ties by
+    // index), so the longest sequential sums start in the first wave; by rank
+    // against every other cell when k fits the block, in index order otherwise
+    __shared__ int scnt[1024];
+    __syncthreads();
+    const int* cn = b.counts + (size_t)t * b.kst;
+    int* ord = b.order + (size_t)t * b.kst;
+    if (k <= (int)blockDim.x) {
+        const int c = threadIdx.x;
+        if (c < k) scnt[c] = cn[c];
+        __syncthreads();
+        if (c < k) {
+            const int mine = scnt[c];
+            int rank = 0;
+            for (int c2 = 0; c2 < k; ++c2) {
+                const int o = scnt[c2];
+                rank += (o > mine || (o == mine && c2 < c)) ? 1 : 0;
+            }
+            ord[rank] = c;
+        }
+    } else {
+        for (int c = threadIdx.x; c < k; c += blockDim.x) ord[c] = c;
+    }
 }
 
 // centroid[c][d] = (sum over members in sample order) * (1 / size); empty cells
 // take the iteration's next reseed draw (kmeans_core.cpp:268-311).
-// One CTA per (centroid, task).  Each dim's sum is one chain of fp32 adds in
-// sample order, so a cell's time is its member count times one add; the
+// One CTA per (task, centroid), the centroids of each task launched largest
+// first (cell_prefix_kernel ranks them by member count) and the tasks
+// interleaved, so the longest sums start in the first wave.  Each dim's sum
+// is one chain of fp32 adds in sample order, so a cell's time is its member
+// count times one add; the
 // member rows are gathered by all four warps with 16-byte cp.async into a
 // ring of MS_STAGES chunks (MS_CHUNK bf16 each), far enough ahead that warp 0,
 // which owns the chains (lane l: bf16 pairs l and, for sub 128, l + 32),
@@ -1331,10 +1358,11 @@ __global__ void __launch_bounds__(MS_THREADS) msum_kernel(Dev b, int it, const i
     constexpr bool TWO = NPAIR > 32;     // sub = 128: each lane owns pairs l and l + 32
     constexpr int ROWS = MS_CHUNK / SUB; // rows per stage
     constexpr int CPR = SUB / 8;         // 16-byte pieces per row
-    const int t = blockIdx.y, c = blockIdx.x;
+    const int t = blockIdx.x;  // tasks vary fastest: every task's largest cells launch first
     if (b.done[t]) return;
     const int k = b.ks[task_s(b, t)];
-    if (c >= k) return;
+    if ((int)blockIdx.y >= k) return;
+    const int c = b.order[(size_t)t * b.kst + blockIdx.y];
     extern __shared__ __align__(16) uint16_t mring[];  // [MS_STAGES][ROWS][SUB]
     const int tid = threadIdx.x, lane = tid & 31;
     const int cnt = b.counts[(size_t)t * b.kst + c];
@@ -1549,7 +1577,7 @@ namespace {
 
 struct Layout {
     size_t labels, md, perm_a, perm_b, part_lo, part_hi, part_minl, part_bad, hist, dig_off, dig_tot, counts, offs,
-        erank, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, xn, total;
+        erank, order, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, xn, total;
     int npad;
 };
 
@@ -1588,6 +1616,7 @@ Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters
     L.counts = take((size_t)T * kmax * 4);
     L.offs = take((size_t)T * (kmax + 1) * 4);
     L.erank = take((size_t)T * kmax * 4);
+    L.order = take((size_t)T * kmax * 4);
     L.draws_u = take((size_t)S * kmax * 8);
     L.first = take((size_t)S * 4);
     L.reseed = take((size_t)std::max(1, max_iters) * kmax * 4);
@@ -1716,7 +1745,7 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
             label_count_kernel<<<dim3(std::min(d.NB, 64), d.T), BT, 0, st>>>(d);
         }
         cell_prefix_kernel<<<d.T, 1024, 0, st>>>(d, two_pass ? 0 : 1);
-        msum_kernel<SUB><<<dim3(kmax_all, d.T), MS_THREADS, ms_smem, st>>>(d, it, perm);
+        msum_kernel<SUB><<<dim3(d.T, kmax_all), MS_THREADS, ms_smem, st>>>(d, it, perm);
     }
     return cudaGetLastError();
 }
@@ -1799,6 +1828,7 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
     d.counts = reinterpret_cast<int32_t*>(ws + L.counts);
     d.offs = reinterpret_cast<int32_t*>(ws + L.offs);
     d.erank = reinterpret_cast<int32_t*>(ws + L.erank);
+    d.order = reinterpret_cast<int32_t*>(ws + L.order);
     d.draws_u = reinterpret_cast<const double*>(ws + L.draws_u);
     d.first = reinterpret_cast<const int32_t*>(ws + L.first);
     d.reseed = reinterpret_cast<const int32_t*>(ws + L.reseed);

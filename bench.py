@@ -262,13 +262,20 @@ def run_ours(args):
     # (the cache has capacity for warmup + steps appended tokens; e2e reuses the
     # last `e2e_steps` positions after a reset of the appended-token counter)
     e2e_steps = min(args.steps, 8)
-    qh = qd[:e2e_steps].cpu().pin_memory()
-    kh = kd[:e2e_steps].cpu().pin_memory()
-    vh = vd[:e2e_steps].cpu().pin_memory()
-    outs_h = torch.empty((e2e_steps, L, 1, 1, hl * G, CFG["head_dim"]), dtype=torch.bfloat16).pin_memory()
+    e2e_warm = min(2, max(0, args.steps - e2e_steps))  # untimed, through the same pinned-copy path
+    e2e_total = e2e_warm + e2e_steps
+    qh = qd[:e2e_total].cpu().pin_memory()
+    kh = kd[:e2e_total].cpu().pin_memory()
+    vh = vd[:e2e_total].cpu().pin_memory()
+    outs_h = torch.empty((e2e_total, L, 1, 1, hl * G, CFG["head_dim"]), dtype=torch.bfloat16).pin_memory()
     qb, kb, vb = torch.empty_like(qd[0]), torch.empty_like(kd[0]), torch.empty_like(vd[0])
-    cache.static_pattern_total -= e2e_steps  # re-use appended positions (same shapes, same work)
-    cache.context -= e2e_steps
+    cache.static_pattern_total -= e2e_total  # re-use appended positions (same shapes, same work)
+    cache.context -= e2e_total
+    for t in range(e2e_steps, e2e_total):  # the warm-up steps (their own inputs)
+        qb.copy_(qh[t], non_blocking=True)
+        kb.copy_(kh[t], non_blocking=True)
+        vb.copy_(vh[t], non_blocking=True)
+        step(t, qb, kb, vb, out_sink=outs_h[t])
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
