@@ -43,7 +43,6 @@ constexpr int AT_PITCH = 272;                            // bytes per row in sha
                                                          // puts the 8 rows of an ldmatrix on distinct banks
 constexpr int AT_STAGE_BYTES = 2 * AT_TILE * AT_PITCH;   // K tile + V tile
 constexpr int AT_RING_BYTES = AT_WARPS * AT_STAGES * AT_STAGE_BYTES;
-constexpr int AT_BAR_BYTES = AT_WARPS * AT_STAGES * 8;   // (reserved; the row list follows it)
 
 IMI_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -455,7 +454,7 @@ cudaError_t launch_combine_shards(const CombineArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-size_t attn_smem_bytes(const AttnArgs&) { return (size_t)AT_RING_BYTES + AT_BAR_BYTES; }
+size_t attn_smem_bytes(const AttnArgs&) { return (size_t)AT_RING_BYTES; }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st) {
     const size_t sm = attn_smem_bytes(a);

@@ -136,8 +136,6 @@ static int check_attention(const imi_attn_desc* d) {
         (reinterpret_cast<uintptr_t>(d->out) & 7u) != 0)
         return fail(IMI_ERR_INVALID, "imi_sparse_attention: part_o must be 16-byte and part_ml/out 8-byte aligned");
     if (d->exec_capacity <= 0) return fail(IMI_ERR_INVALID, "imi_sparse_attention: exec_capacity must be positive");
-    if (imi::attn_smem_bytes(*d) > 227 * 1024)
-        return fail(IMI_ERR_INVALID, "imi_sparse_attention: too few splits for the row capacity (raise splits)");
     return IMI_OK;
 }
 

@@ -218,21 +218,17 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
     _lib.check(L.imi_select_cells(ctypes.byref(d), _stream(q.device)), "imi_select_cells")
 
 
-ATTN_MAX_ROWS_PER_CTA = 5632  # staged row entries per CTA that fit beside the copy ring in shared memory
-
-
 def default_splits(bg: int, rows_per_group: int, sms: int = 148, exec_capacity: Optional[int] = None) -> int:
     """CTAs per KV group for the split-K attention: one wave (one CTA per SM,
-    the kernel's shared-memory ring allows one), at least 64 rows per CTA, and
-    few enough rows per CTA that its share of the row list (sized from
-    ``exec_capacity``, the row-list stride) fits in shared memory."""
+    the kernel's shared-memory ring allows one) and at least 64 rows per CTA.
+    ``exec_capacity`` is accepted for callers that pass it; the kernel reads
+    the row list straight from global memory, so it no longer bounds the
+    split."""
     # one CTA per SM, but at most 48 per group: past that the split merge costs
     # more than the extra streaming width gains (one group on a B200: 13.7 µs at
     # 148 splits, 11.3 µs at 37-74)
     want = max(1, min(48, sms // bg))
-    s = max(1, min(want, (rows_per_group + 63) // 64, 512))
-    cap = max(rows_per_group, exec_capacity or 0)
-    return int(max(s, (cap + ATTN_MAX_ROWS_PER_CTA - 1) // ATTN_MAX_ROWS_PER_CTA))
+    return int(max(1, min(want, (rows_per_group + 63) // 64, 512)))
 
 
 def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: torch.Tensor,
