@@ -729,12 +729,15 @@ __global__ void cent_split_kernel(Dev b) {
 
 // Lloyd E-step on the tensor cores, warp-specialised.  One CTA per SM walks
 // a run of 128-sample tiles of one task:
-//  * a control thread keeps up to `stages` tiles in flight with TMA (a 4-D
+//  * a producer thread keeps up to `stages` tiles in flight with TMA (a 4-D
 //    tensor map over the keys writes each tile chunk-major: 16-byte column
 //    chunk c of row r at c * 2 KB + r * 16 B, the no-swizzle K-major
 //    core-matrix layout with LBO = 2 KB, SBO = 128 B) plus the tile's 128
-//    sample norms, and issues the hi, norm and lo MMA chains of tile j into
-//    TMEM accumulator j % 4 (npad fp32 columns, d~(c) = ||c||^2 - 2 x.c);
+//    sample norms;
+//  * an MMA thread (another warp) issues the hi, norm and lo MMA chains of
+//    tile j into TMEM accumulator j % 4 (npad fp32 columns,
+//    d~(c) = ||c||^2 - 2 x.c) once the tile has landed and the accumulator
+//    is free (each role waits on its own barriers);
 //  * two groups of eight epilogue warps take alternate tiles; sample r (TMEM
 //    lane r) of a tile is shared by two warps of the group, each scanning one
 //    half of the columns: the minimum m1, then the centroids with
@@ -748,9 +751,8 @@ __global__ void cent_split_kernel(Dev b) {
 // sets the status flag and drains the copies and MMAs in flight.
 constexpr int TC_MAX_STAGES = 8;
 constexpr int TC_GROUP = 256;                       // eight epilogue warps
-constexpr int TC_CTA_THREADS = 2 * TC_GROUP + 32;   // two groups and the control warp (17 warps: at most
-                                                    // 96 registers, five warps share one SM quarter)
-constexpr long long TC_SPIN_LIMIT = 1ll << 24;      // control polls without progress before giving up
+constexpr int TC_CTA_THREADS = 2 * TC_GROUP + 64;   // two groups, the MMA warp and the TMA warp (18 warps:
+                                                    // at most 96 registers, five warps share one SM quarter)
 
 // element (r, d) of a staged sample tile (chunk-major, see above)
 IMI_DEV int a_off(int r, int d) { return (d >> 3) * (TC_M * 8) + r * 8 + (d & 7); }
@@ -897,7 +899,7 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
     for (int w = 1; w < TC_CTA_THREADS / 32; ++w) cmax = fmaxf(cmax, red[w]);
 
     if (warp == 2 * TC_GROUP / 32) {
-        // ---- control: TMA producer and MMA issuer (one thread)
+        // ---- MMA issuer (one thread): tile j once it has landed and its accumulator is free
         if (lane == 0) {
             // instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = npad, M = 128
             const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(npad >> 3) << 17) |
@@ -907,75 +909,68 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
             const uint64_t ext_desc = umma_desc(tc_smem(Ae), 128, 256);
             const uint64_t a_desc0 = umma_desc(tc_smem(As), LBO_A, SBO_A);
             const uint64_t bh_desc = umma_desc(bh0, LBO_B, SBO_B), bl_desc = umma_desc(bl0, LBO_B, SBO_B);
-            const uint32_t stage_bytes = TC_M * SUB * 2;
-            const int h = task_h(b, t), s0 = task_s(b, t) * CPR;
-            const float* xn_t = b.xn + (size_t)t * b.nx;
-            int issued = 0, jm = 0;
-            long long idle = 0;
-            while (jm < nt) {
-                bool prog = false;
-                if (issued < nt && issued < jm + stages) {
-                    const int q = issued % stages;
-                    if (issued < stages || mb_test(empty0 + 8 * q, (uint32_t)((issued / stages) - 1) & 1u)) {
-                        const uint32_t fb = full0 + 8 * q;
-                        const int row0 = (tile0 + issued) * TC_M;
-                        mb_expect(fb, stage_bytes + TC_M * 4);
-                        asm volatile(
-                            "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-                            "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(tc_smem(As + q * TC_M * SUB)),
-                            "l"(reinterpret_cast<uint64_t>(&tmap)), "r"(0), "r"(row0), "r"(s0), "r"(h), "r"(fb)
-                            : "memory");
-                        asm volatile(
-                            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                                tc_smem(xs + q * TC_M)),
-                            "l"(xn_t + row0), "r"(TC_M * 4), "r"(fb)
-                            : "memory");
-                        ++issued;
-                        prog = true;
-                    }
-                }
-                if (jm < issued) {
-                    const int q = jm % stages, ac = jm & 3;
-                    if (mb_test(full0 + 8 * q, (uint32_t)(jm / stages) & 1u) &&
-                        (jm < 4 || mb_test(acce0 + 8 * ac, (uint32_t)((jm >> 2) - 1) & 1u))) {
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const uint32_t acc = tmem + (uint32_t)(ac * acc_cols);
-                        // descriptor start addresses sit in the low bits (16-byte units):
-                        // a K step is a plain add
-                        const uint64_t ad = a_desc0 + (uint64_t)(q * (TC_M * SUB * 2 / 16));
-#pragma unroll
-                        for (int kk = 0; kk < SUB / 16; ++kk)
-                            umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bh_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
-                                      idesc, kk > 0 ? 1u : 0u);
-                        umma_bf16(acc, ext_desc, bh_desc + (uint64_t)((SUB / 16) * (2 * LBO_B / 16)), idesc, 1u);
-#pragma unroll
-                        for (int kk = 0; kk < SUB / 16; ++kk)
-                            umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bl_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
-                                      idesc, 1u);
-                        asm volatile(
-                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                accf0 + 8 * ac)
-                            : "memory");
-                        asm volatile(
-                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                empty0 + 8 * q)
-                            : "memory");
-                        ++jm;
-                        prog = true;
-                    }
-                }
-                if (prog) {
-                    idle = 0;
-                } else if (++idle > TC_SPIN_LIMIT || s_fail) {
+            int jm = 0;
+            for (; jm < nt; ++jm) {
+                const int q = jm % stages, ac = jm & 3;
+                if (!tc_wait(full0 + 8 * q, (uint32_t)(jm / stages) & 1u) ||
+                    (jm >= 4 && !tc_wait(acce0 + 8 * ac, (uint32_t)((jm >> 2) - 1) & 1u))) {
                     s_fail = 1;
                     break;
                 }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + (uint32_t)(ac * acc_cols);
+                // descriptor start addresses sit in the low bits (16-byte units):
+                // a K step is a plain add
+                const uint64_t ad = a_desc0 + (uint64_t)(q * (TC_M * SUB * 2 / 16));
+#pragma unroll
+                for (int kk = 0; kk < SUB / 16; ++kk)
+                    umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bh_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
+                              idesc, kk > 0 ? 1u : 0u);
+                umma_bf16(acc, ext_desc, bh_desc + (uint64_t)((SUB / 16) * (2 * LBO_B / 16)), idesc, 1u);
+#pragma unroll
+                for (int kk = 0; kk < SUB / 16; ++kk)
+                    umma_bf16(acc, ad + (uint64_t)(kk * (2 * LBO_A / 16)), bl_desc + (uint64_t)(kk * (2 * LBO_B / 16)),
+                              idesc, 1u);
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 accf0 + 8 * ac)
+                             : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 empty0 + 8 * q)
+                             : "memory");
             }
-            s_issued = issued;
             s_mma = jm;
         }
+    } else if (warp == 2 * TC_GROUP / 32 + 1) {
+        // ---- TMA producer (one thread): tile j into its stage once that stage is free
+        if (lane == 0) {
+            const uint32_t stage_bytes = TC_M * SUB * 2;
+            const int h = task_h(b, t), s0 = task_s(b, t) * CPR;
+            const float* xn_t = b.xn + (size_t)t * b.nx;
+            int issued = 0;
+            for (; issued < nt; ++issued) {
+                const int q = issued % stages;
+                if (issued >= stages && !tc_wait(empty0 + 8 * q, (uint32_t)((issued / stages) - 1) & 1u)) {
+                    s_fail = 1;
+                    break;
+                }
+                const uint32_t fb = full0 + 8 * q;
+                const int row0 = (tile0 + issued) * TC_M;
+                mb_expect(fb, stage_bytes + TC_M * 4);
+                asm volatile(
+                    "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                    "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(tc_smem(As + q * TC_M * SUB)),
+                    "l"(reinterpret_cast<uint64_t>(&tmap)), "r"(0), "r"(row0), "r"(s0), "r"(h), "r"(fb)
+                    : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        tc_smem(xs + q * TC_M)),
+                    "l"(xn_t + row0), "r"(TC_M * 4), "r"(fb)
+                    : "memory");
+            }
+            s_issued = issued;
+        }
     } else {
-        // ---- epilogue: group g takes tiles g, g + 2, ...
+        // ---- epilogue (warps 0-15): group g takes tiles g, g + 2, ...
         const int g = warp >> 3, lw = warp & 7, half = lw >> 2;
         const int row = (lw & 3) * 32 + lane;            // this thread's sample (TMEM lane) in a tile
         const int gid = 1 + g;                           // the group's named barrier
