@@ -32,7 +32,7 @@ class BuildDesc(ctypes.Structure):
         ("cell_sizes", P), ("cell_offsets", P), ("cell_mask", P), ("cell_code", P),
         ("centroids", P), ("sub_centroids", P), ("sub_labels", P), ("n_active", P), ("iters_run", P),
         ("workspace", P), ("workspace_bytes", sz),
-        ("status", P),
+        ("status", P), ("phase_ns", P),
     ]
 
 
@@ -161,7 +161,7 @@ def load():
         L.imi_decode_layer.argtypes = [ctypes.POINTER(AppendDesc), ctypes.POINTER(AsyncDesc),
                                        ctypes.POINTER(ApplyDesc), ctypes.POINTER(SelectDesc),
                                        ctypes.POINTER(AttnDesc), P]
-        if L.imi_abi_version() != 1:
+        if L.imi_abi_version() != 2:
             raise ImportError("libimi_b200.so ABI version mismatch")
         _lib = L
         return _lib

@@ -214,11 +214,14 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         return None
 
     def ensure_layer_ready(self, layer_idx: int) -> None:
-        """The device build is stream-ordered before decode; only metadata checks remain."""
+        """Wait for the layer's device build and check it (indexing.py ensure_layer_ready):
+        a build whose device status reports a give-up, or whose cell count
+        overflows the slots, raises here, before any decode step reads it."""
         if self.layer_ready[layer_idx] or not self.build_index_when_prefilling:
             return
         if not self.layer_started[layer_idx]:
             raise RuntimeError(f"IMI layer {layer_idx} not started")
+        self.imi_pipelines[layer_idx].finish_index(as_host_metadata=False)
         self.layer_ready[layer_idx] = True
 
     # ------------------------------------------------------------------------
@@ -241,7 +244,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                 part_o=torch.empty((bg, self.splits, G, self.head_dim), dtype=torch.float32, device=dev),
                 part_ml=torch.empty((bg, self.splits, G, 2), dtype=torch.float32, device=dev),
                 counters=torch.zeros((bg,), dtype=torch.int32, device=dev),
-                status=torch.zeros((1,), dtype=torch.int32, device=dev),
             )
             self.execution_buffer_keys_dict[dev] = rows
             self.execution_buffer_values_dict[dev] = rows
@@ -298,7 +300,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             att.delta_rows = self.async_update_delta_tokens
         att.part_o, att.part_ml = buf["part_o"].data_ptr(), buf["part_ml"].data_ptr()
         att.counters = buf["counters"].data_ptr()
-        att.status = buf["status"].data_ptr()
         app = None
         if st is not None:
             app = _lib.ApplyDesc()

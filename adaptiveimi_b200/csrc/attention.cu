@@ -490,22 +490,52 @@ static __device__ __align__(256) unsigned char g_attn_scratch[IMI_NOALLOC_SCRATC
 namespace {
 
 std::mutex g_scratch_mu;
+// per device: the context the address was looked up in, and the address
+void* g_scratch_ctx[128] = {};
 void* g_scratch_ptr[128] = {};
 
+typedef int (*CtxGetCurrentFn)(void**);
+
+// The current driver context (the primary context under the runtime API), or
+// null when the entry point is unavailable.
+void* current_context() {
+    static CtxGetCurrentFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+        else
+            (void)cudaGetLastError();
+    }
+    void* ctx = nullptr;
+    if (fn && fn(&ctx) != 0) ctx = nullptr;
+    return ctx;
+}
+
 // Device address of g_attn_scratch for the current device.  The name is only
-// a host-side stand-in, so the address is asked of the runtime, once per
-// device, with that device current.
+// a host-side stand-in, so the address is asked of the runtime with that
+// device current: once per device, and again whenever the device's context
+// has changed since (after cudaDeviceReset the module, and with it the array,
+// is loaded anew at another address).
 cudaError_t scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    // null before the runtime has made a context current: the lookup below
+    // does that, and the next call caches against the context
+    void* ctx = current_context();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
+    if (!g_scratch_ptr[dev] || ctx == nullptr || ctx != g_scratch_ctx[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn_scratch);
         if (e != cudaSuccess) return e;
         g_scratch_ptr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_ptr[dev];
     return cudaSuccess;

@@ -1080,6 +1080,17 @@ __global__ void __launch_bounds__(TC_CTA_THREADS, 1)
         }
     }
     __syncthreads();
+    if (s_fail) {
+        // a wait gave up: the CTA's labels are not valid.  Leave every row of its
+        // tiles with an in-range label (0) so that the kernels that index by
+        // label (counts, M-step, reorganize) stay in bounds; the status bit
+        // tells the caller the build is void.
+        const int r0 = tile0 * TC_M, r1 = min(b.n, (tile0 + nt) * TC_M);
+        for (int i = r0 + tid; i < r1; i += TC_CTA_THREADS) {
+            b.labels[(size_t)t * b.n + i] = 0;
+            if (want_md) b.md[(size_t)t * b.n + i] = 0.0f;
+        }
+    }
     if (tid == 2 * TC_GROUP && s_fail) {
         // report, then let the copies and MMAs in flight finish (bounded) before TMEM and shared memory go
         if (b.status) atomicOr(b.status, 1);
@@ -1565,6 +1576,15 @@ __global__ void reorg_gather_kernel(Dev b, BuildArgs a, const int32_t* perm) {
     }
 }
 
+// device timestamp of a point in the build's stream order (per-stage times)
+__global__ void stamp_kernel(unsigned long long* out) {
+    if (threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        *out = t;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // host orchestration
 // ---------------------------------------------------------------------------
@@ -1882,11 +1902,13 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
         cudaStreamSynchronize(st);
     }
     cudaError_t e;
+    if (a.phase_ns) stamp_kernel<<<1, 32, 0, st>>>(a.phase_ns);
     if (sub == 64) e = run_kmeans_sub<64>(d, a, st);
     else if (sub == 32) e = run_kmeans_sub<32>(d, a, st);
     else e = run_kmeans_sub<128>(d, a, st);
     if (e != cudaSuccess) return e;
     if (a.iters_run) cudaMemcpyAsync(a.iters_run, d.iters_run, (size_t)d.T * 4, cudaMemcpyDeviceToDevice, st);
+    if (a.phase_ns) stamp_kernel<<<1, 32, 0, st>>>(a.phase_ns + 1);
     // ---- reorganize
     cudaMemsetAsync(d.used, 0, (size_t)a.heads * G, st);
     reorg_mark_kernel<<<dim3((a.n_tokens + 255) / 256, a.heads), 256, 0, st>>>(d);
@@ -1924,6 +1946,7 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
     reorg_offsets_kernel<<<dim3((a.n_tokens + 255) / 256, a.heads), 256, 0, st>>>(d, a, perm);
     reorg_meta_kernel<<<dim3(a.n_slots + 1, a.heads), 128, 0, st>>>(d, a);
     reorg_gather_kernel<<<dim3((a.n_tokens + 15) / 16, a.heads), 256, 0, st>>>(d, a, perm);
+    if (a.phase_ns) stamp_kernel<<<1, 32, 0, st>>>(a.phase_ns + 2);
     return cudaGetLastError();
 }
 

@@ -8,8 +8,10 @@ K/V that are already in HBM instead of a D2H copy and CPU k-means
 
 Stages follow ``PipelineStage`` (layer_pipeline.hpp:32-40); ``get_pipeline_stats``
 keeps the reference's keys (``PipelineStats``, layer_pipeline.hpp:42-53) with the
-host-copy stages at zero, and ``kmeans_ms`` / ``reorganize_ms`` measured with CUDA
-events (reported together as one device build: ``build_ms``).
+host-copy stages at zero; ``kmeans_ms`` and ``reorganize_ms`` come from device
+timestamps the build takes between its stages on the stream.  A build whose
+device status word reports a give-up (or whose cells overflow the slots) goes to
+``PipelineStage.Failed`` and ``finish_index`` raises ``RuntimeError``.
 """
 from __future__ import annotations
 
@@ -85,7 +87,8 @@ class IMIPipeline:
         self._staging: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
         self._chunks_seen = 0
         self._done_event: Optional[torch.cuda.Event] = None
-        self._t0 = self._t1 = None
+        self._status: Optional[torch.Tensor] = None
+        self._phase_ns: Optional[torch.Tensor] = None
         self.index: Optional[ops.IMIIndex] = None
         self._last_pipeline_stats: Optional[Dict[str, object]] = None
         self._batch_allocate_cpu_buffer_callback = None
@@ -105,6 +108,7 @@ class IMIPipeline:
         self._keys = self._values = None
         self._staging = None
         self._token_count = None
+        self._done_event = None
         self.stage = PipelineStage.Idle
 
     def close(self) -> None:
@@ -131,21 +135,41 @@ class IMIPipeline:
             n_slots = prod + 1
         settings = _kmeans_settings(self.runtime_config.kmeans)
         self.stage = PipelineStage.Clustering
-        self._t0 = torch.cuda.Event(enable_timing=True)
-        self._t1 = torch.cuda.Event(enable_timing=True)
+        self.error_message = ""
+        dev = self._device()
+        # device status word (bit 0: an E-step wait gave up) and the stage
+        # timestamps (k-means start / end, reorganize end), read at finish
+        self._status = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self._phase_ns = torch.zeros((3,), dtype=torch.int64, device=dev)
         self._done_event = torch.cuda.Event()
-        with torch.cuda.device(self._device()):
-            self._t0.record()
+        with torch.cuda.device(dev):
             try:
                 self.index = ops.build_index(keys, values, parts=self.subspace_parts, ks=ks, n_slots=n_slots,
-                                             list_keys=list_keys, list_values=list_values, **settings)
+                                             list_keys=list_keys, list_values=list_values, status=self._status,
+                                             phase_ns=self._phase_ns, **settings)
             except Exception as exc:  # mark_failure (layer_pipeline.cpp:232-236)
-                self.stage = PipelineStage.Failed
-                self.error_message = str(exc)
+                self._mark_failure(str(exc))
                 raise RuntimeError(f"IMI pipeline failed: {exc}") from exc
-            self._t1.record()
             self._done_event.record()
         self._token_count = n
+
+    def _mark_failure(self, message: str) -> None:
+        """layer_pipeline.cpp:232-236: keep the message, stage Failed."""
+        self.error_message = message
+        self.stage = PipelineStage.Failed
+
+    def _check_device_result(self) -> None:
+        """After the build's event: a set status bit or an overflowing cell
+        count voids the index (the reference's merge path raises on a head
+        whose k-means result is missing, layer_pipeline.cpp:360-402)."""
+        st = int(self._status.item())
+        if st & 1:
+            self._mark_failure("IMI build: a tensor-core E-step wait gave up (device status 0x%x); "
+                               "the index is not valid" % st)
+            return
+        na = int(self.index.n_active.max().item())
+        if na > self.index.n_slots - 1:
+            self._mark_failure(f"IMI build produced {na} cells for {self.index.n_slots} slots")
 
     def build_index(self, keys, values, list_keys=None, list_values=None) -> List[Dict[str, object]]:
         self.start_index(keys, values, list_keys, list_values)
@@ -234,38 +258,50 @@ class IMIPipeline:
         return self.finish_index(list_keys, list_values)
 
     def wait_ready(self, timeout_sec: float) -> bool:
-        if self._done_event is None:
+        """True once the device build has completed and passed its checks;
+        False on timeout, before any build, or when the build failed
+        (layer_pipeline.cpp:121-137 returns the ready flag, which a failure
+        never sets)."""
+        if self._done_event is None or self.stage == PipelineStage.Failed:
             return False
         deadline = time.monotonic() + max(0.0, float(timeout_sec))
         while not self._done_event.query():
             if time.monotonic() > deadline:
                 return False
             time.sleep(0.0005)
-        return self.stage != PipelineStage.Failed
+        if self.stage not in (PipelineStage.Complete, PipelineStage.Failed):
+            self._check_device_result()
+            if self.stage != PipelineStage.Failed:
+                self.stage = PipelineStage.Complete
+        return self.stage == PipelineStage.Complete
 
     def finish_index(self, list_keys=None, list_values=None, as_host_metadata: bool = True):
         token_count = self._token_count
         if token_count is None or self.index is None:
             raise RuntimeError("IMI pipeline finish called before start")
         if not self.wait_ready(timeout_sec=max(60.0, token_count / 1024.0 * 5.0)):
+            if self.stage == PipelineStage.Failed:
+                raise RuntimeError(f"IMI pipeline failed: {self.error_message}")
             raise RuntimeError("IMI pipeline did not finish in time")
-        build_ms = float(self._t0.elapsed_time(self._t1))
+        t = [int(x) for x in self._phase_ns.tolist()]
+        kmeans_ms = max(0, t[1] - t[0]) / 1e6
+        reorganize_ms = max(0, t[2] - t[1]) / 1e6
         idx = self.index
-        self.stage = PipelineStage.Complete
+        # PipelineStats keys (layer_pipeline.hpp:42-53).  The host-copy stages
+        # do not exist in a device build (0); the reorganize kernels write the
+        # list rows directly, so write_ms is part of reorganize_ms.
         self._last_pipeline_stats = {
-            "d2h_ms": 0.0, "cpu_copy_ms": 0.0, "kmeans_ms": build_ms, "kmeans_cpu_time_ms": 0.0,
-            "kmeans_cpu_util_cores": 0.0, "reorganize_ms": 0.0, "write_ms": 0.0, "kmeans_gate_wait_ms": 0,
-            "total_chunks": max(1, self._chunks_seen), "total_tokens": int(token_count), "build_ms": build_ms,
+            "d2h_ms": 0.0, "cpu_copy_ms": 0.0, "kmeans_ms": kmeans_ms, "kmeans_cpu_time_ms": 0.0,
+            "kmeans_cpu_util_cores": 0.0, "reorganize_ms": reorganize_ms, "write_ms": 0.0, "kmeans_gate_wait_ms": 0,
+            "total_chunks": max(1, self._chunks_seen), "total_tokens": int(token_count),
+            "build_ms": kmeans_ms + reorganize_ms,
         }
-        na = idx.n_active.cpu()
-        if int(na.max()) > idx.n_slots - 1:
-            self.stage = PipelineStage.Failed
-            raise RuntimeError(f"IMI build produced {int(na.max())} cells for {idx.n_slots} slots")
         if list_keys is not None and list_values is not None and list_keys.data_ptr() != idx.list_keys.data_ptr():
             list_keys[0, :, :token_count].copy_(idx.list_keys)
             list_values[0, :, :token_count].copy_(idx.list_values)
         if not as_host_metadata:
             return idx
+        na = idx.n_active.cpu()
         out = []
         for h in range(self.kv_heads):
             c = int(na[h])

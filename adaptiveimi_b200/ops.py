@@ -85,13 +85,17 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
                 max_iters: int = 25, tol: float = 5e-4, early_stop_min_iter: int = 5,
                 early_stop_rel_tol: float = 5e-4, list_keys: Optional[torch.Tensor] = None,
                 list_values: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-                kmax: Optional[int] = None, status: Optional[torch.Tensor] = None) -> IMIIndex:
+                kmax: Optional[int] = None, status: Optional[torch.Tensor] = None,
+                phase_ns: Optional[torch.Tensor] = None) -> IMIIndex:
     """Build the IMI of one layer on the device.
 
     keys / values: [heads, n, D] bf16 CUDA views whose last dim is contiguous
     (e.g. ``key_states[0, start:end].transpose(0, 1)`` -- no copy is made).
     ``list_keys`` / ``list_values`` ([heads, >= n, D]) receive the rows in cell
-    order; allocated when not given.
+    order; allocated when not given.  ``status``: int32 [1] device word, bit 0
+    set when the tensor-core E-step gave up (the index is then void).
+    ``phase_ns``: int64 [3] device timestamps (k-means start, k-means end,
+    reorganize end).
     """
     if keys.dim() != 3 or keys.shape != values.shape:
         raise ValueError("keys/values must be [kv_heads, tokens, head_dim] and share a shape")
@@ -137,6 +141,7 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
         setattr(d, name, out[name].data_ptr())
     d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel()
     d.status = status.data_ptr() if status is not None else None
+    d.phase_ns = phase_ns.data_ptr() if phase_ns is not None else None
     L = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(L.imi_build_index(ctypes.byref(d), _stream(dev)), "imi_build_index")
@@ -241,7 +246,7 @@ def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: tor
     """Attention of q [bg, G, 128] over the rows named by row_index.
     counters: int32 [bg] zeroed scratch; when given the split merge happens in
     the attention kernel itself (its last CTA per group).
-    status: int32 [1] or None; bit 0 is set if a wait for a row copy gave up."""
+    status: int32 [1] or None (reserved: the kernel has no waits and sets no bit)."""
     bg, G, D = q.shape
     if D != 128:
         raise ValueError("sparse attention supports head_dim 128")

@@ -132,10 +132,16 @@ class SeqShard:
         p = self.plan
         if keys.shape[1] != p.lengths[self.rank]:
             raise ValueError(f"shard {self.rank} holds {p.lengths[self.rank]} tokens, got {keys.shape[1]}")
+        status = torch.zeros((1,), dtype=torch.int32, device=self.dev)
         self.index = ops.build_index(keys, values, parts=p.parts, ks=p.ks[self.rank], n_slots=p.n_slots[self.rank],
                                      max_iters=max_iters, tol=tol, early_stop_min_iter=early_stop_min_iter,
-                                     early_stop_rel_tol=early_stop_rel_tol)
+                                     early_stop_rel_tol=early_stop_rel_tol, status=status)
         self.slot_bound = int(self.index.n_active.max().item())
+        if int(status.item()) & 1:
+            raise RuntimeError(f"shard {self.rank}: IMI build failed (a tensor-core E-step wait gave up)")
+        if self.slot_bound > p.n_slots[self.rank] - 1:
+            raise RuntimeError(f"shard {self.rank}: IMI build produced {self.slot_bound} cells for "
+                               f"{p.n_slots[self.rank]} slots")
 
     # -- exchange over NVLink peer memory ---------------------------------------
     def enable_peer_exchange(self, group=None) -> bool:
@@ -172,8 +178,30 @@ class SeqShard:
                    torch.tensor([x + 4 * world for x in fp], dtype=i64, device=self.dev)),
             counters=torch.zeros((2, 2), dtype=torch.int32, device=self.dev),  # per channel: epoch, ticket
             status=torch.zeros((1,), dtype=torch.int32, device=self.dev),
+            # host mirror of the status word, refreshed without a sync after
+            # every step's exchanges and checked at the next step
+            status_host=torch.zeros((1,), dtype=torch.int32, pin_memory=True),
             bytes=(self.cand.numel() * 8, self.partials.numel() * 4))
         return True
+
+    def exchange_failed(self) -> bool:
+        """Whether a peer exchange so far gave up waiting for a peer (synchronises)."""
+        pe = getattr(self, "_peer", None)
+        return pe is not None and bool(int(pe["status"].item()) & 1)
+
+    def check_exchange(self, lagged: bool = False) -> None:
+        """Raise when a peer exchange gave up waiting for a peer: its copy of
+        that peer's block was skipped, so the merge or the combine read stale
+        data.  lagged=True reads the host mirror that the previous step's
+        exchange refreshed (no synchronisation; a failure shows at most one
+        step late); otherwise the device word is read."""
+        pe = getattr(self, "_peer", None)
+        if pe is None:
+            return
+        bad = int(pe["status_host"][0]) & 1 if lagged else self.exchange_failed()
+        if bad:
+            raise RuntimeError(f"shard {self.rank}: a peer exchange timed out waiting for a peer "
+                               "(the step's candidates or partials are not valid)")
 
     def peer_allgather(self, channel: int, dst: torch.Tensor) -> None:
         """Channel 0: the candidate records; 1: the partials block."""
@@ -280,6 +308,8 @@ def decode_step(local: Sequence[SeqShard], q: torch.Tensor, zone_keys: Optional[
         raise ValueError("pass every shard, or this process's one shard")
     s = local[0]
     peer = getattr(s, "_peer", None) is not None
+    if peer:
+        s.check_exchange(lagged=True)
     s.select_local(q)
     cand_all = torch.empty((plan.shards, bg, plan.record), dtype=torch.int64, device=dev)
     if peer:
@@ -291,6 +321,7 @@ def decode_step(local: Sequence[SeqShard], q: torch.Tensor, zone_keys: Optional[
     parts_all = torch.empty((plan.shards, s.partials.numel()), dtype=torch.float32, device=dev)
     if peer:
         s.peer_allgather(1, parts_all)
+        s._peer["status_host"].copy_(s._peer["status"], non_blocking=True)
     else:
         torch.distributed.all_gather_into_tensor(parts_all, s.partials, group=group)
     return combine(parts_all, plan.shards, bg, G, out)

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define IMI_ABI_VERSION 1
+#define IMI_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define IMI_API __attribute__((visibility("default")))
@@ -96,7 +96,13 @@ typedef struct imi_build_desc {
     void* workspace;
     size_t workspace_bytes;
     int32_t* status;                       /* [1] or NULL: bit 0 is set when a wait of the tensor-core
-                                              E-step gave up (the labels are then not valid) */
+                                              E-step gave up (the index is then not valid; the labels
+                                              that CTA owned are left at 0 so that later kernels stay
+                                              in bounds) */
+    unsigned long long* phase_ns;          /* [3] or NULL: device timestamps (ns, globaltimer) taken on
+                                              the stream when k-means starts, when it ends and when
+                                              the reorganize (CSR lists, padded metadata, list rows)
+                                              ends: the per-stage times of PipelineStats */
 } imi_build_desc;
 
 typedef struct imi_select_desc {
@@ -159,8 +165,9 @@ typedef struct imi_attn_desc {
                                               with it the last CTA of a group merges the
                                               splits (and re-zeroes its counter); without it a
                                               separate merge kernel runs */
-    int32_t* status;                       /* [1] or NULL: bit 0 is set when a wait for a row
-                                              copy gave up (the output is then not valid) */
+    int32_t* status;                       /* [1] or NULL: reserved.  The kernel has no spin-waits
+                                              (its row copies are cp.async groups), so it never sets
+                                              a bit; callers may pass NULL */
     float* o_part;                         /* [bg, G, 128] out or NULL: unnormalised output (sequence
                                               sharding); needs counters */
     float* ml_part;                        /* [bg, G, 2] out or NULL: (max in log2 units, sum) */

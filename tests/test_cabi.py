@@ -21,7 +21,7 @@ def test_library_exports_every_declared_symbol():
     for s in syms:
         assert hasattr(L, s), s
     assert set(syms) == set(_lib.EXPORTS)
-    assert L.imi_abi_version() == 1
+    assert L.imi_abi_version() == 2
 
 
 def test_descriptor_sizes_match_header():

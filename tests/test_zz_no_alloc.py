@@ -66,10 +66,12 @@ def _desc(idx, zk, zv, q, r, rc, out, splits):
     return d  # part_o / part_ml / counters stay NULL: the no-alloc entry does not read them
 
 
-def test_noalloc_attention_matches_regular_entry_two_calls():
+@pytest.mark.parametrize("splits", [8, 126])
+def test_noalloc_attention_matches_regular_entry_two_calls(splits):
+    # 126 splits: 4 groups * 126 * 4 heads * 520 B plus alignment is exactly the
+    # 1 MiB array, so the partial outputs reach its last byte
     idx, zk, zv, qs, rows, rcs, heads, G = _setup()
     L = _lib.load()
-    splits = 8
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     for t in range(2):  # two calls in a row reuse the same library-owned array
         ref = torch.empty(heads, G, 128, dtype=torch.bfloat16, device="cuda")
@@ -90,8 +92,12 @@ def test_noalloc_attention_matches_regular_entry_two_calls():
 def test_noalloc_attention_rejects_requests_beyond_the_array():
     idx, zk, zv, qs, rows, rcs, heads, G = _setup()
     L = _lib.load()
-    out = torch.empty(heads, G, 128, dtype=torch.bfloat16, device="cuda")
-    d = _desc(idx, zk, zv, qs[0], rows[0], rcs[0], out, 4096)  # 4 * 4096 * 4 * 520 B > 1 MiB
-    rc = L.imi_sparse_attention_noalloc(ctypes.byref(d), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert rc != 0
-    assert b"scratch" in L.imi_last_error()
+    out = torch.full((heads, G, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for splits in (127, 4096):  # 127: one split past the array; 4096: far past it
+        d = _desc(idx, zk, zv, qs[0], rows[0], rcs[0], out, splits)
+        rc = L.imi_sparse_attention_noalloc(ctypes.byref(d), stream)
+        assert rc != 0
+        assert b"scratch" in L.imi_last_error()
+    torch.cuda.synchronize()
+    assert bool((out.float() == 7.0).all())  # a rejected request launches nothing
