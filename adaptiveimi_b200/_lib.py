@@ -104,7 +104,7 @@ class AsyncDesc(ctypes.Structure):
         ("batch_keys", P), ("batch_values", P), ("sub_centroids", P), ("cell_code", P),
         ("shadow", P), ("shadow_dirty", P), ("pending", P), ("counts", P), ("delta_counts", P), ("delta_sums", P),
         ("ring_keys", P), ("ring_values", P), ("ring_cell_ids", P), ("ring_write_pos", P), ("ring_count", P),
-        ("ids_out", P), ("part_best", P), ("part_chunks", i32),
+        ("ids_out", P), ("part_best", P), ("part_chunks", i32), ("ring_store", i32),
     ]
 
 

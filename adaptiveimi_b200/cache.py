@@ -146,6 +146,11 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.async_update_batch = max(int(acfg.get("batch", 16)), 1)
         self.async_update_threshold = max(int(acfg.get("threshold", 16)), 1)
         self.async_update_delta_tokens = max(int(acfg.get("delta_tokens", 512)), 1)
+        # The reference's delta ring never receives its rows (async_update.py:151-157
+        # copies into a temporary made by tensor indexing), so by default its rows
+        # stay zero with padding ids and only its count grows; "store_delta_rows"
+        # stores the batch's keys, values and cells instead.
+        self.async_update_store_delta_rows = bool(acfg.get("store_delta_rows", False))
         self._async: List[Optional[Dict[str, object]]] = [None] * layer_num
         # per-device decode buffers (filled by prepare_cache)
         self.execution_buffer_keys_dict: Dict[str, torch.Tensor] = {}
@@ -329,6 +334,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             asd.ring_keys, asd.ring_values = st["ring_keys"].data_ptr(), st["ring_values"].data_ptr()
             asd.ring_cell_ids, asd.ring_write_pos = st["ring_ids"].data_ptr(), st["ring_pos"].data_ptr()
             asd.ring_count = st["ring_count"].data_ptr()
+            asd.ring_store = 1 if self.async_update_store_delta_rows else 0
             asd.part_best, asd.part_chunks = st["part_best"].data_ptr(), ops.async_chunks(idx.n_slots)
         return dict(sel=sel, att=att, app=app, append=ap, **{"async": asd})
 

@@ -321,9 +321,11 @@ __global__ void __launch_bounds__(256) imi_async_finish_kernel(AsyncArgs a) {
             a.delta_counts[cs] = dc;
         }
     }
-    // delta ring (async_update.py:146-161)
+    // delta ring (async_update.py:146-161); without ring_store only the write
+    // position and count advance, as in the reference (its indexed copy_ lands
+    // in a temporary)
     const int wp = a.ring_write_pos[h];
-    for (int e = tid; e < B * (a.dim / 8); e += blockDim.x) {
+    for (int e = tid; a.ring_store && e < B * (a.dim / 8); e += blockDim.x) {
         const int b = e / (a.dim / 8), q8 = e - b * (a.dim / 8);
         const int pos = (wp + b) % a.ring_cap;
         const uint4* sk = reinterpret_cast<const uint4*>(a.batch_keys + (hs * a.batch_cap + b) * a.dim) + q8;
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(256) imi_async_finish_kernel(AsyncArgs a) {
         reinterpret_cast<uint4*>(a.ring_keys + (hs * a.ring_cap + pos) * a.dim)[q8] = *sk;
         reinterpret_cast<uint4*>(a.ring_values + (hs * a.ring_cap + pos) * a.dim)[q8] = *sv;
     }
-    if (tid < B) a.ring_cell_ids[hs * a.ring_cap + (wp + tid) % a.ring_cap] = ids[tid];
+    if (a.ring_store && tid < B) a.ring_cell_ids[hs * a.ring_cap + (wp + tid) % a.ring_cap] = ids[tid];
     __syncthreads();
     if (tid == 0) {
         a.ring_write_pos[h] = (wp + B) % a.ring_cap;

@@ -291,8 +291,10 @@ def async_assign(*, index: IMIIndex, batch: int, batch_keys: torch.Tensor, batch
                  delta_counts: torch.Tensor, delta_sums: torch.Tensor, ring_keys: torch.Tensor,
                  ring_values: torch.Tensor, ring_cell_ids: torch.Tensor, ring_write_pos: torch.Tensor,
                  ring_count: torch.Tensor, threshold: int, ids_out: Optional[torch.Tensor] = None,
-                 part_best: Optional[torch.Tensor] = None) -> None:
+                 part_best: Optional[torch.Tensor] = None, ring_store: bool = False) -> None:
     """One batched decode-time cell assignment (async_update.py:122-161).
+    ring_store: store the batch's rows and cells in the delta ring (False: only
+    its position and count advance, as in the reference).
     part_best: int64 scratch [bg, ceil(n_slots / 512), batch] (allocated when absent)."""
     bg = batch_keys.shape[0]
     d = _lib.AsyncDesc()
@@ -311,6 +313,7 @@ def async_assign(*, index: IMIIndex, batch: int, batch_keys: torch.Tensor, batch
     if part_best is None or part_best.numel() < bg * chunks * batch:
         part_best = torch.empty((bg, chunks, batch), dtype=torch.int64, device=batch_keys.device)
     d.part_best, d.part_chunks = part_best.data_ptr(), chunks
+    d.ring_store = 1 if ring_store else 0
     L = _lib.load()
     _lib.check(L.imi_async_assign(ctypes.byref(d), _stream(batch_keys.device)), "imi_async_assign")
 

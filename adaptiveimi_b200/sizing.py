@@ -3,8 +3,8 @@
 * ``adaptive_k`` -- ``calculate_adaptive_k_values`` (layer_pipeline.cpp:177-228)
   with the config overrides of ``merge_all_chunks`` (layer_pipeline.cpp:1131-1163).
 * ``RetrievalSizes.from_capacity`` -- ``prepare_cache`` sizing
-  (runtime.py:31-63) and ``_ensure_metadata_buffers`` for IVF
-  (indexing.py:176-196).
+  (runtime.py:31-63), which also fixes the IVF slot count; the one divergence
+  (IVF builds with more cells than k*k) is described at the rule.
 """
 from __future__ import annotations
 
@@ -64,11 +64,22 @@ class RetrievalSizes:
         if subspace_parts == 4:
             k = max(int(round(max(n_tokens / 16.0, 1.0) ** 0.25)), 2)
             n_centroids = k ** 4 + 1
-        elif subspace_parts == 0:
-            n_centroids = max(int(round(n_tokens / 16.0)), 1) + 1
         else:
+            # prepare_cache (runtime.py:34-39) sizes every mode but S=4 as k*k + 1,
+            # IVF included, and it runs before the first layer's metadata is
+            # loaded, so _ensure_metadata_buffers' IVF rule (indexing.py:179-181)
+            # never fires there.
             k = max(int(math.sqrt(total_clusters)), 32)
             n_centroids = k * k + 1
+            if subspace_parts == 0:
+                # An IVF build makes up to round(n/16) cells (the build rounds as
+                # std::round, layer_pipeline.cpp:177-228).  When that exceeds k*k
+                # the reference's metadata copy into k*k + 1 slots fails
+                # (indexing.py:128-129, a size mismatch); here the slots widen to
+                # hold every cell instead, which is the only divergence.
+                ivf_cells = max(int(_cpp_round(n_tokens / 16.0)), 1)
+                if ivf_cells > k * k:
+                    n_centroids = ivf_cells + 1
         nprobe = max(round((n_centroids - 1) * retrieval_budget), 1)
         nprobe = min(nprobe, n_centroids - 1)
         max_tokens = max(int(retrieval_budget * list_capacity), 1)

@@ -260,6 +260,12 @@ typedef struct imi_async_desc {
     int32_t* ids_out;                      /* [bg, batch] or NULL */
     unsigned long long* part_best;         /* scratch [bg, part_chunks, batch] */
     int32_t part_chunks;                   /* = ceil(n_slots / 512) */
+    int32_t ring_store;                    /* 0: the ring's rows and cell ids are left as they are and
+                                              only its write position and count advance -- what the
+                                              reference does: its `ring[g, pos].copy_(x)` with a tensor
+                                              index `pos` (async_update.py:151-157) writes into a
+                                              temporary, so its ring keeps zero rows and padding ids;
+                                              1: the batch's keys, values and cells are stored */
 } imi_async_desc;
 
 typedef struct imi_apply_desc {

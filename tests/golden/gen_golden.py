@@ -15,8 +15,16 @@ code on them:
   same torch calls) followed by the reference's ``AdpIMI_Index.batch_access``
   page truncation (wave_buffer_cpu_hotcold.cpp:303-371, 897-929).
 
-The decode scorer (compute_impl.cu:62-103) is CUDA and is pinned on the GPU box
-instead (tests/test_gpu_scorer_ref.py runs the reference kernel built from source).
+* the config-1 geometry (one KV head of 130 976 middle tokens, k = 90 x 90,
+  the Llama k-means settings: 20 iterations, early stop 20 / 5e-4): the
+  reference's labels and sub-centroids stored whole, the CSR offsets, and
+  SHA-256 digests of the merged centroids and list rows
+  (``cfg1_build_digest.npz``).
+
+The decode scorer (compute_impl.cu:62-103) is CUDA; it is pinned on the GPU box
+by running the reference kernel, compiled from its source into oracle/_ref by
+oracle/build_ref_cuda.py, against the device scorer
+(tests/test_gpu_reference_pins.py).
 """
 from __future__ import annotations
 
@@ -90,6 +98,36 @@ def main():
     save_build("imi2_duplicates", dict(kind="duplicates", heads=2, parts=2, ks=[16, 16], max_iters=6, tol=0.0,
                                        min_iter=6, rel_tol=0.0), k, v, r)
     gen_selection(imi_ref, AI)
+    gen_cfg1_digest(imi_ref)
+
+
+# config-1 geometry: the inputs are head 0 of this call
+CFG1 = dict(heads=2, q_heads=8, ctx=131072, comps=64, seed=0, theta=500000.0, ks=[90, 90], max_iters=20,
+            tol=5e-4, min_iter=20, rel_tol=5e-4)
+
+
+def cfg1_inputs():
+    c = CFG1
+    K, V, Q = make_layer(c["heads"], c["q_heads"], c["ctx"], 128, c["comps"], c["seed"], c["theta"], n_queries=16)
+    return K, V, Q, K[:, 32:c["ctx"] - 64].contiguous(), V[:, 32:c["ctx"] - 64].contiguous()
+
+
+def gen_cfg1_digest(imi_ref):
+    c = CFG1
+    _, _, _, k, v = cfg1_inputs()
+    k0, v0 = k[:1].contiguous(), v[:1].contiguous()
+    r = imi_ref.build(k0, v0, 2, c["ks"], c["max_iters"], c["tol"], c["min_iter"], c["rel_tol"], 1)
+    na = int(r["cluster_counts"][0])
+    np.savez_compressed(
+        OUT / "cfg1_build_digest.npz",
+        meta=np.array(repr(c)), input_sha=np.array(sha(bits(k0), bits(v0))),
+        n_active=np.array(na), labels1=r["labels1"][0].numpy().astype(np.uint8),
+        labels2=r["labels2"][0].numpy().astype(np.uint8),
+        centroids1=r["centroids1"][0].numpy(), centroids2=r["centroids2"][0].numpy(),
+        cluster_offsets=r["cluster_offsets"][0][:na + 1].numpy(),
+        merged_sha=np.array(sha(r["centroids"][0][:na].numpy())),
+        list_keys_sha=np.array(sha(bits(r["list_keys"][0]))), list_values_sha=np.array(sha(bits(r["list_values"][0]))))
+    print("wrote cfg1_build_digest", na)
 
 
 def save_build(name, meta, k, v, r):
@@ -197,4 +235,10 @@ def gen_selection(imi_ref, AI):
 
 
 if __name__ == "__main__":
-    main()
+    if "--cfg1-only" in sys.argv:
+        build_ref.build()
+        sys.path.insert(0, str(ROOT / "oracle" / "_ref"))
+        import imi_ref  # noqa: E402
+        gen_cfg1_digest(imi_ref)
+    else:
+        main()

@@ -81,6 +81,8 @@ class RefSim:
             for h in range(self.kv):
                 ids = O.async_update(np.ascontiguousarray(bk[h]), self.shadow[h], self.counts[h], self.dcounts[h],
                                      self.dsums[h], self.acfg["threshold"])
+                if not self.acfg.get("store_delta_rows", False):
+                    continue  # the reference's ring keeps its zero rows and padding ids
                 for b in range(B):
                     p = (self.ring_pos + b) % R
                     self.ring_k[h, p] = bk[h, b]
@@ -119,11 +121,17 @@ class RefSim:
         return np.stack(outs), sels
 
 
-@pytest.mark.parametrize("async_on", [False, True])
-def test_cache_decode_matches_reference_simulation(async_on):
+@pytest.mark.parametrize("mode", ["off", "reference_ring", "stored_ring"])
+def test_cache_decode_matches_reference_simulation(mode):
+    """off: no async update.  reference_ring: the reference's behaviour, whose
+    delta ring never receives rows (zero rows with padding ids are attended
+    whenever the selection holds a dropped entry).  stored_ring: the ring holds
+    the batch's rows and cells."""
     torch.manual_seed(0)
     layers, kv, G, ctx, gen = 2, 4, 4, 4096, 24
-    acfg = {"enabled": True, "batch": 4, "threshold": 2, "delta_tokens": 16} if async_on else {}
+    async_on = mode != "off"
+    acfg = {"enabled": True, "batch": 4, "threshold": 2, "delta_tokens": 16,
+            "store_delta_rows": mode == "stored_ring"} if async_on else {}
     cache = adpimi_cache(
         valid_start=[0], layer_num=layers, batch_size=1, max_length=ctx + gen + 1, num_key_value_heads=kv,
         num_heads=kv * G, head_dim=128, dtype=torch.bfloat16, layer_mapping={"0": "cuda:0", "1": "cuda:0"},
