@@ -331,7 +331,7 @@ def run_ours(args):
                      "frac": round(achieved / hbm, 4), "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": ATTN_TRAFFIC_BYTES,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 3 launches of "
-                                       "the same kernel on the same geometry (profiles/imi_attn_kernel_cfg1_128K.md)",
+                                       "the same kernel on the same geometry",
                      "algorithmic_bytes_per_launch": int(attn["algo_bytes"]),
                      "avg_launch_us": round(attn_avg_us, 3), "launches_timed": attn["launches"],
                      "rows_per_launch": attn["rows_per_launch"]},
@@ -485,16 +485,22 @@ def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
     build_mkeys = build_heads * n / build_s / 1e6
     # ---- decode sample: the index of `build_heads` heads tiled over the 8 KV
     # groups (the selection and gather work per group does not depend on which
-    # head's index it scans).  Scorer (compute_impl.cu:62-103), top-k + token
-    # budget (retrieval.py:295-303) and page truncation
-    # (wave_buffer_cpu_hotcold.cpp:303-371) are the C port in oracle/; the
-    # attention over the gathered rows is torch fp32 on the host cores.
+    # head's index it scans), queried with the mixture queries the GPU arm uses.
+    #  * scorer: the C port of compute_impl.cu:62-103 (the reference scores on
+    #    the GPU; its CPU fallback is a torch einsum with other rounding);
+    #  * top-k + token budget: the reference's torch calls (retrieval.py:295-303);
+    #  * page truncation: the reference's own AdpIMI_Index.batch_access (C++,
+    #    oracle/_ref), cold cache;
+    #  * gather + attention: torch fp32 on the host cores (the reference's
+    #    weighted_flash_decoding is an absent GPU package).
+    from oracle.ref_index import PageTruncation, reference_select, rows_of
+
     sizes = RetrievalSizes.from_capacity(n, 2, CFG["retrieval_budget"], CFG["buffer_cluster_num"], 96 + 256)
     if mods is None:
         raise RuntimeError("decode CPU baseline needs the reference build (oracle/_ref)")
     ns = sizes.n_centroids
-    sizes_np = np.zeros((kvh, ns), np.int32)
-    offs_np = np.zeros((kvh, ns + 1), np.int32)
+    sizes_t = torch.zeros((kvh, ns), dtype=torch.int32)
+    offs_t = torch.zeros((kvh, ns + 1), dtype=torch.int32)
     cents = np.zeros((kvh, ns, D), np.float32)
     mask = np.ones((kvh, ns), np.uint8)
     lk = [None] * kvh
@@ -502,35 +508,40 @@ def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
     for h in range(kvh):
         src = h % build_heads
         c = int(r["cluster_counts"][src])
-        sizes_np[h, :c] = r["cluster_sizes"][src, :c].numpy()
-        offs_np[h, :c + 1] = r["cluster_offsets"][src, :c + 1].numpy()
-        offs_np[h, c + 1:] = offs_np[h, c]
+        sizes_t[h, :c] = r["cluster_sizes"][src, :c]
+        offs_t[h, :c + 1] = r["cluster_offsets"][src, :c + 1]
+        offs_t[h, c + 1:] = offs_t[h, c]
         cents[h, :c] = r["centroids"][src, :c].numpy()
         mask[h, :c] = 0
         lk[h] = r["list_keys"][src]
         lv[h] = r["list_values"][src]
-    q = torch.randn(kvh, G, D).to(torch.bfloat16)
-    qb = O.bf16_bits(q)
+    trunc = PageTruncation(mods[1], sizes_t, offs_t, sizes.nprobe, sizes.buffer_size, threads=min(cores, 8))
+    steps_total = sample_steps * sample_layers
+    qs, _, _ = decode_inputs([means], G, ctx, steps_total, "cpu", seed=0)
     t0 = time.perf_counter()
-    for _ in range(sample_steps * sample_layers):
+    for t in range(steps_total):
+        q = qs[t, 0, 0, 0].reshape(kvh, G, D)
+        qb = O.bf16_bits(q)
+        sims = torch.from_numpy(np.stack([O.scores(qb[h], cents[h], mask[h]) for h in range(kvh)]))
+        sel = reference_select(sims, sizes_t, sizes.nprobe, sizes.max_retrieval_tokens, sizes.padding_cluster_id)
+        runs = trunc.access(sel)
         for h in range(kvh):
-            sc = O.scores(qb[h], cents[h], mask[h])
-            sel, _ = O.select(sc, sizes_np[h], sizes.nprobe, sizes.max_retrieval_tokens, sizes.buffer_size, 8,
-                              sizes.padding_cluster_id)
-            ridx = torch.cat([torch.arange(int(offs_np[h, c]), int(offs_np[h, c]) + int(sizes_np[h, c]))
-                              for c in sel]) if len(sel) else torch.zeros(0, dtype=torch.int64)
+            ridx = torch.from_numpy(rows_of(runs[h]))
             kr = lk[h][ridx].float()
             vr = lv[h][ridx].float()
-            s = (q[h].float() @ kr.T) / math.sqrt(D)
-            torch.softmax(s, -1) @ vr
+            s_ = (q[h].float() @ kr.T) / math.sqrt(D)
+            torch.softmax(s_, -1) @ vr
     dec_s = time.perf_counter() - t0
-    us = dec_s * 1e6 / (sample_steps * sample_layers)
-    return {"value": round(us, 1), "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"decode (C port of the scorer/selection/truncation + torch fp32 attention): "
-                      f"{sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, {ctx}-token context; "
-                      f"build (the reference's own kmeans_execute + reorganize_from_kmeans): "
-                      f"build: {build_heads} heads x {n} keys, k={ks[0]}x{ks[1]}, {KMEANS['max_iters']} iters",
-            "build": {"value": round(build_mkeys, 4), "unit": "Mkeys/s", "seconds": round(build_s, 2)}}
+    us = dec_s * 1e6 / steps_total
+    return {"value": round(us, 1), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"decode: {sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, {ctx}-token context, "
+                      f"mixture queries; scorer = C port of compute_impl.cu, top-k/budget = the reference's torch "
+                      f"calls, page truncation = the reference's AdpIMI_Index.batch_access (C++), gather + "
+                      f"attention = torch fp32",
+            "build": {"value": round(build_mkeys, 4), "unit": "Mkeys/s", "seconds": round(build_s, 2),
+                      "kind": kind, "cores": cores,
+                      "sample": f"the reference's own kmeans_execute + reorganize_from_kmeans (oracle/_ref): "
+                                f"{build_heads} heads x {n} keys, k={ks[0]}x{ks[1]}, {KMEANS['max_iters']} iters"}}
 
 
 def run_reference(args):
