@@ -223,6 +223,11 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
     _lib.check(L.imi_select_cells(ctypes.byref(d), _stream(q.device)), "imi_select_cells")
 
 
+def fused_scratch_size(bg: int, n_slots: int, splits: int) -> int:
+    """Bytes of the fused decode launch's scratch (imi_decode_fused_scratch_size)."""
+    return int(_lib.load().imi_decode_fused_scratch_size(bg, n_slots, splits))
+
+
 def default_splits(bg: int, rows_per_group: int, sms: int = 148, exec_capacity: Optional[int] = None) -> int:
     """CTAs per KV group for the split-K attention: one wave (one CTA per SM,
     the kernel's shared-memory ring allows one) and at least 64 rows per CTA.
@@ -265,6 +270,60 @@ def sparse_attention(*, q: torch.Tensor, row_index: torch.Tensor, row_count: tor
     d.status = status.data_ptr() if status is not None else None
     L = _lib.load()
     _lib.check(L.imi_sparse_attention(ctypes.byref(d), _stream(q.device)), "imi_sparse_attention")
+    return out
+
+
+def decode_attend(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: int, buffer_pages: int,
+                  page_size: int, padding_id: int, static_len: int, exec_capacity: int, sel_cells: torch.Tensor,
+                  sel_count: torch.Tensor, row_index: torch.Tensor, row_count: torch.Tensor, static_keys: torch.Tensor,
+                  static_values: torch.Tensor, out: torch.Tensor, part_o: torch.Tensor, part_ml: torch.Tensor,
+                  counters: torch.Tensor, splits: int, kept_count: Optional[torch.Tensor] = None,
+                  slot_bound: int = 0, fused_scratch: Optional[torch.Tensor] = None,
+                  status: Optional[torch.Tensor] = None, delta_cell_ids: Optional[torch.Tensor] = None,
+                  delta_count: Optional[torch.Tensor] = None, delta_keys: Optional[torch.Tensor] = None,
+                  delta_values: Optional[torch.Tensor] = None, scores_out: Optional[torch.Tensor] = None,
+                  phase_ns: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Selection + attention of one layer through imi_decode_attend: one fused
+    launch when ``fused_scratch`` (zeroed, ``fused_scratch_size`` bytes) is given
+    and the layer fits it, else the select kernel then the attention kernel."""
+    bg, G, D = q.shape
+    d = _lib.SelectDesc()
+    d.bg, d.G, d.dim, d.n_slots, d.parts, d.kmax = bg, G, D, index.n_slots, index.parts, index.kmax
+    d.ks = _ks4(index.ks)
+    d.q = q.data_ptr()
+    d.sub_centroids, d.cell_code = index.sub_centroids.data_ptr(), index.cell_code.data_ptr()
+    d.cell_sizes, d.cell_offsets = index.cell_sizes.data_ptr(), index.cell_offsets.data_ptr()
+    d.cell_mask, d.centroids = index.cell_mask.data_ptr(), index.centroids.data_ptr()
+    d.nprobe, d.max_tokens, d.buffer_pages, d.page_size, d.padding_id = nprobe, max_tokens, buffer_pages, \
+        page_size, padding_id
+    d.static_len, d.exec_capacity = static_len, exec_capacity
+    if delta_cell_ids is not None:
+        d.delta_cell_ids, d.delta_count = delta_cell_ids.data_ptr(), delta_count.data_ptr()
+        d.delta_capacity = delta_cell_ids.shape[1]
+    d.sel_cells, d.sel_count = sel_cells.data_ptr(), sel_count.data_ptr()
+    d.kept_count = kept_count.data_ptr() if kept_count is not None else None
+    d.row_index, d.row_count = row_index.data_ptr(), row_count.data_ptr()
+    d.scores_out = scores_out.data_ptr() if scores_out is not None else None
+    d.phase_ns = phase_ns.data_ptr() if phase_ns is not None else None
+    d.slot_bound = int(slot_bound)
+    if fused_scratch is not None:
+        d.fused_scratch, d.fused_scratch_bytes = fused_scratch.data_ptr(), fused_scratch.numel()
+    a = _lib.AttnDesc()
+    a.bg, a.G, a.splits, a.exec_capacity = bg, G, splits, exec_capacity
+    a.scale = 1.0 / math.sqrt(D)
+    a.q, a.row_index, a.row_count = q.data_ptr(), row_index.data_ptr(), row_count.data_ptr()
+    a.list_keys, a.list_values, a.list_rows = index.list_keys.data_ptr(), index.list_values.data_ptr(), \
+        index.list_keys.shape[1]
+    a.static_keys, a.static_values, a.static_rows = static_keys.data_ptr(), static_values.data_ptr(), \
+        static_keys.shape[-2]
+    if delta_keys is not None:
+        a.delta_keys, a.delta_values, a.delta_rows = delta_keys.data_ptr(), delta_values.data_ptr(), \
+            delta_keys.shape[-2]
+    a.part_o, a.part_ml, a.out = part_o.data_ptr(), part_ml.data_ptr(), out.data_ptr()
+    a.counters = counters.data_ptr()
+    a.status = status.data_ptr() if status is not None else None
+    L = _lib.load()
+    _lib.check(L.imi_decode_attend(ctypes.byref(d), ctypes.byref(a), None, _stream(q.device)), "imi_decode_attend")
     return out
 
 
