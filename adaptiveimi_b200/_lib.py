@@ -49,7 +49,7 @@ class SelectDesc(ctypes.Structure):
         ("sel_cells", P), ("sel_count", P), ("kept_count", P), ("row_index", P), ("row_count", P),
         ("scores_out", P), ("phase_ns", P),
         ("slot_bound", i32), ("key_base", i32), ("cand_out", P),
-        ("fused_scratch", P), ("fused_scratch_bytes", sz),
+        ("fuse", i32),
     ]
 
 
@@ -121,7 +121,6 @@ EXPORTS = (
     "imi_query_group_similarities", "imi_select_cells", "imi_sparse_attention", "imi_decode_append",
     "imi_async_assign", "imi_apply_updates", "imi_decode_attend", "imi_decode_layer",
     "imi_merge_candidates", "imi_combine_partials", "imi_sparse_attention_noalloc", "imi_peer_allgather",
-    "imi_decode_fused_scratch_size",
 )
 
 _lib = None
@@ -148,8 +147,6 @@ def load():
         L.imi_build_workspace_size.restype = sz
         L.imi_build_workspace_size.argtypes = [i32, i32, i32, i32, P]
         L.imi_build_index.argtypes = [ctypes.POINTER(BuildDesc), P]
-        L.imi_decode_fused_scratch_size.restype = sz
-        L.imi_decode_fused_scratch_size.argtypes = [i32, i32, i32]
         L.imi_query_group_similarities.argtypes = [P, P, P, i32, i32, i32, i32, i64, P]
         L.imi_select_cells.argtypes = [ctypes.POINTER(SelectDesc), P]
         L.imi_sparse_attention.argtypes = [ctypes.POINTER(AttnDesc), P]

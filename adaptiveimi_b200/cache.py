@@ -157,15 +157,22 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.execution_buffer_values_dict: Dict[str, torch.Tensor] = {}
         self.valid_lengths_dict: Dict[str, torch.Tensor] = {}
         self._dec: Dict[str, Dict[str, torch.Tensor]] = {}
-        self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity,
-                                          exec_capacity=self.execution_stride)
+        # selection and attention of a layer in one launch where the layer fits
+        # (runtime_config["pipeline"]["fuse_decode"], default on); its splits are
+        # whole 8-CTA clusters
+        self.fuse_decode = bool(self.runtime_config["pipeline"].get("fuse_decode", True))
+        sms = 148
+        if torch.cuda.is_available():
+            sms = torch.cuda.get_device_properties(torch.device(self.layer_mapping["0"])).multi_processor_count
+        if self.fuse_decode:
+            self.splits = ops.fused_splits(self.batch_groups, sms)
+        else:
+            self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity,
+                                              sms=sms, exec_capacity=self.execution_stride)
         # optional measurement hooks (bench.py): per-call row counts and CUDA
         # events around the attention launch, both on the launching stream
         self._pending = None  # deferred append: (layer, k, v, head stride, pos, batch slot, async batch)
         self._fused = False   # set by prepare_cache: appends ride on the layer's attention call
-        # selection and attention of a layer in one launch where the layer fits
-        # (runtime_config["pipeline"]["fuse_decode"], default on)
-        self.fuse_decode = bool(self.runtime_config["pipeline"].get("fuse_decode", True))
         self._dev_index = [torch.device(self.layer_mapping[str(i)]).index or 0 for i in range(layer_num)]
         self._rc: List[Optional[torch.Tensor]] = [None] * layer_num
         self.row_count_log: Optional[torch.Tensor] = None
@@ -252,11 +259,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
                 part_o=torch.empty((bg, self.splits, G, self.head_dim), dtype=torch.float32, device=dev),
                 part_ml=torch.empty((bg, self.splits, G, 2), dtype=torch.float32, device=dev),
                 counters=torch.zeros((bg,), dtype=torch.int32, device=dev),
-                # one decode layer as one launch (selection + attention): its
-                # scratch, zeroed once; the kernel re-arms what it counts with
-                fused=torch.zeros((max(1, ops.fused_scratch_size(bg, self.n_centroids, self.splits)),),
-                                  dtype=torch.uint8, device=dev),
-                status=torch.zeros((1,), dtype=torch.int32, device=dev),
             )
             self.execution_buffer_keys_dict[dev] = rows
             self.execution_buffer_values_dict[dev] = rows
@@ -296,8 +298,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         sel.sel_cells, sel.sel_count, sel.kept_count = buf["sel"].data_ptr(), buf["sel_count"].data_ptr(), \
             buf["kept"].data_ptr()
         sel.row_index = buf["rows"].data_ptr()
-        if self.fuse_decode:
-            sel.fused_scratch, sel.fused_scratch_bytes = buf["fused"].data_ptr(), buf["fused"].numel()
+        sel.fuse = 1 if self.fuse_decode else 0
         # every slot at or above the largest n_active is padding: one host read
         # per layer, here at preparation, lets the selection skip them
         sel.slot_bound = int(idx.n_active.max().item())
@@ -315,7 +316,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             att.delta_rows = self.async_update_delta_tokens
         att.part_o, att.part_ml = buf["part_o"].data_ptr(), buf["part_ml"].data_ptr()
         att.counters = buf["counters"].data_ptr()
-        att.status = buf["status"].data_ptr()
         app = None
         if st is not None:
             app = _lib.ApplyDesc()
@@ -565,16 +565,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.layer_started = [False] * self.layer_num
         self.cache_prepared = False
         self._async = [None] * self.layer_num
-
-    def check_status(self) -> None:
-        """Raise when a decode launch reported a failure on the device (bit 1:
-        a fused launch's bounded wait for the CTAs of a group ran out, so that
-        step's output is not valid).  Reads the status words (synchronises)."""
-        for dev, buf in self._dec.items():
-            st = int(buf["status"].item())
-            if st:
-                raise RuntimeError(f"IMI decode on {dev} reported device status 0x{st:x}: a bounded wait of the "
-                                   "fused decode launch ran out; the affected outputs are not valid")
 
     def cleanup(self) -> None:
         self._pending = None

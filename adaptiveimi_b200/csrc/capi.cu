@@ -204,17 +204,13 @@ static int launch_decode_attend(const imi_select_desc* sel, const imi_attn_desc*
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
     }
     const char* why = "";
-    if (sel->fused_scratch && imi::fused_eligible(*sel, *attn, sel->fused_scratch_bytes, &why))
+    if (sel->fuse && imi::fused_eligible(*sel, *attn, &why))
         return cuda_status(imi::launch_decode_fused(*sel, *attn, S(stream), app), "imi_decode_attend(fused)");
     cudaError_t e = imi::launch_select(*sel, S(stream), app);
     if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
     return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");
 }
 
-size_t imi_decode_fused_scratch_size(int32_t bg, int32_t n_slots, int32_t splits) {
-    if (bg <= 0 || n_slots <= 0 || splits <= 0) return 0;
-    return imi::fused_scratch_bytes(bg, n_slots, splits);
-}
 
 int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
                       void* stream) {

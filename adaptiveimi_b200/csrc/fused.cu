@@ -1,97 +1,136 @@
 // fused.cu -- one decode layer's retrieval and attention in a single launch
-// (sm_100a): cell scoring, the two selection boundaries, the execution-row
-// layout and the split-K gather attention with its split merge.
+// (sm_100a): cell scoring, the selection, the execution-row layout and the
+// split-K gather attention with its split merge.
 //
-// Semantics: exactly those of the select kernel (select.cu; retrieval.py:295-303,
+// Semantics: those of the select kernel (select.cu; retrieval.py:295-303,
 // wave_buffer_cpu_hotcold.cpp:303-371, async_update.py:46-76) followed by the
 // attention kernel (attention.cu; weighted_flash_decoding as retrieval.py:439-447
-// calls it).  Only the orchestration differs.
+// calls it), with one difference in order only: the selected cells, and so their
+// rows, come out in rank order (descending score), the order of the
+// reference's own top-k list and of its page walk, rather than slot order.
 //
-// Grid (splits, groups), one CTA per SM, a cooperative launch (every CTA is
-// resident at once, so a CTA may wait for the others of its group).  Each CTA:
-//  1. scores its slice of the group's occupied slots (the separable fma chains
-//     of the select kernel, bit-identical to compute_impl.cu:62-103) and writes
-//     the slice's ranking keys and sizes to the group's scratch, then arrives at
-//     the group's counter (release);
-//  2. waits for the group's other CTAs (acquire, bounded: a wait that runs out
-//     sets bit 1 of the attention status and the CTA contributes nothing);
-//  3. loads every key of the group into shared memory and finds both
-//     boundaries itself (all CTAs of a group reach the same thresholds, so no
-//     broadcast is needed);
-//  4. lays out the execution rows as runs in shared memory -- the steady zone,
-//     each selected cell's list rows (cells in slot order), each matching delta
-//     row -- so a row's source is one binary search away;
-//  5. streams its contiguous share of the group's 16-row tiles through the
-//     attention loop of attention.cu and writes one (m, l, o) partial; the last
-//     CTA of the group (a ticket) merges the partials into the output and
-//     re-arms the group's counters.
-// CTA 0 of a group writes the selection outputs (selected cells, counts); every
-// CTA writes the row-list entries of its own tiles when a row list is given.
-// Compared with the select kernel followed by the attention kernel this saves
-// the hand-off between the two launches, the cluster barriers of the
-// selection, and the row list's round trip through memory.
+// Grid (clusters x 8, groups) with clusters of 8 CTAs, one CTA per SM.  Every
+// cluster of a group computes the group's selection (the clusters of a group
+// agree, so no CTA ever waits for another cluster), then every CTA of the group
+// streams its share of the rows:
+//  1. each CTA scores one eighth of the occupied slots (the separable fma chains
+//     of the select kernel, bit-identical to compute_impl.cu:62-103) and sorts
+//     its slice's ranking keys (bitonic, shared memory);
+//  2. through distributed shared memory the sorted slices, and each slot's key,
+//     size and list offset, reach the cluster's leader;
+//  3. the leader merges the eight sorted slices (a merge-path tree, only the
+//     first nprobe + 1 ranks), scans their tokens and pages in rank order and
+//     finds the selection (all three rules) and the kept list (rank and token
+//     rules); it lays the execution rows out as runs -- the steady zone, each
+//     selected cell's list rows, each matching delta row -- and the cluster's
+//     CTAs copy that run table;
+//  4. each CTA streams its contiguous share of the group's 16-row tiles through
+//     the attention loop of attention.cu (a row's source is a binary search in
+//     the run table away) and writes one (m, l, o) partial; the last CTA of the
+//     group (an atomic ticket) merges the partials into the output.
+// The first cluster of a group writes the selection outputs; every CTA writes
+// the row-list entries of its own tiles when a row list is given.  Every wait
+// is a hardware cluster barrier; the split merge is a ticket, not a wait.
+#include <cooperative_groups.h>
+
 #include "attn_core.cuh"
 #include "common.cuh"
 #include "imi_internal.h"
 #include "select_core.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace imi {
 
-constexpr int FU_THREADS = AT_WARPS * 32;  // the streaming warps do the selection too
-constexpr int FU_WARPS = AT_WARPS;
-constexpr int FU_CPT = 4;                  // slots per thread when scoring a slice
-constexpr unsigned FU_SPIN_LIMIT = 1u << 21;
+constexpr int FC_CL = 8;                    // CTAs per cluster
+constexpr int FC_THREADS = AT_WARPS * 32;   // the streaming warps do the selection too
+constexpr int FC_WARPS = AT_WARPS;
+constexpr int FC_CPT = 8;                   // slots per thread of a slice
+constexpr int FC_SLICE_MAX = FC_THREADS * FC_CPT;  // 2048 slots per CTA, 16384 per cluster
+constexpr int FC_RANKS_MAX = 2048;          // merged ranks the leader scans (nprobe + 1)
 
 struct FusedArgs {
     SelectArgs s;
     AttnArgs a;
-    AppendArgs ap;                // ap.new_keys set: the step's steady-zone append, done before the barrier
-    unsigned long long* keys;     // [bg, n_slots] scratch: ranking keys (0: not a candidate)
-    int32_t* sizes;               // [bg, n_slots] scratch
-    unsigned long long* range;    // [bg, splits, 2] scratch: each slice's lowest and highest key
-    uint32_t* arrive;             // [bg] group counters: zero before the first call, re-armed by the kernel
-    int runs_cap;                 // run-table entries (static + nprobe + delta capacity)
+    AppendArgs ap;   // ap.new_keys set: the step's steady-zone append
+    int runs_cap;    // run-table entries: steady zone + nprobe + delta capacity
 };
 
-// Byte offsets of the shared-memory regions (identical in every CTA).
-struct FusedLayout {
-    size_t keys, sizes, qs, tab, tables, sel_end, runs, total;
+struct FcHdr {
+    unsigned long long red64[FC_WARPS];
+    unsigned int red32[FC_WARPS];
+    int redi[FC_WARPS];
+    int cnt[FC_CL];        // candidates in each CTA's sorted slice (leader)
+    int len1[4], len2[2];  // merge-tree level lengths (leader)
+    int A, B;              // first rank out of the selection / of the kept list
+    int tokA;              // tokens of the selected cells
 };
 
-__host__ __device__ inline size_t fu_align(size_t x) { return (x + 127) & ~size_t(127); }
+struct FcLayout {
+    size_t keys, sizes, offs, lists, sortbuf, b1, b2, fin, qs, tab, tables, runs, total;
+};
 
-__host__ __device__ inline FusedLayout fused_layout(const SelectArgs& a, int runs_cap) {
+__host__ __device__ inline size_t fc_align(size_t x) { return (x + 127) & ~size_t(127); }
+__host__ __device__ inline int fc_pow2(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+__host__ __device__ inline int fc_ne(const SelectArgs& a) {
+    return (a.slot_bound > 0 && a.slot_bound < a.n_slots) ? a.slot_bound : a.n_slots;
+}
+__host__ __device__ inline int fc_ranks(const SelectArgs& a) {
+    const int ne = fc_ne(a);
+    return ne < a.nprobe + 1 ? ne : a.nprobe + 1;
+}
+
+// Shared-memory regions (identical offsets in every CTA: DSMEM addresses are
+// offsets).  The selection area is reused as the attention ring once the run
+// table (past both) is built.
+__host__ __device__ inline FcLayout fc_layout(const SelectArgs& a, int runs_cap) {
     const int S = a.parts == 0 ? 1 : a.parts;
     const int sub = a.dim / S;
     int table = 1;
     for (int s = 0; s < S - 1; ++s) table *= a.ks[s];
-    const int ne = (a.slot_bound > 0 && a.slot_bound < a.n_slots) ? a.slot_bound : a.n_slots;
-    FusedLayout L;
-    size_t o = fu_align(sizeof(SelHdr));
-    L.keys = o;
-    o = fu_align(o + 8 * (size_t)ne);
-    L.sizes = o;
-    o = fu_align(o + 4 * (size_t)ne);
+    const int ne = fc_ne(a);
+    const int chunk = (ne + FC_CL - 1) / FC_CL;
+    const int M = fc_ranks(a);
+    FcLayout L;
+    size_t o = fc_align(sizeof(FcHdr));
+    L.keys = o;  // [ne] leader: key by slot
+    o = fc_align(o + 8 * (size_t)ne);
+    L.sizes = o;  // [ne] leader: size by slot
+    o = fc_align(o + 4 * (size_t)ne);
+    L.offs = o;  // [ne] leader: list offset by slot
+    o = fc_align(o + 4 * (size_t)ne);
+    L.lists = o;  // [8 * chunk] leader: the sorted slices
+    o = fc_align(o + 8 * (size_t)FC_CL * chunk);
+    L.sortbuf = o;  // [pow2(chunk)] this CTA's slice being sorted
+    o = fc_align(o + 8 * (size_t)fc_pow2(chunk));
+    L.b1 = o;  // [4 * M] merge level 1
+    o = fc_align(o + 8 * 4 * (size_t)M);
+    L.b2 = o;  // [2 * M] merge level 2
+    o = fc_align(o + 8 * 2 * (size_t)M);
+    L.fin = o;  // [M] merged ranks
+    o = fc_align(o + 8 * (size_t)M);
     L.qs = o;
-    o = fu_align(o + 4 * (size_t)a.dim);
+    o = fc_align(o + 4 * (size_t)a.dim);
     L.tab = o;
-    o = fu_align(o + 4 * ((size_t)table + 4));
+    o = fc_align(o + 4 * ((size_t)table + 4));
     L.tables = o;
     size_t tables = 0;
     if (S > 1) {
         for (int s = 0; s < S; ++s) tables += (size_t)sub * sl_ld(a.ks[s]) * sizeof(float);
         if (S > 2) tables += (256 + (size_t)a.ks[0] * a.ks[1]) * sizeof(float);
     }
-    o = fu_align(o + tables);
-    L.sel_end = o;
-    // the run table lives past both the selection area and the attention ring
+    o = fc_align(o + tables);
     const size_t ring = (size_t)AT_RING_BYTES;
-    L.runs = fu_align(o > ring ? o : ring);
-    L.total = L.runs + 8 * ((size_t)runs_cap + 1);
+    L.runs = fc_align(o > ring ? o : ring);  // [4] run count and rows, then the run table
+    L.total = L.runs + 16 + 4 * (2 * (size_t)runs_cap + 1);
     return L;
 }
 
-IMI_DEV void fu_stamp(const SelectArgs& a, int h, int k, bool on) {
+IMI_DEV void fc_stamp(const SelectArgs& a, int h, int k, bool on) {
     if (on) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -99,11 +138,80 @@ IMI_DEV void fu_stamp(const SelectArgs& a, int h, int k, bool on) {
     }
 }
 
-__global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const __grid_constant__ FusedArgs f) {
+// Bitonic sort of buf[0, P) (P a power of two), descending, all threads.
+// Stages whose pairs stay inside one warp's 64-element chunks sync the warp
+// only.
+IMI_DEV void fc_sort_desc(unsigned long long* buf, int P) {
+    const int tid = threadIdx.x;
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int p = tid; p < (P >> 1); p += FC_THREADS) {
+                const int i = 2 * j * (p / j) + (p % j), l = i + j;
+                const unsigned long long x = buf[i], y = buf[l];
+                const bool desc = (i & k) == 0;
+                if (desc ? (x < y) : (x > y)) {
+                    buf[i] = y;
+                    buf[l] = x;
+                }
+            }
+            const int nj = j > 1 ? (j >> 1) : (k << 1 <= P ? k : 0);
+            if (j >= 64 || nj >= 64 || nj == 0)
+                __syncthreads();
+            else
+                __syncwarp();
+        }
+    }
+    __syncthreads();
+}
+
+// Output ranks [o0, o1) of the descending merge of X[0, nx) and Y[0, ny)
+// (unique keys): the merge-path split of diagonal o0, then a sequential merge.
+IMI_DEV void fc_merge_range(const unsigned long long* X, int nx, const unsigned long long* Y, int ny,
+                            unsigned long long* out, int o0, int o1) {
+    if (o0 >= o1) return;
+    int lo = max(0, o0 - ny), hi = min(o0, nx);
+    while (lo < hi) {  // the smallest i whose X[i] ranks after Y[o0 - 1 - i]
+        const int i = (lo + hi) >> 1;
+        const int j = o0 - 1 - i;
+        if (j < 0 || X[i] < Y[j])
+            hi = i;
+        else
+            lo = i + 1;
+    }
+    int i = lo, j = o0 - lo;
+    for (int o = o0; o < o1; ++o) {
+        const bool takeX = j >= ny || (i < nx && X[i] > Y[j]);
+        out[o] = takeX ? X[i++] : Y[j++];
+    }
+}
+
+// One level of the merge tree: `pairs` merges of (in + 2m * stride_in, len[2m])
+// with (in + (2m+1) * stride_in, len[2m+1]) into out + m * stride_out, each
+// keeping its first M ranks; lengths into len_out.
+IMI_DEV void fc_merge_level(const unsigned long long* in, const int* len_in, int stride_in, unsigned long long* out,
+                            int* len_out, int stride_out, int pairs, int M) {
+    const int per = FC_THREADS / pairs;
+    const int m = threadIdx.x / per, t = threadIdx.x - m * per;
+    if (m < pairs) {
+        const int nx = len_in[2 * m], ny = len_in[2 * m + 1];
+        const int L = min(nx + ny, M);
+        const int step = (L + per - 1) / per;
+        fc_merge_range(in + (size_t)(2 * m) * stride_in, nx, in + (size_t)(2 * m + 1) * stride_in, ny,
+                       out + (size_t)m * stride_out, min(L, t * step), min(L, (t + 1) * step));
+        if (t == 0) len_out[m] = L;
+    }
+    __syncthreads();
+}
+
+__global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
+    imi_decode_fused_kernel(const __grid_constant__ FusedArgs f) {
     extern __shared__ __align__(128) unsigned char fsm[];
     const SelectArgs& a = f.s;
     const AttnArgs& at = f.a;
-    const int h = blockIdx.y, split = blockIdx.x, J = gridDim.x;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int cl = blockIdx.x / FC_CL;  // this cluster among the group's clusters
+    const int h = blockIdx.y;
     const int tid = threadIdx.x, wid = tid >> 5, lid = tid & 31;
     const size_t hs = (size_t)h;
     const int S = a.parts == 0 ? 1 : a.parts;
@@ -111,18 +219,18 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
     const int sub_shift = __ffs(sub) - 1;
     const int k_last = a.ks[S - 1];
     const int n = a.n_slots;
-    const int ne = (a.slot_bound > 0 && a.slot_bound < n) ? a.slot_bound : n;
-    SelRules rules;
-    rules.nprobe = a.nprobe;
-    rules.max_tokens = a.max_tokens;
-    rules.buffer_pages = a.buffer_pages;
-    rules.page_size = a.page_size;
-    rules.pg_shift = __ffs(a.page_size) - 1;
-    rules.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
-    const FusedLayout Lo = fused_layout(a, f.runs_cap);
-    SelHdr& sm = *reinterpret_cast<SelHdr*>(fsm);
+    const int ne = fc_ne(a);
+    const int M = fc_ranks(a);
+    const FcLayout Lo = fc_layout(a, f.runs_cap);
+    FcHdr& hd = *reinterpret_cast<FcHdr*>(fsm);
     unsigned long long* skey = reinterpret_cast<unsigned long long*>(fsm + Lo.keys);
     int* ssz = reinterpret_cast<int*>(fsm + Lo.sizes);
+    int* soff = reinterpret_cast<int*>(fsm + Lo.offs);
+    unsigned long long* lists = reinterpret_cast<unsigned long long*>(fsm + Lo.lists);
+    unsigned long long* sortbuf = reinterpret_cast<unsigned long long*>(fsm + Lo.sortbuf);
+    unsigned long long* b1 = reinterpret_cast<unsigned long long*>(fsm + Lo.b1);
+    unsigned long long* b2 = reinterpret_cast<unsigned long long*>(fsm + Lo.b2);
+    unsigned long long* fin = reinterpret_cast<unsigned long long*>(fsm + Lo.fin);
     float* qs = reinterpret_cast<float*>(fsm + Lo.qs);
     float* tab = reinterpret_cast<float*>(fsm + Lo.tab);
     float* cT = reinterpret_cast<float*>(fsm + Lo.tables);
@@ -130,38 +238,45 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
     float* cP = cT + (S > 1 ? sub * ldT : 0);
     float* bufA = cP + (S > 1 ? prefix_table_offset(a, S - 1, sub) : 0);
     float* bufB = bufA + 256;
-    int* run_start = reinterpret_cast<int*>(fsm + Lo.runs);  // [runs + 1] first execution row of each run
-    int* run_src = run_start + f.runs_cap + 1;               // [runs] row-list entry of the run's first row
-    const bool stamping = a.phase_ns != nullptr && tid == 0 && split == 0;
-    __shared__ int s_fail, s_nruns, s_total;
+    // outside the ring, so other CTAs may read the leader's copy while it streams
+    int* run_hdr = reinterpret_cast<int*>(fsm + Lo.runs);  // [0] runs, [1] execution rows
+    int* run_start = run_hdr + 4;                          // [runs + 1] first execution row of each run
+    int* run_src = run_start + f.runs_cap + 1;             // [runs] row-list entry of the run's first row
+    const bool stamping = a.phase_ns != nullptr && tid == 0 && rank == 0 && cl == 0;
 
-    fu_stamp(a, h, 0, stamping);
-    // the next layer's kernel may be scheduled once every CTA here runs; it
-    // waits for this grid's completion before touching memory
+    fc_stamp(a, h, 0, stamping);
+    // the next kernel may be scheduled once every CTA here runs; it waits for
+    // this grid's completion before touching memory
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    const int chunk = (ne + J - 1) / J;
-    const int c0 = min(ne, split * chunk), c1 = min(ne, c0 + chunk);
+    // first half of the cluster barrier that guards the DSMEM stores
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    const int chunk = (ne + FC_CL - 1) / FC_CL;
+    const int c0 = min(ne, rank * chunk), c1 = min(ne, c0 + chunk);
     {  // warm L2 for this CTA's inputs while the previous kernel drains
         auto pf = [](const void* ptr) { asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr)); };
         const size_t base = hs * n;
-        for (int i = c0 + tid * 32; i < c1; i += FU_THREADS * 32) {
+        for (int i = c0 + tid * 32; i < c1; i += FC_THREADS * 32) {
             pf(a.cell_code + base + i);
             pf(a.cell_sizes + base + i);
+            pf(a.cell_offsets + hs * (n + 1) + i);
             if ((i & 127) == 0) pf(a.cell_mask + base + i);
         }
         if (S > 1) {
             const char* sc = reinterpret_cast<const char*>(a.sub_centroids + hs * S * a.kmax * sub);
             const size_t bytes = (size_t)S * a.kmax * sub * 4;
-            for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)FU_THREADS * 128) pf(sc + o);
+            for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)FC_THREADS * 128) pf(sc + o);
         }
+        if (tid < (a.G * a.dim * 2 + 127) / 128)
+            pf(reinterpret_cast<const char*>(a.q + hs * a.G * a.dim) + tid * 128);
     }
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    if (f.ap.new_keys && split == J - 1 && wid < 2) append_group(f.ap, h, wid, lid);
+    if (f.ap.new_keys && cl == 0 && rank == FC_CL - 1 && wid < 2) append_group(f.ap, h, wid, lid);
 
     // ---------------- 1. score this CTA's slice ----------------
     const int32_t* sizes = a.cell_sizes + hs * n;
     const uint8_t* mask = a.cell_mask + hs * n;
     const int32_t* code = a.cell_code + hs * n;
+    const int32_t* offs = a.cell_offsets + hs * (n + 1);
     const uint8_t* dirty = a.cell_dirty ? a.cell_dirty + hs * n : nullptr;
     const float* merged = a.centroids + hs * n * (size_t)a.dim;
     const float* subc = a.sub_centroids + hs * (size_t)S * a.kmax * sub;
@@ -171,19 +286,20 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
             float* dst = s == S - 1 ? cT : cP + prefix_table_offset(a, s, sub);
             const int ld = sl_ld(k);
             const float* src = subc + (size_t)s * a.kmax * sub;
-            for (int e = tid; e < k * sub; e += FU_THREADS) cp_async4(dst + (e & (sub - 1)) * ld + (e >> sub_shift), src + e);
+            for (int e = tid; e < k * sub; e += FC_THREADS) cp_async4(dst + (e & (sub - 1)) * ld + (e >> sub_shift), src + e);
         }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    int ccv[FU_CPT], szv[FU_CPT];
-    bool mkv[FU_CPT], dkv[FU_CPT];
+    int ccv[FC_CPT], szv[FC_CPT], ofv[FC_CPT];
+    bool mkv[FC_CPT], dkv[FC_CPT];
 #pragma unroll
-    for (int j = 0; j < FU_CPT; ++j) {
-        const int c = c0 + tid + j * FU_THREADS;
+    for (int j = 0; j < FC_CPT; ++j) {
+        const int c = c0 + tid + j * FC_THREADS;
         const bool in = c < c1;
         ccv[j] = in ? code[c] : -1;
         mkv[j] = in ? mask[c] != 0 : true;
         szv[j] = in ? sizes[c] : 0;
+        ofv[j] = in ? offs[c] : 0;
         dkv[j] = in && dirty ? dirty[c] != 0 : false;
     }
     if (tid < a.dim) {
@@ -191,9 +307,9 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
         for (int g = 0; g < a.G; ++g) acc = __fadd_rn(acc, bf16_bits_to_f32(a.q[(hs * a.G + g) * a.dim + tid]));
         qs[tid] = acc;
     }
-    if (tid == 0) s_fail = 0;
     asm volatile("cp.async.wait_all;\n" ::: "memory");
     __syncthreads();
+    fc_stamp(a, h, 1, stamping);
     if (S > 1) {  // prefix table over the first S-1 subspaces (level s chains subspace s onto level s-1)
         int width = 1;
         for (int s = 0; s < S - 1; ++s) {
@@ -203,7 +319,7 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
             const float* src = s == 0 ? nullptr : (((s - 1) & 1) ? bufB : bufA);
             float* dst = s == S - 2 ? tab : ((s & 1) ? bufB : bufA);
             const float* qq = qs + s * sub;
-            for (int e = tid; e < total; e += FU_THREADS) {
+            for (int e = tid; e < total; e += FC_THREADS) {
                 const int pi = e / ks, i = e - pi * ks;
                 float acc = src ? src[pi] : 0.0f;
 #pragma unroll 8
@@ -214,189 +330,193 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
             width = total;
         }
     }
+    unsigned long long kv[FC_CPT];
     {
-        float acc[SL_CPT];
-        int il[SL_CPT];
-        bool sep[SL_CPT], cand[SL_CPT];
+        float acc[FC_CPT];
+        int il[FC_CPT];
+        bool sep[FC_CPT];
 #pragma unroll
-        for (int j = 0; j < SL_CPT; ++j) {
+        for (int j = 0; j < FC_CPT; ++j) {
             acc[j] = 0.0f;
             il[j] = 0;
             const int cc = ccv[j];
-            cand[j] = !mkv[j] && cc >= 0;
-            sep[j] = cand[j] && S > 1 && !dkv[j];
+            const bool cand = !mkv[j] && cc >= 0;
+            sep[j] = cand && S > 1 && !dkv[j];
             if (sep[j]) {
                 int pidx = 0;
                 for (int t = 0; t < S - 1; ++t) pidx = pidx * a.ks[t] + ((cc >> (8 * t)) & 0xff);
                 il[j] = (cc >> (8 * (S - 1))) & 0xff;
                 acc[j] = tab[pidx];
             }
+            kv[j] = cand ? 1ull : 0ull;  // candidate flag until the score is in
         }
-        if (S > 1) {
+        if (S > 1) {  // the last subspace's chain, several cells per thread interleaved
             const float* q2 = qs + (S - 1) * sub;
-            if (c1 - c0 <= 2 * FU_THREADS)
-                score_chains<2>(acc, sep, il, q2, cT, ldT, sub);
-            else
-                score_chains<SL_CPT>(acc, sep, il, q2, cT, ldT, sub);
-        }
-        unsigned long long kmn = ~0ull, kmx = 0ull;
+            float ch[FC_CPT];
 #pragma unroll
-        for (int j = 0; j < FU_CPT; ++j) {
-            const int c = c0 + tid + j * FU_THREADS;
-            if (c >= c1) continue;
-            unsigned long long key = 0ull;
-            float s = -INFINITY;
-            if (cand[j]) {
-                if (sep[j]) {
-                    s = acc[j];
-                } else {  // an updated (or IVF) centroid: the chain over the live merged row
-                    const float* row = merged + (size_t)c * a.dim;
-                    s = 0.0f;
-                    for (int d = 0; d < a.dim; d += 4) {
-                        const float4 v = *reinterpret_cast<const float4*>(row + d);
-                        s = __fmaf_rn(qs[d], v.x, s);
-                        s = __fmaf_rn(qs[d + 1], v.y, s);
-                        s = __fmaf_rn(qs[d + 2], v.z, s);
-                        s = __fmaf_rn(qs[d + 3], v.w, s);
+            for (int j = 0; j < FC_CPT; ++j) ch[j] = acc[j];
+            const int live = (c1 - c0 + FC_THREADS - 1) / FC_THREADS;  // uniform over the CTA
+            for (int d0 = 0; d0 < sub; d0 += 4) {
+                float qv[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) qv[u] = q2[d0 + u];
+#pragma unroll
+                for (int j = 0; j < FC_CPT; ++j) {
+                    if (j < live) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) ch[j] = __fmaf_rn(qv[u], cT[(d0 + u) * ldT + il[j]], ch[j]);
                     }
                 }
-                key = ((unsigned long long)ord_f32(s) << 32) | (0xffffffffu - (uint32_t)c);
-                kmn = min(kmn, key);
-                kmx = max(kmx, key);
             }
-            f.keys[hs * n + c] = key;
-            f.sizes[hs * n + c] = key ? szv[j] : 0;
-            if (a.scores_out) a.scores_out[hs * n + c] = s;
+#pragma unroll
+            for (int j = 0; j < FC_CPT; ++j)
+                if (sep[j]) acc[j] = ch[j];
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            kmn = min(kmn, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmn, o));
-            kmx = max(kmx, (unsigned long long)__shfl_xor_sync(0xffffffffu, kmx, o));
-        }
-        if (lid == 0) {
-            sm.rscr[0][wid] = kmn;
-            sm.rscr[1][wid] = kmx;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            for (int w = 1; w < FU_WARPS; ++w) {
-                kmn = min(kmn, sm.rscr[0][w]);
-                kmx = max(kmx, sm.rscr[1][w]);
-            }
-            f.range[(hs * J + split) * 2 + 0] = kmn;
-            f.range[(hs * J + split) * 2 + 1] = kmx;
-        }
-    }
-    if (a.scores_out)
-        for (int c = ne + split * FU_THREADS + tid; c < n; c += J * FU_THREADS) a.scores_out[hs * n + c] = -INFINITY;
-    fu_stamp(a, h, 1, stamping);
-
-    // ---------------- 2. the group barrier ----------------
-    __syncthreads();  // every thread's keys, sizes and range are stored
-    if (tid == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(f.arrive + h) : "memory");
-        unsigned seen = 0, spins = 0;
-        while (true) {
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(seen) : "l"(f.arrive + h) : "memory");
-            if (seen >= (unsigned)J) break;
-            if (++spins > FU_SPIN_LIMIT) {
-                s_fail = 1;
-                if (at.status) atomicOr(at.status, 2);
-                break;
-            }
-            __nanosleep(32);
-        }
-    }
-    __syncthreads();
-    fu_stamp(a, h, 2, stamping);
-
-    // ---------------- 3. both boundaries, in every CTA ----------------
-    unsigned long long thrA = ~0ull, thrB = ~0ull;  // no candidates: nothing selected
-    int dcount = 0;
-    if (!s_fail) {
-        const unsigned long long* gk = f.keys + hs * n;
-        const int* gz = f.sizes + hs * n;
-        for (int c = tid; c < ne; c += FU_THREADS) {
-            skey[c] = __ldcg(gk + c);
-            ssz[c] = __ldcg(gz + c);
-        }
-        unsigned long long key_lo0 = ~0ull, key_hi0 = 0ull;
-        for (int r = 0; r < J; ++r) {
-            key_lo0 = min(key_lo0, __ldcg(f.range + (hs * J + r) * 2 + 0));
-            key_hi0 = max(key_hi0, __ldcg(f.range + (hs * J + r) * 2 + 1));
-        }
-        dcount = a.delta_count ? min(a.delta_count[h], a.delta_capacity) : 0;
-        __syncthreads();
-        if (key_hi0 != 0ull) {
-            const DenseKeys dk{skey, ssz};
-            if (search_both<FU_THREADS>(sm, dk, ne, key_lo0, key_hi0, rules)) {
-                thrA = sm.T;
-                thrB = sm.T2;
-            } else {
-                search_one<FU_THREADS>(sm, dk, ne, key_lo0, key_hi0, 1, rules);
-                thrA = sm.T;
-                const bool token_or_rank = sm.flags != 0ull;
-                __syncthreads();
-                if (token_or_rank) {
-                    thrB = thrA;
-                } else {
-                    search_one<FU_THREADS>(sm, dk, ne, key_lo0, key_hi0, 0, rules);
-                    thrB = sm.T;
+        for (int j = 0; j < FC_CPT; ++j) {
+            const int c = c0 + tid + j * FC_THREADS;
+            float sc = -INFINITY;
+            if (kv[j]) {
+                if (sep[j]) {
+                    sc = acc[j];
+                } else {  // an updated (or IVF) centroid: the chain over the live merged row
+                    const float* row = merged + (size_t)c * a.dim;
+                    sc = 0.0f;
+                    for (int d = 0; d < a.dim; d += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(row + d);
+                        sc = __fmaf_rn(qs[d], v.x, sc);
+                        sc = __fmaf_rn(qs[d + 1], v.y, sc);
+                        sc = __fmaf_rn(qs[d + 2], v.z, sc);
+                        sc = __fmaf_rn(qs[d + 3], v.w, sc);
+                    }
                 }
+                kv[j] = ((unsigned long long)ord_f32(sc) << 32) | (0xffffffffu - (uint32_t)c);
             }
-            __syncthreads();
+            if (a.scores_out && cl == 0 && c < c1) a.scores_out[hs * n + c] = sc;
         }
     }
-    fu_stamp(a, h, 3, stamping);
+    if (a.scores_out && cl == 0)
+        for (int c = ne + rank * FC_THREADS + tid; c < n; c += FC_CL * FC_THREADS) a.scores_out[hs * n + c] = -INFINITY;
 
-    // ---------------- 4. the execution rows as runs ----------------
-    // Slots in contiguous per-thread ranges (slot order = thread order): one
-    // scan ranks the selected cells and places their rows.
+    // ---------------- 2. sort the slice; everything to the leader ----------------
+    const int P = fc_pow2(max(chunk, 2));
+#pragma unroll
+    for (int j = 0; j < FC_CPT; ++j) {
+        const int i = tid + j * FC_THREADS;
+        if (i < P) sortbuf[i] = (c0 + i < c1) ? kv[j] : 0ull;
+    }
+    for (int i = tid + FC_CPT * FC_THREADS; i < P; i += FC_THREADS) sortbuf[i] = 0ull;
+    __syncthreads();
+    fc_sort_desc(sortbuf, P);
+    int ncand = 0;  // the slice's candidates: they sort first (non-candidates are 0)
+    {
+        int mine = 0;
+#pragma unroll
+        for (int j = 0; j < FC_CPT; ++j) mine += kv[j] != 0ull ? 1 : 0;
+        sl_scan<FC_THREADS>(mine, hd.redi, &ncand);
+    }
+    fc_stamp(a, h, 2, stamping);
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+    {
+        FcHdr* lead = cluster.map_shared_rank(&hd, 0);
+        unsigned long long* lkey = cluster.map_shared_rank(skey, 0);
+        int* lsz = cluster.map_shared_rank(ssz, 0);
+        int* loff = cluster.map_shared_rank(soff, 0);
+        unsigned long long* llist = cluster.map_shared_rank(lists, 0) + (size_t)rank * chunk;
+        for (int i = tid; i < ncand; i += FC_THREADS) llist[i] = sortbuf[i];
+#pragma unroll
+        for (int j = 0; j < FC_CPT; ++j) {
+            const int c = c0 + tid + j * FC_THREADS;
+            if (c < c1) {
+                lkey[c] = kv[j];
+                lsz[c] = kv[j] ? szv[j] : 0;
+                loff[c] = ofv[j];
+            }
+        }
+        if (tid == 0) lead->cnt[rank] = ncand;
+    }
+    cluster.sync();  // every slice is in the leader
+
+    // ---------------- 3. the leader: merge, scan, runs ----------------
     const int static_len = a.static_len;
     const int base_run = static_len > 0 ? 1 : 0;
-    if (!s_fail) {
-        const int per = (ne + FU_THREADS - 1) / FU_THREADS;
-        const int e0 = min(ne, tid * per), e1 = min(ne, e0 + per);
-        unsigned int nsel = 0, nkept = 0, rows = 0;
-        for (int c = e0; c < e1; ++c) {
-            const unsigned long long k = skey[c];
-            if (k != 0ull && k > thrA) {
-                ++nsel;
-                rows += (unsigned)ssz[c];
-            }
-            if (k != 0ull && k > thrB) ++nkept;
+    if (rank == 0) {
+        fc_stamp(a, h, 3, stamping);
+        fc_merge_level(lists, hd.cnt, chunk, b1, hd.len1, M, 4, M);
+        fc_merge_level(b1, hd.len1, M, b2, hd.len2, M, 2, M);
+        fc_merge_level(b2, hd.len2, M, fin, &hd.A, 0, 1, M);  // hd.A temporarily holds the merged length
+        const int Mt = hd.A;
+        SelRules r;
+        r.nprobe = a.nprobe;
+        r.max_tokens = a.max_tokens;
+        r.buffer_pages = a.buffer_pages;
+        r.page_size = a.page_size;
+        r.pg_shift = __ffs(a.page_size) - 1;
+        r.pg_pow2 = (a.page_size & (a.page_size - 1)) == 0;
+        // ranks [tid * E, tid * E + E): tokens and pages, then one scan
+        const int E = (Mt + FC_THREADS - 1) / FC_THREADS;
+        const int r0 = min(Mt, tid * E), r1 = min(Mt, r0 + E);
+        unsigned int tk = 0;
+        unsigned long long pg = 0;
+        for (int i = r0; i < r1; ++i) {
+            const int slot = (int)(0xffffffffu - (uint32_t)fin[i]);
+            const int z = ssz[slot];
+            tk += (unsigned)z;
+            pg += (unsigned long long)sl_pages(z, r);
         }
-        unsigned long long x = ((unsigned long long)nkept << 32) | nsel;
-        unsigned int y = rows;
-        sl_scan_pair<FU_THREADS>(x, y, sm);  // inclusive
-        const unsigned long long xt = sm.red64[FU_WARPS - 1];
-        const int tot_sel = (int)(xt & 0xffffffffu), tot_kept = (int)(xt >> 32);
-        const int sel_rows = (int)sm.red32[FU_WARPS - 1];
-        int my = (int)((x & 0xffffffffu) - nsel);
-        int row = static_len + (int)(y - rows);
-        const int32_t* offs = a.cell_offsets + hs * (n + 1);
-        for (int c = e0; c < e1; ++c) {
-            const unsigned long long k = skey[c];
-            if (k != 0ull && k > thrA) {
-                run_start[base_run + my] = row;
-                run_src[base_run + my] = __ldg(offs + c);
-                if (split == 0 && my < a.nprobe) a.sel_cells[hs * a.nprobe + my] = c;
-                ++my;
-                row += ssz[c];
-            }
+        unsigned long long xp = pg;
+        unsigned int yt = tk;
+        __syncthreads();  // hd.A is read by every thread above before it is reset
+        if (tid == 0) {
+            hd.A = Mt;
+            hd.B = Mt;
         }
+        sl_scan_pair<FC_THREADS>(xp, yt, hd);
+        long long tok_b = (long long)(yt - tk), pg_b = (long long)(xp - pg);
+        for (int i = r0; i < r1; ++i) {  // the first rank where a rule fires
+            const int slot = (int)(0xffffffffu - (uint32_t)fin[i]);
+            const int z = ssz[slot];
+            const int pz = sl_pages(z, r);
+            const bool rc = (i >= r.nprobe) || (tok_b >= r.max_tokens);
+            const bool rp = pg_b + pz > r.buffer_pages;
+            if (rc || rp) atomicMin(&hd.A, i);
+            if (rc) atomicMin(&hd.B, i);
+            tok_b += z;
+            pg_b += pz;
+        }
+        __syncthreads();
+        const int A = hd.A, B = hd.B;
+        // the selected cells' runs (rank order) and the selection outputs
+        tok_b = (long long)(yt - tk);
+        for (int i = r0; i < r1; ++i) {
+            const int slot = (int)(0xffffffffu - (uint32_t)fin[i]);
+            const int z = ssz[slot];
+            if (i < A) {
+                run_start[base_run + i] = static_len + (int)tok_b;
+                run_src[base_run + i] = soff[slot];
+                if (cl == 0) a.sel_cells[hs * a.nprobe + i] = slot;
+            }
+            if (i == A) hd.tokA = (int)tok_b;
+            tok_b += z;
+        }
+        if (A == Mt && r1 == Mt && r0 < r1) hd.tokA = (int)tok_b;  // everything selected
+        if (Mt == 0 && tid == 0) hd.tokA = 0;
         if (tid == 0 && static_len > 0) {
             run_start[0] = 0;
             run_src[0] = 1 << 30;
         }
-        // delta rows whose cell is in the kept list (or the padding id when
-        // that list holds a dropped entry), in ring order, after the cells
+        __syncthreads();
+        const int sel_rows = hd.tokA;
+        // delta rows whose cell is in the kept list (or the padding id when that
+        // list holds a dropped entry), in ring order, after the cells
+        const unsigned long long thrB = B < Mt ? fin[B] : 0ull;
+        const int dcount = a.delta_count ? min(a.delta_count[h], a.delta_capacity) : 0;
         int appended = 0;
-        const int r0 = base_run + tot_sel;
+        const int rd = base_run + A;
         if (dcount > 0) {
             const int32_t* dids = a.delta_cell_ids + hs * a.delta_capacity;
-            const bool has_pad = tot_kept < a.nprobe;
-            for (int base = 0; base < dcount; base += FU_THREADS) {
+            const bool has_pad = B < a.nprobe;
+            for (int base = 0; base < dcount; base += FC_THREADS) {
                 const int pidx = base + tid;
                 int fl = 0;
                 if (pidx < dcount) {
@@ -408,35 +528,49 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
                     if (cid == a.padding_id && has_pad) fl = 1;
                 }
                 int tot;
-                const int incl = sl_scan<FU_THREADS>(fl, sm.redi, &tot);
+                const int incl = sl_scan<FC_THREADS>(fl, hd.redi, &tot);
                 if (fl) {
-                    const int at_ = appended + incl - 1;
-                    run_start[r0 + at_] = static_len + sel_rows + at_;
-                    run_src[r0 + at_] = (2 << 30) | pidx;
+                    const int q = appended + incl - 1;
+                    run_start[rd + q] = static_len + sel_rows + q;
+                    run_src[rd + q] = (2 << 30) | pidx;
                 }
                 appended += tot;
             }
         }
-        const int total = min(static_len + sel_rows + appended, a.exec_capacity);
         if (tid == 0) {
-            s_nruns = r0 + appended;
-            s_total = total;
-            run_start[r0 + appended] = static_len + sel_rows + appended;
-            if (split == 0) {
-                a.sel_count[h] = min(tot_sel, a.nprobe);
+            const int total = min(static_len + sel_rows + appended, a.exec_capacity);
+            run_hdr[0] = rd + appended;
+            run_hdr[1] = total;
+            run_start[rd + appended] = static_len + sel_rows + appended;
+            if (cl == 0) {
+                a.sel_count[h] = A;
                 if (a.row_count) a.row_count[h] = total;
-                if (a.kept_count) a.kept_count[h] = tot_kept;
+                if (a.kept_count) a.kept_count[h] = B;
             }
         }
-    } else if (tid == 0) {
-        s_nruns = 0;
-        s_total = 0;
+        fc_stamp(a, h, 4, stamping);
     }
-    __syncthreads();  // the run table is complete; the selection area becomes the ring
-    fu_stamp(a, h, 4, stamping);
+    cluster.sync();  // the leader's run table is complete
+    int nruns, rows_total;
+    {
+        const int* lh = cluster.map_shared_rank(run_hdr, 0);
+        nruns = lh[0];
+        rows_total = lh[1];
+        if (rank != 0) {
+            const int* ls = cluster.map_shared_rank(run_start, 0);
+            const int* lr = cluster.map_shared_rank(run_src, 0);
+            for (int i = tid; i <= nruns; i += FC_THREADS) run_start[i] = ls[i];
+            for (int i = tid; i < nruns; i += FC_THREADS) run_src[i] = lr[i];
+        }
+    }
+    // nothing reads the leader's shared memory after this point; the matching
+    // wait is just before the CTA exits
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+    __syncthreads();  // the local run table is complete; the selection area becomes the ring
+    fc_stamp(a, h, 5, stamping);
 
-    // ---------------- 5. attention over this CTA's tiles ----------------
-    const int rows_total = s_total, nruns = s_nruns;
+    // ---------------- 4. attention over this CTA's tiles ----------------
+    const int J = gridDim.x, split = blockIdx.x;
     const int gtiles = (rows_total + AT_TILE - 1) / AT_TILE;
     const int per = (gtiles + J - 1) / J;
     const int ct0 = min(gtiles, split * per), ct1 = min(gtiles, ct0 + per);
@@ -448,54 +582,41 @@ __global__ void __launch_bounds__(FU_THREADS, 1) imi_decode_fused_kernel(const _
 #pragma unroll
     for (int u = 0; u < 16; ++u) o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
     auto entry = [&](int t) -> int {
-        const int r = t * AT_TILE + (lid & 15);
-        if (t >= ct1 || r >= rows_total) return -1;
-        int lo = 0, hi = nruns;  // the last run whose start is <= r
+        const int rr = t * AT_TILE + (lid & 15);
+        if (t >= ct1 || rr >= rows_total) return -1;
+        int lo = 0, hi = nruns;  // the last run whose start is <= rr
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
-            if (run_start[mid] <= r) lo = mid;
-            else hi = mid;
+            if (run_start[mid] <= rr)
+                lo = mid;
+            else
+                hi = mid;
         }
-        const int e = run_src[lo] + (r - run_start[lo]);
-        if (rlist && lid < 16) rlist[r] = e;
+        const int e = run_src[lo] + (rr - run_start[lo]);
+        if (rlist && lid < 16) rlist[rr] = e;
         return e;
     };
     attn_stream(at, h, wid, lid, smem_u32(fsm), ct0, ct1, rows_total, qa, entry, m_run, l_run, o);
-    fu_stamp(a, h, 5, stamping);
+    fc_stamp(a, h, 6, stamping);
     attn_write_partial(at, h, split, fsm, m_run, l_run, o);
-    if (attn_ticket_merge(at, h, fsm)) {
-        // every CTA of the group has passed the barrier (each took the ticket
-        // after it): re-arm it for the next launch
-        if (tid == 0) f.arrive[h] = 0;
-        fu_stamp(a, h, 6, tid == 0 && a.phase_ns != nullptr);
-    }
-}
-
-size_t fused_scratch_bytes(int bg, int n_slots, int splits) {
-    auto r = [](size_t x) { return (x + 255) & ~size_t(255); };
-    return r((size_t)bg * 4) + r((size_t)bg * n_slots * 8) + r((size_t)bg * n_slots * 4) + r((size_t)bg * splits * 16);
+    attn_ticket_merge(at, h, fsm);
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
 
 int fused_runs_cap(const SelectArgs& s) { return 1 + s.nprobe + (s.delta_count ? s.delta_capacity : 0); }
 
-size_t fused_smem_bytes(const SelectArgs& s) { return fused_layout(s, fused_runs_cap(s)).total; }
+size_t fused_smem_bytes(const SelectArgs& s) { return fc_layout(s, fused_runs_cap(s)).total; }
 
 // Whether this layer can run as one fused launch: the selection's shared
-// memory and the run table fit next to the attention ring, every CTA scores
-// at most FU_CPT slots per thread, and the grid is co-resident.
-bool fused_eligible(const SelectArgs& s, const AttnArgs& a, size_t scratch_bytes, const char** why) {
-    if (!s.fused_scratch) return (*why = "no fused scratch"), false;
-    if (scratch_bytes < fused_scratch_bytes(s.bg, s.n_slots, a.splits)) return (*why = "fused scratch too small"), false;
+// memory and the run table fit next to the attention ring, the slices and
+// ranks fit the leader's buffers, and the attention splits are whole clusters.
+bool fused_eligible(const SelectArgs& s, const AttnArgs& a, const char** why) {
     if (s.cand_out || s.key_base != 0 || a.o_part || a.ml_part || !a.counters)
         return (*why = "sequence-sharding outputs or no merge counters"), false;
+    if (a.splits % FC_CL != 0) return (*why = "splits not a multiple of 8"), false;
+    if ((fc_ne(s) + FC_CL - 1) / FC_CL > FC_SLICE_MAX) return (*why = "too many slots"), false;
+    if (fc_ranks(s) > FC_RANKS_MAX) return (*why = "nprobe too large"), false;
     if (fused_smem_bytes(s) > 227 * 1024) return (*why = "selection too large for one CTA"), false;
-    const int ne = (s.slot_bound > 0 && s.slot_bound < s.n_slots) ? s.slot_bound : s.n_slots;
-    if ((ne + a.splits - 1) / a.splits > FU_CPT * FU_THREADS) return (*why = "too few splits for the slots"), false;
-    int dev = 0, sms = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
-                                                  cudaSuccess)
-        return (*why = "device query failed"), false;
-    if ((long long)a.splits * a.bg > sms) return (*why = "more CTAs than SMs"), false;
     return true;
 }
 
@@ -504,39 +625,12 @@ cudaError_t launch_decode_fused(const SelectArgs& s, const AttnArgs& a, cudaStre
     f.s = s;
     f.a = a;
     if (app) f.ap = *app;
-    unsigned char* base = static_cast<unsigned char*>(s.fused_scratch);
-    auto r = [](size_t x) { return (x + 255) & ~size_t(255); };
-    f.arrive = reinterpret_cast<uint32_t*>(base);
-    base += r((size_t)s.bg * 4);
-    f.keys = reinterpret_cast<unsigned long long*>(base);
-    base += r((size_t)s.bg * s.n_slots * 8);
-    f.sizes = reinterpret_cast<int32_t*>(base);
-    base += r((size_t)s.bg * s.n_slots * 4);
-    f.range = reinterpret_cast<unsigned long long*>(base);
     f.runs_cap = fused_runs_cap(s);
-    const size_t sm = fused_layout(s, f.runs_cap).total;
+    const size_t sm = fc_layout(s, f.runs_cap).total;
     static int smem_set[64] = {};
     cudaError_t e = ensure_smem(reinterpret_cast<const void*>(&imi_decode_fused_kernel), sm, smem_set, 64);
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.splits, a.bg);
-    cfg.blockDim = dim3(FU_THREADS);
-    cfg.dynamicSmemBytes = sm;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, imi_decode_fused_kernel, f);
-    if (e != cudaSuccess) {  // a cooperative launch that may not also be programmatic: launch it plainly ordered
-        (void)cudaGetLastError();
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, imi_decode_fused_kernel, f);
-    }
-    return e;
+    return launch_pdl(imi_decode_fused_kernel, dim3(a.splits, a.bg), dim3(FC_THREADS), sm, st, f);
 }
 
 }  // namespace imi

@@ -102,8 +102,8 @@ IMI_DEV int sl_scan(int v, int* red, int* total) {
 }
 
 // Block-wide inclusive scan of a (64-bit, 32-bit) pair under one set of barriers.
-template <int NT = SL_THREADS>
-IMI_DEV void sl_scan_pair(unsigned long long& x, unsigned int& y, SelHdr& sm) {
+template <int NT = SL_THREADS, class Hdr>
+IMI_DEV void sl_scan_pair(unsigned long long& x, unsigned int& y, Hdr& sm) {
     constexpr int NW = NT / 32;
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
 #pragma unroll

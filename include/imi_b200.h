@@ -141,11 +141,11 @@ typedef struct imi_select_desc {
                                               selected cells in slot order, then the stop marker (the
                                               highest-ranked cell left out, if any); their sizes from
                                               offset nprobe + 1; the entry count last */
-    void* fused_scratch;                   /* NULL, or scratch of imi_decode_fused_scratch_size bytes,
-                                              zeroed before the first call: imi_decode_attend and
-                                              imi_decode_layer then run selection and attention as one
-                                              launch when the layer fits it */
-    size_t fused_scratch_bytes;
+    int32_t fuse;                          /* nonzero: imi_decode_attend and imi_decode_layer run the
+                                              selection and the attention as one launch when the layer
+                                              fits it (attention splits a multiple of 8, at most 16384
+                                              occupied slots, nprobe < 2048, shared memory); the
+                                              selected cells and rows then come in rank order */
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
@@ -170,10 +170,10 @@ typedef struct imi_attn_desc {
                                               with it the last CTA of a group merges the
                                               splits (and re-zeroes its counter); without it a
                                               separate merge kernel runs */
-    int32_t* status;                       /* [1] or NULL: bit 1 is set when, in the fused decode
-                                              launch, a CTA's bounded wait for the other CTAs of its
-                                              group ran out (the output is then not valid); the
-                                              separate attention kernel has no waits */
+    int32_t* status;                       /* [1] or NULL: reserved.  The attention kernels have no
+                                              spin-waits (row copies are cp.async groups, the split
+                                              merge is a ticket), so no bit is set; callers may pass
+                                              NULL */
     float* o_part;                         /* [bg, G, 128] out or NULL: unnormalised output (sequence
                                               sharding); needs counters */
     float* ml_part;                        /* [bg, G, 2] out or NULL: (max in log2 units, sum) */
@@ -306,15 +306,13 @@ IMI_API int imi_sparse_attention(const imi_attn_desc* desc, void* stream);
  * can overlap on the GPU (other streams, other host threads) race: serialise
  * them.  It allocates nothing (no cudaMalloc/cudaFree). */
 IMI_API int imi_sparse_attention_noalloc(const imi_attn_desc* desc, void* stream);
-/* Bytes of sel->fused_scratch for bg groups, n_slots slots and attn->splits splits. */
-IMI_API size_t imi_decode_fused_scratch_size(int32_t bg, int32_t n_slots, int32_t splits);
 /* apply (optional, NULL to skip) + select + attention in one call: the per-layer
  * decode attention of the cache (retrieval.py:320-602).  sel and attn must name
- * the same q, row_index, row_count and exec_capacity.  With sel->fused_scratch
- * the selection and the attention run as one cooperative launch (fused.cu) when
- * the layer fits (shared memory, splits * bg <= SMs); otherwise as the select
- * kernel followed by the attention kernel.  Both give the same selection and
- * the same rows. */
+ * the same q, row_index, row_count and exec_capacity.  With sel->fuse the
+ * selection and the attention run as one launch of 8-CTA clusters (fused.cu)
+ * when the layer fits; otherwise as the select kernel followed by the attention
+ * kernel.  Both select the same cells and attend the same rows (the fused launch
+ * lists them in rank order, the pair in slot order). */
 IMI_API int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
                               void* stream);
 /* One decode layer in one call: append (NULL to skip), the batched cell
