@@ -67,7 +67,7 @@ struct FcHdr {
 };
 
 struct FcLayout {
-    size_t keys, sizes, offs, lists, sortbuf, b1, b2, fin, qs, tab, tables, runs, total;
+    size_t sizes, kept, lists, sortbuf, b1, qs, tab, tables, runs, total;
 };
 
 __host__ __device__ inline size_t fc_align(size_t x) { return (x + 127) & ~size_t(127); }
@@ -97,22 +97,17 @@ __host__ __device__ inline FcLayout fc_layout(const SelectArgs& a, int runs_cap)
     const int M = fc_ranks(a);
     FcLayout L;
     size_t o = fc_align(sizeof(FcHdr));
-    L.keys = o;  // [ne] leader: key by slot
-    o = fc_align(o + 8 * (size_t)ne);
     L.sizes = o;  // [ne] leader: size by slot
     o = fc_align(o + 4 * (size_t)ne);
-    L.offs = o;  // [ne] leader: list offset by slot
-    o = fc_align(o + 4 * (size_t)ne);
-    L.lists = o;  // [8 * chunk] leader: the sorted slices
-    o = fc_align(o + 8 * (size_t)FC_CL * chunk);
+    L.kept = o;  // [ne / 32] leader: kept-list membership by slot
+    o = fc_align(o + 4 * (((size_t)ne + 31) / 32));
+    L.lists = o;  // [8 * chunk] leader: the sorted slices; later merge level 2 ([2 * M])
+    const size_t nl = (size_t)FC_CL * chunk > 2 * (size_t)M ? (size_t)FC_CL * chunk : 2 * (size_t)M;
+    o = fc_align(o + 8 * nl);
     L.sortbuf = o;  // [pow2(chunk)] this CTA's slice being sorted
     o = fc_align(o + 8 * (size_t)fc_pow2(chunk));
-    L.b1 = o;  // [4 * M] merge level 1
+    L.b1 = o;  // [4 * M] merge level 1; later the merged ranks ([M])
     o = fc_align(o + 8 * 4 * (size_t)M);
-    L.b2 = o;  // [2 * M] merge level 2
-    o = fc_align(o + 8 * 2 * (size_t)M);
-    L.fin = o;  // [M] merged ranks
-    o = fc_align(o + 8 * (size_t)M);
     L.qs = o;
     o = fc_align(o + 4 * (size_t)a.dim);
     L.tab = o;
@@ -131,11 +126,19 @@ __host__ __device__ inline FcLayout fc_layout(const SelectArgs& a, int runs_cap)
 }
 
 IMI_DEV void fc_stamp(const SelectArgs& a, int h, int k, bool on) {
+#ifdef FC_DEBUG_STAMPS  // every rank of the first cluster: phase_ns[(h * 8 + rank) * 8 + k]
+    if (a.phase_ns && threadIdx.x == 0 && blockIdx.x < FC_CL) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.phase_ns[((size_t)h * 8 + blockIdx.x) * 8 + k] = t;
+    }
+#else
     if (on) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         a.phase_ns[(size_t)h * 8 + k] = t;
     }
+#endif
 }
 
 // Bitonic sort of buf[0, P) (P a power of two), descending, all threads.
@@ -145,8 +148,9 @@ IMI_DEV void fc_sort_desc(unsigned long long* buf, int P) {
     const int tid = threadIdx.x;
     for (int k = 2; k <= P; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
+            const int lj = __ffs(j) - 1;  // j is a power of two
             for (int p = tid; p < (P >> 1); p += FC_THREADS) {
-                const int i = 2 * j * (p / j) + (p % j), l = i + j;
+                const int i = ((p >> lj) << (lj + 1)) + (p & (j - 1)), l = i + j;
                 const unsigned long long x = buf[i], y = buf[l];
                 const bool desc = (i & k) == 0;
                 if (desc ? (x < y) : (x > y)) {
@@ -223,14 +227,13 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
     const int M = fc_ranks(a);
     const FcLayout Lo = fc_layout(a, f.runs_cap);
     FcHdr& hd = *reinterpret_cast<FcHdr*>(fsm);
-    unsigned long long* skey = reinterpret_cast<unsigned long long*>(fsm + Lo.keys);
     int* ssz = reinterpret_cast<int*>(fsm + Lo.sizes);
-    int* soff = reinterpret_cast<int*>(fsm + Lo.offs);
+    unsigned int* kept = reinterpret_cast<unsigned int*>(fsm + Lo.kept);
     unsigned long long* lists = reinterpret_cast<unsigned long long*>(fsm + Lo.lists);
     unsigned long long* sortbuf = reinterpret_cast<unsigned long long*>(fsm + Lo.sortbuf);
     unsigned long long* b1 = reinterpret_cast<unsigned long long*>(fsm + Lo.b1);
-    unsigned long long* b2 = reinterpret_cast<unsigned long long*>(fsm + Lo.b2);
-    unsigned long long* fin = reinterpret_cast<unsigned long long*>(fsm + Lo.fin);
+    unsigned long long* b2 = lists;  // the slices are consumed by level 1
+    unsigned long long* fin = b1;    // level 1 is consumed by level 2
     float* qs = reinterpret_cast<float*>(fsm + Lo.qs);
     float* tab = reinterpret_cast<float*>(fsm + Lo.tab);
     float* cT = reinterpret_cast<float*>(fsm + Lo.tables);
@@ -290,7 +293,7 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
         }
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    int ccv[FC_CPT], szv[FC_CPT], ofv[FC_CPT];
+    int ccv[FC_CPT], szv[FC_CPT];
     bool mkv[FC_CPT], dkv[FC_CPT];
 #pragma unroll
     for (int j = 0; j < FC_CPT; ++j) {
@@ -299,7 +302,6 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
         ccv[j] = in ? code[c] : -1;
         mkv[j] = in ? mask[c] != 0 : true;
         szv[j] = in ? sizes[c] : 0;
-        ofv[j] = in ? offs[c] : 0;
         dkv[j] = in && dirty ? dirty[c] != 0 : false;
     }
     if (tid < a.dim) {
@@ -399,6 +401,7 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
         for (int c = ne + rank * FC_THREADS + tid; c < n; c += FC_CL * FC_THREADS) a.scores_out[hs * n + c] = -INFINITY;
 
     // ---------------- 2. sort the slice; everything to the leader ----------------
+    fc_stamp(a, h, 5, stamping);
     const int P = fc_pow2(max(chunk, 2));
 #pragma unroll
     for (int j = 0; j < FC_CPT; ++j) {
@@ -417,31 +420,36 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
     }
     fc_stamp(a, h, 2, stamping);
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+#ifdef FC_DEBUG_STAMPS
+    fc_stamp(a, h, 3, false);
+#endif
     {
         FcHdr* lead = cluster.map_shared_rank(&hd, 0);
-        unsigned long long* lkey = cluster.map_shared_rank(skey, 0);
         int* lsz = cluster.map_shared_rank(ssz, 0);
-        int* loff = cluster.map_shared_rank(soff, 0);
         unsigned long long* llist = cluster.map_shared_rank(lists, 0) + (size_t)rank * chunk;
         for (int i = tid; i < ncand; i += FC_THREADS) llist[i] = sortbuf[i];
 #pragma unroll
         for (int j = 0; j < FC_CPT; ++j) {
             const int c = c0 + tid + j * FC_THREADS;
-            if (c < c1) {
-                lkey[c] = kv[j];
-                lsz[c] = kv[j] ? szv[j] : 0;
-                loff[c] = ofv[j];
-            }
+            if (c < c1) lsz[c] = kv[j] ? szv[j] : 0;
         }
         if (tid == 0) lead->cnt[rank] = ncand;
     }
+#ifdef FC_DEBUG_STAMPS
+    fc_stamp(a, h, 4, false);
+#endif
     cluster.sync();  // every slice is in the leader
+#ifdef FC_DEBUG_STAMPS
+    fc_stamp(a, h, 5, false);
+#endif
 
     // ---------------- 3. the leader: merge, scan, runs ----------------
     const int static_len = a.static_len;
     const int base_run = static_len > 0 ? 1 : 0;
     if (rank == 0) {
+#ifndef FC_DEBUG_STAMPS
         fc_stamp(a, h, 3, stamping);
+#endif
         fc_merge_level(lists, hd.cnt, chunk, b1, hd.len1, M, 4, M);
         fc_merge_level(b1, hd.len1, M, b2, hd.len2, M, 2, M);
         fc_merge_level(b2, hd.len2, M, fin, &hd.A, 0, 1, M);  // hd.A temporarily holds the merged length
@@ -484,8 +492,13 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
             tok_b += z;
             pg_b += pz;
         }
+        for (int w = tid; w < (ne + 31) / 32; w += FC_THREADS) kept[w] = 0u;
         __syncthreads();
         const int A = hd.A, B = hd.B;
+        for (int i = r0; i < min(r1, B); ++i) {  // kept-list membership by slot (delta rows)
+            const int slot = (int)(0xffffffffu - (uint32_t)fin[i]);
+            atomicOr(&kept[slot >> 5], 1u << (slot & 31));
+        }
         // the selected cells' runs (rank order) and the selection outputs
         tok_b = (long long)(yt - tk);
         for (int i = r0; i < r1; ++i) {
@@ -493,7 +506,7 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
             const int z = ssz[slot];
             if (i < A) {
                 run_start[base_run + i] = static_len + (int)tok_b;
-                run_src[base_run + i] = soff[slot];
+                run_src[base_run + i] = __ldg(offs + slot);
                 if (cl == 0) a.sel_cells[hs * a.nprobe + i] = slot;
             }
             if (i == A) hd.tokA = (int)tok_b;
@@ -509,7 +522,6 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
         const int sel_rows = hd.tokA;
         // delta rows whose cell is in the kept list (or the padding id when that
         // list holds a dropped entry), in ring order, after the cells
-        const unsigned long long thrB = B < Mt ? fin[B] : 0ull;
         const int dcount = a.delta_count ? min(a.delta_count[h], a.delta_capacity) : 0;
         int appended = 0;
         const int rd = base_run + A;
@@ -521,10 +533,7 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
                 int fl = 0;
                 if (pidx < dcount) {
                     const int cid = dids[pidx];
-                    if (cid >= 0 && cid < ne) {
-                        const unsigned long long k = skey[cid];
-                        fl = (k != 0ull && k > thrB) ? 1 : 0;
-                    }
+                    if (cid >= 0 && cid < ne) fl = (kept[cid >> 5] >> (cid & 31)) & 1u;
                     if (cid == a.padding_id && has_pad) fl = 1;
                 }
                 int tot;
@@ -548,7 +557,9 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
                 if (a.kept_count) a.kept_count[h] = B;
             }
         }
+#ifndef FC_DEBUG_STAMPS
         fc_stamp(a, h, 4, stamping);
+#endif
     }
     cluster.sync();  // the leader's run table is complete
     int nruns, rows_total;
@@ -567,7 +578,7 @@ __global__ void __cluster_dims__(FC_CL, 1, 1) __launch_bounds__(FC_THREADS, 1)
     // wait is just before the CTA exits
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
     __syncthreads();  // the local run table is complete; the selection area becomes the ring
-    fc_stamp(a, h, 5, stamping);
+    fc_stamp(a, h, 7, stamping);
 
     // ---------------- 4. attention over this CTA's tiles ----------------
     const int J = gridDim.x, split = blockIdx.x;
