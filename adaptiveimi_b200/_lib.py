@@ -49,7 +49,6 @@ class SelectDesc(ctypes.Structure):
         ("sel_cells", P), ("sel_count", P), ("kept_count", P), ("row_index", P), ("row_count", P),
         ("scores_out", P), ("phase_ns", P),
         ("slot_bound", i32), ("key_base", i32), ("cand_out", P),
-        ("fuse", i32),
     ]
 
 

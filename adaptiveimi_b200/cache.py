@@ -157,18 +157,8 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.execution_buffer_values_dict: Dict[str, torch.Tensor] = {}
         self.valid_lengths_dict: Dict[str, torch.Tensor] = {}
         self._dec: Dict[str, Dict[str, torch.Tensor]] = {}
-        # selection and attention of a layer in one launch where the layer fits
-        # (runtime_config["pipeline"]["fuse_decode"], default on); its splits are
-        # whole 8-CTA clusters
-        self.fuse_decode = bool(self.runtime_config["pipeline"].get("fuse_decode", True))
-        sms = 148
-        if torch.cuda.is_available():
-            sms = torch.cuda.get_device_properties(torch.device(self.layer_mapping["0"])).multi_processor_count
-        if self.fuse_decode:
-            self.splits = ops.fused_splits(self.batch_groups, sms)
-        else:
-            self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity,
-                                              sms=sms, exec_capacity=self.execution_stride)
+        self.splits = ops.default_splits(self.batch_groups, self.max_retrieval_tokens + self.static_capacity,
+                                          exec_capacity=self.execution_stride)
         # optional measurement hooks (bench.py): per-call row counts and CUDA
         # events around the attention launch, both on the launching stream
         self._pending = None  # deferred append: (layer, k, v, head stride, pos, batch slot, async batch)
@@ -298,7 +288,6 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         sel.sel_cells, sel.sel_count, sel.kept_count = buf["sel"].data_ptr(), buf["sel_count"].data_ptr(), \
             buf["kept"].data_ptr()
         sel.row_index = buf["rows"].data_ptr()
-        sel.fuse = 1 if self.fuse_decode else 0
         # every slot at or above the largest n_active is padding: one host read
         # per layer, here at preparation, lets the selection skip them
         sel.slot_bound = int(idx.n_active.max().item())

@@ -1,5 +1,5 @@
-// attn_core.cuh -- the gather-attention building blocks shared by the split-K
-// attention kernel (attention.cu) and the fused decode kernel (fused.cu):
+// attn_core.cuh -- the gather-attention building blocks of the split-K
+// attention kernel (attention.cu), as device functions any kernel can compose:
 // the per-warp streaming loop over 16-row tiles (16-byte cp.async pieces into
 // a 3-deep ring, mma.sync m16n8k16, online softmax in exp2 space), the CTA's
 // warp merge into one (m, l, o) partial, and the split merge by the last CTA

@@ -17,7 +17,7 @@ PKG = HERE.parent
 ROOT = PKG.parent
 OUT = PKG / "lib" / "libimi_b200.so"
 OBJ = PKG / "lib" / "obj"
-SOURCES = ["decode.cu", "select.cu", "attention.cu", "fused.cu", "build.cu", "peer.cu", "capi.cu"]
+SOURCES = ["decode.cu", "select.cu", "attention.cu", "build.cu", "peer.cu", "capi.cu"]
 HEADERS = ["common.cuh", "imi_internal.h", "select_core.cuh", "attn_core.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",

@@ -203,13 +203,6 @@ static int launch_decode_attend(const imi_select_desc* sel, const imi_attn_desc*
         cudaError_t e = imi::launch_apply(*apply, S(stream));
         if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(apply)");
     }
-    const char* why = "";
-    if (sel->fuse) {
-        if (imi::fused_eligible(*sel, *attn, &why))
-            return cuda_status(imi::launch_decode_fused(*sel, *attn, S(stream), app), "imi_decode_attend(fused)");
-        static const bool report = std::getenv("IMI_REPORT_UNFUSED") != nullptr;
-        if (report) std::fprintf(stderr, "[imi_b200] decode layer not fused: %s\n", why);
-    }
     cudaError_t e = imi::launch_select(*sel, S(stream), app);
     if (e != cudaSuccess) return cuda_status(e, "imi_decode_attend(select)");
     return cuda_status(imi::launch_attention(*attn, S(stream)), "imi_decode_attend(attention)");

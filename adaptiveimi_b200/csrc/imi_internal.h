@@ -87,7 +87,6 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why);
-bool fused_eligible(const SelectArgs& s, const AttnArgs& a, const char** why);
-cudaError_t launch_decode_fused(const SelectArgs& s, const AttnArgs& a, cudaStream_t st, const AppendArgs* app);
+
 
 }  // namespace imi

@@ -1,5 +1,5 @@
-// select_core.cuh -- the selection machinery shared by the cluster select
-// kernel (select.cu) and the fused decode kernel (fused.cu): the ranking key,
+// select_core.cuh -- the selection machinery of the cluster select kernel and
+// the sequence-sharded merge (select.cu), kept apart from them: the ranking key,
 // the block-wide scans, the two-boundary histogram search over the candidates
 // (all three rules: rank, tokens and pages; and rank and tokens only), the
 // exact resolve of a boundary bucket, and the separable scorer's helpers.

@@ -223,12 +223,6 @@ def select_cells(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: i
     _lib.check(L.imi_select_cells(ctypes.byref(d), _stream(q.device)), "imi_select_cells")
 
 
-def fused_splits(bg: int, sms: int = 148) -> int:
-    """Attention splits of the fused decode launch: whole 8-CTA clusters, one
-    wave over the SMs (at least one cluster per group)."""
-    return 8 * max(1, (sms // 8) // max(1, bg))
-
-
 def default_splits(bg: int, rows_per_group: int, sms: int = 148, exec_capacity: Optional[int] = None) -> int:
     """CTAs per KV group for the split-K attention: one wave (one CTA per SM,
     the kernel's shared-memory ring allows one) and at least 64 rows per CTA.
@@ -279,14 +273,13 @@ def decode_attend(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: 
                   sel_count: torch.Tensor, row_index: torch.Tensor, row_count: torch.Tensor, static_keys: torch.Tensor,
                   static_values: torch.Tensor, out: torch.Tensor, part_o: torch.Tensor, part_ml: torch.Tensor,
                   counters: torch.Tensor, splits: int, kept_count: Optional[torch.Tensor] = None,
-                  slot_bound: int = 0, fuse: bool = False,
+                  slot_bound: int = 0,
                   status: Optional[torch.Tensor] = None, delta_cell_ids: Optional[torch.Tensor] = None,
                   delta_count: Optional[torch.Tensor] = None, delta_keys: Optional[torch.Tensor] = None,
                   delta_values: Optional[torch.Tensor] = None, scores_out: Optional[torch.Tensor] = None,
                   phase_ns: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Selection + attention of one layer through imi_decode_attend: one fused
-    launch when ``fuse`` is set and the layer fits it (``splits`` a multiple of
-    8), else the select kernel then the attention kernel."""
+    """Selection + attention of one layer through imi_decode_attend (the select
+    kernel, then the attention kernel as its programmatic dependent)."""
     bg, G, D = q.shape
     d = _lib.SelectDesc()
     d.bg, d.G, d.dim, d.n_slots, d.parts, d.kmax = bg, G, D, index.n_slots, index.parts, index.kmax
@@ -307,7 +300,6 @@ def decode_attend(*, q: torch.Tensor, index: IMIIndex, nprobe: int, max_tokens: 
     d.scores_out = scores_out.data_ptr() if scores_out is not None else None
     d.phase_ns = phase_ns.data_ptr() if phase_ns is not None else None
     d.slot_bound = int(slot_bound)
-    d.fuse = 1 if fuse else 0
     a = _lib.AttnDesc()
     a.bg, a.G, a.splits, a.exec_capacity = bg, G, splits, exec_capacity
     a.scale = 1.0 / math.sqrt(D)

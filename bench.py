@@ -54,10 +54,6 @@ KMEANS = {"max_iters": 20, "tol": 0.0005, "early_stop_min_iter": 20, "early_stop
 # --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 # -k regex:imi_attn_kernel -s 4 -c 3 (each launch is one full layer).
 ATTN_TRAFFIC_BYTES = 50_290_518
-# ncu DRAM bytes (read + write) per launch of the fused decode kernel at this
-# geometry; None until measured
-FUSED_TRAFFIC_BYTES = None
-FUSED_TRAFFIC_SOURCE = "not measured yet"
 ASYNC = {"enabled": True, "batch": 16, "threshold": 16, "delta_tokens": 512}
 
 
@@ -262,7 +258,6 @@ def run_ours(args):
     cache.row_count_log = None
     cache.attn_event_log = None
     attn = attention_kernel_pass(cache, qd[args.warmup + args.steps - 1], L, hl, G, dev)
-    fused = fused_kernel_pass(cache, qd[args.warmup + args.steps - 1], L, hl, G, dev) if cache.fuse_decode else None
     # ---- e2e: pinned host inputs copied in, outputs copied out, every step
     # (the cache has capacity for warmup + steps appended tokens; e2e reuses the
     # last `e2e_steps` positions after a reset of the appended-token counter)
@@ -295,8 +290,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
     # ---- max over ranks
-    dev_ms, e2e_ms, attn_avg_us, build_ms_max, fused_avg_us = max_over_ranks(
-        [dev_ms, e2e_ms, attn["avg_us"], build_ms, fused["avg_us"] if fused else 0.0], dev)
+    dev_ms, e2e_ms, attn_avg_us, build_ms_max = max_over_ranks([dev_ms, e2e_ms, attn["avg_us"], build_ms], dev)
     if rank != 0:
         if ws > 1:
             torch.distributed.destroy_process_group()
@@ -305,25 +299,13 @@ def run_ours(args):
     e2e_us = e2e_ms * 1e3 / (e2e_steps * L)
     hbm, src = peaks()
     achieved = attn["algo_bytes"] / (attn_avg_us * 1e-6) / 1e9 if attn_avg_us > 0 else 0.0
-    attn_line = {"kernel": "imi_attn_kernel (gather attention with in-kernel split merge)", "bound": "hbm",
-                 "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                 "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)", "traffic": ATTN_TRAFFIC_BYTES,
-                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 3 launches of "
-                                   "the same kernel on the same geometry",
-                 "algorithmic_bytes_per_launch": int(attn["algo_bytes"]), "avg_launch_us": round(attn_avg_us, 3),
-                 "launches_timed": attn["launches"], "rows_per_launch": attn["rows_per_launch"]}
-    if fused is not None:
-        f_ach = fused["algo_bytes"] / (fused_avg_us * 1e-6) / 1e9 if fused_avg_us > 0 else 0.0
-        roofline = {"kernel": "imi_decode_fused_kernel (selection + gather attention + split merge: one launch "
-                              "per layer)", "bound": "hbm", "achieved": round(f_ach, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(f_ach / hbm, 4), "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)",
-                    "traffic": FUSED_TRAFFIC_BYTES, "traffic_source": FUSED_TRAFFIC_SOURCE,
-                    "algorithmic_bytes_per_launch": int(fused["algo_bytes"]),
-                    "avg_launch_us": round(fused_avg_us, 3), "launches_timed": fused["launches"],
-                    "rows_per_launch": fused["rows_per_launch"],
-                    "attention_only_kernel": attn_line}
-    else:
-        roofline = attn_line
+    roofline = {"kernel": "imi_attn_kernel (gather attention with in-kernel split merge)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                "peak_source": src + " (MEASURED_PEAKS.json hbm_gbs)", "traffic": ATTN_TRAFFIC_BYTES,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of 3 launches of "
+                                  "the same kernel on the same geometry",
+                "algorithmic_bytes_per_launch": int(attn["algo_bytes"]), "avg_launch_us": round(attn_avg_us, 3),
+                "launches_timed": attn["launches"], "rows_per_launch": attn["rows_per_launch"]}
     keys_built = L * kvh * n_mid
     # algorithmic k-means flops of the whole build, from each index's own iteration counts
     build_flops = 0
@@ -365,13 +347,11 @@ def run_ours(args):
         "host_launch_us_per_layer_step": round(host_s * 1e6 / (args.steps * L), 2),
         "clocks": clk.summary(),
     }
-    # our kernels per layer-step: the fused launch (selection, the append,
-    # attention and its split merge) -- or, unfused, select (which also does
-    # the append) + attention; every ASYNC["batch"] steps a layer also launches
-    # the append and the two assignment kernels before them (+3), and at its
-    # next visit the centroid publish (+1)
-    per_layer = 1 if fused is not None else 2
-    res["gpu_launches"] = int(args.steps * L * per_layer + (args.steps // ASYNC["batch"]) * L * 4)
+    # our kernels per layer-step: select (which also does the append) +
+    # attention (which also merges its splits); every ASYNC["batch"] steps a
+    # layer instead launches the append and the two assignment kernels before
+    # them (+3), and at its next visit the centroid publish (+1)
+    res["gpu_launches"] = int(args.steps * L * 2 + (args.steps // ASYNC["batch"]) * L * 4)
     if ws == 1 and not args.no_cpu_baseline:
         try:
             res["cpu_baseline"] = cpu_baseline(args, sample_layers=1, sample_steps=2)
@@ -449,65 +429,6 @@ def attention_kernel_pass(cache, q_last, L, hl, G, dev, repeats=6):
     algo = rows_per_launch * (512 + 4) + bg * G * 128 * 2 * 2 + bg * cache.splits * G * (128 + 2) * 4 * 2
     return {"avg_us": sum(times) / len(times), "algo_bytes": algo, "launches": len(times) * L,
             "rows_per_launch": rows_per_launch}
-
-
-def fused_kernel_pass(cache, q_last, L, hl, G, dev, repeats=6):
-    """Per-launch device time of the fused decode launch (imi_decode_fused_kernel:
-    selection + gather attention + split merge of one layer), timed live over
-    sweeps of the L layers back to back with the last step's queries, one event
-    pair per sweep.  Uses the cache's own per-layer descriptors (the row list
-    and outputs are rewritten with the same values).
-
-    Algorithmic bytes per launch = rows * (256 B key + 256 B value) + per group
-    the index metadata the selection must read (sub-centroid tables and, per
-    occupied slot, code, size, mask and offset: 13 B) + q and out (bf16) + the
-    split partials written and read back.  Row-list entries are computed on
-    chip, not read."""
-    import ctypes
-
-    from adaptiveimi_b200 import _lib
-
-    L_ = _lib.load()
-    bg = hl
-    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    qs = [q_last[l].reshape(bg, G, 128).contiguous() for l in range(L)]
-    descs = []
-    for l in range(L):
-        d = cache._descs[l]
-        sel, att = _lib.SelectDesc(), _lib.AttnDesc()
-        ctypes.pointer(sel)[0] = d["sel"]
-        ctypes.pointer(att)[0] = d["att"]
-        sel.q = att.q = qs[l].data_ptr()
-        sel.static_len = cache.static_pattern_total
-        descs.append((sel, att))
-    rc = cache._dec[f"cuda:{dev.index}"]["row_count"]
-    log = torch.zeros((L, bg), dtype=torch.int32, device=dev)
-    evs = []
-    torch.cuda.synchronize()
-    for rep in range(repeats + 1):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for l in range(L):
-            sel, att = descs[l]
-            _lib.check(L_.imi_decode_attend(ctypes.byref(sel), ctypes.byref(att), None, stream), "imi_decode_attend")
-            if rep == 0:  # the untimed first sweep records every layer's row counts
-                log[l].copy_(rc)
-        b.record()
-        if rep > 0:
-            evs.append((a, b))
-    torch.cuda.synchronize()
-    times = [a.elapsed_time(b) * 1e3 / L for a, b in evs]
-    rows_per_launch = int(log.to(torch.int64).sum()) / L
-    meta = 0
-    for l in range(L):
-        idx = cache.index[l]
-        ne = int(idx.n_active.max())
-        S_ = len(idx.ks)
-        meta += bg * (sum(int(k) for k in idx.ks) * (128 // S_) * 4 + ne * 13)
-    meta_per_launch = meta / L
-    algo = rows_per_launch * 512 + meta_per_launch + bg * G * 128 * 2 * 2 + bg * cache.splits * G * (128 + 2) * 4 * 2
-    return {"avg_us": sum(times) / len(times), "algo_bytes": algo, "launches": len(times) * L,
-            "rows_per_launch": rows_per_launch, "meta_bytes_per_launch": meta_per_launch}
 
 
 # ----------------------------------------------------------------------------

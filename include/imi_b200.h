@@ -141,11 +141,6 @@ typedef struct imi_select_desc {
                                               selected cells in slot order, then the stop marker (the
                                               highest-ranked cell left out, if any); their sizes from
                                               offset nprobe + 1; the entry count last */
-    int32_t fuse;                          /* nonzero: imi_decode_attend and imi_decode_layer run the
-                                              selection and the attention as one launch when the layer
-                                              fits it (attention splits a multiple of 8, at most 16384
-                                              occupied slots, nprobe < 2048, shared memory); the
-                                              selected cells and rows then come in rank order */
 } imi_select_desc;
 
 typedef struct imi_attn_desc {
@@ -308,11 +303,7 @@ IMI_API int imi_sparse_attention(const imi_attn_desc* desc, void* stream);
 IMI_API int imi_sparse_attention_noalloc(const imi_attn_desc* desc, void* stream);
 /* apply (optional, NULL to skip) + select + attention in one call: the per-layer
  * decode attention of the cache (retrieval.py:320-602).  sel and attn must name
- * the same q, row_index, row_count and exec_capacity.  With sel->fuse the
- * selection and the attention run as one launch of 8-CTA clusters (fused.cu)
- * when the layer fits; otherwise as the select kernel followed by the attention
- * kernel.  Both select the same cells and attend the same rows (the fused launch
- * lists them in rank order, the pair in slot order). */
+ * the same q, row_index, row_count and exec_capacity. */
 IMI_API int imi_decode_attend(const imi_select_desc* sel, const imi_attn_desc* attn, const imi_apply_desc* apply,
                               void* stream);
 /* One decode layer in one call: append (NULL to skip), the batched cell

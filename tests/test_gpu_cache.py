@@ -121,9 +121,8 @@ class RefSim:
         return np.stack(outs), sels
 
 
-@pytest.mark.parametrize("fuse", [True, False])
 @pytest.mark.parametrize("mode", ["off", "reference_ring", "stored_ring"])
-def test_cache_decode_matches_reference_simulation(mode, fuse):
+def test_cache_decode_matches_reference_simulation(mode):
     """off: no async update.  reference_ring: the reference's behaviour, whose
     delta ring never receives rows (zero rows with padding ids are attended
     whenever the selection holds a dropped entry).  stored_ring: the ring holds
@@ -140,8 +139,7 @@ def test_cache_decode_matches_reference_simulation(mode, fuse):
         pages_per_cluster=2, retrieval_budget=0.1, cache_ratio=0.05, buffer_cluster_num=32, prefill_bsz=1,
         num_gpus=1, model_size=8, subspace_parts=2,
         runtime_config={"kmeans": {"k1": 16, "k2": 16, "max_iters": 6, "early_stop_min_iter": 6, "tol": 0.0,
-                                   "early_stop_rel_tol": 0.0}, "async_update": acfg,
-                        "pipeline": {"fuse_decode": fuse}})
+                                   "early_stop_rel_tol": 0.0}, "async_update": acfg})
     sims, means = [], []
     sizes = dict(n_slots=cache.n_centroids, nprobe=cache.nprobe, max_tokens=cache.max_retrieval_tokens,
                  buffer=cache.buffer_size, padding=cache.padding_cluster_id, exec=cache.execution_stride)
