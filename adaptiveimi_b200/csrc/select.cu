@@ -40,11 +40,14 @@
 // through DSMEM, with its slice's key range in a per-rank slot (plain stores:
 // no shared initial value that remote updates could race with).  The first
 // cluster barrier is split (arrive at entry, wait just before the first DSMEM
-// store) so it costs nothing.  The leader alone
-// runs the boundary search, ranks the selected cells by warp ballots in slot
-// order, computes their row offsets with one block scan and writes the rows
-// with every warp.  Only slots below `slot_bound` (the occupied compact ids)
-// are scored and scanned.
+// store) so it costs nothing.  The leader alone runs the boundary search and
+// sends both thresholds to every CTA through DSMEM.  The emission is spread
+// over the cluster: each CTA ranks its own slice's selected cells (one block
+// scan of per-slot flags), places their rows (a second scan), publishes its
+// counts to every CTA, and after one cluster barrier writes its cells and
+// rows at the cluster-wide offsets; the leader adds the steady-zone rows, the
+// delta rows, the stop marker and the counts.  Only slots below `slot_bound`
+// (the occupied compact ids) are scored and scanned.
 //
 // Code shape matters here: the leader's code runs once per launch, so it is
 // kept compact -- plain functions with explicit arguments, one shared copy of

@@ -315,7 +315,9 @@ def decode_step(local: Sequence[SeqShard], q: torch.Tensor, zone_keys: Optional[
     if peer:
         s.peer_allgather(0, cand_all)
     else:
-        torch.distributed.all_gather_into_tensor(cand_all, s.cand, group=group)
+        # the flat form (output = the inputs concatenated along dim 0) works on
+        # every backend, gloo included
+        torch.distributed.all_gather_into_tensor(cand_all.view(plan.shards * bg, plan.record), s.cand, group=group)
     s.merge(cand_all, static_len)
     s.attend(q, zone_keys, zone_values)
     parts_all = torch.empty((plan.shards, s.partials.numel()), dtype=torch.float32, device=dev)
@@ -323,5 +325,5 @@ def decode_step(local: Sequence[SeqShard], q: torch.Tensor, zone_keys: Optional[
         s.peer_allgather(1, parts_all)
         s._peer["status_host"].copy_(s._peer["status"], non_blocking=True)
     else:
-        torch.distributed.all_gather_into_tensor(parts_all, s.partials, group=group)
+        torch.distributed.all_gather_into_tensor(parts_all.view(-1), s.partials, group=group)
     return combine(parts_all, plan.shards, bg, G, out)

@@ -640,11 +640,13 @@ def run_1m(args):
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
 
+    from adaptiveimi_b200 import ops
+
     def step(t):
         for l in range(L):
-            if rank == 0:  # decode append into the steady zone
-                zk[l][:, static0 + t] = nk[l][t]
-                zv[l][:, static0 + t] = nv[l][t]
+            if rank == 0:  # decode append into the steady zone (imi_decode_append)
+                ops.decode_append(new_keys=nk[l][t], new_values=nv[l][t], zone_keys=zk[l], zone_values=zv[l],
+                                  pos=static0 + t)
             seqshard.decode_step([shards[l]], qs[l][t], zk[l], zv[l], static0 + t + 1)
 
     for t in range(args.warmup):
