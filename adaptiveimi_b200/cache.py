@@ -84,6 +84,7 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             "kmeans": dict(runtime_config.get("kmeans") or {}),
             "async_update": dict(runtime_config.get("async_update") or {}),
             "prefetch": dict(runtime_config.get("prefetch") or {}),
+            "retrieval": dict(runtime_config.get("retrieval") or {}),
         }
         self.input_length = int(input_length) if input_length is not None else self.max_length - max_new_length
         self.actual_gen_len = max_new_length - 1
@@ -103,8 +104,12 @@ class adpimi_cache:  # noqa: N801  (reference class name)
             self.static_stride = self.input_length + self.actual_gen_len
         self.static_capacity = max(self.static_capacity, 1)
         # sizing (runtime.py:31-63), fixed at construction from the capacity
+        # runtime_config["retrieval"]["fixed_budget"] = False: top-nprobe cells
+        # without a token cap (not a reference mode; see RetrievalSizes)
+        self.fixed_budget = bool(self.runtime_config["retrieval"].get("fixed_budget", True))
         self.sizes = RetrievalSizes.from_capacity(self.list_capacity, self.subspace_parts, self.retrieval_budget,
-                                                  self.buffer_cluster_num, self.static_capacity, self.page_size)
+                                                  self.buffer_cluster_num, self.static_capacity, self.page_size,
+                                                  fixed_budget=self.fixed_budget)
         self.n_centroids = self.sizes.n_centroids
         self.padding_cluster_id = self.sizes.padding_cluster_id
         self.nprobe = self.sizes.nprobe

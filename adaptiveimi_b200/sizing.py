@@ -58,7 +58,13 @@ class RetrievalSizes:
 
     @staticmethod
     def from_capacity(list_capacity: int, subspace_parts: int, retrieval_budget: float, buffer_cluster_num: int,
-                      static_capacity: int, page_size: int = 8) -> "RetrievalSizes":
+                      static_capacity: int, page_size: int = 8, fixed_budget: bool = True) -> "RetrievalSizes":
+        """fixed_budget=False: the token budget is not fixed -- the selection is
+        the top nprobe cells (nprobe = the budget ratio of the cell count) with
+        neither a token cap nor page truncation.  The reference has no such
+        mode (its token budget is always int(budget * capacity)); this rule is
+        this library's reading of "budget_ratio without a fixed budget" and is
+        not pinned to reference code."""
         n_tokens = max(list_capacity, 1)
         total_clusters = max(int(n_tokens / 16), 1)
         if subspace_parts == 4:
@@ -82,7 +88,7 @@ class RetrievalSizes:
                     n_centroids = ivf_cells + 1
         nprobe = max(round((n_centroids - 1) * retrieval_budget), 1)
         nprobe = min(nprobe, n_centroids - 1)
-        max_tokens = max(int(retrieval_budget * list_capacity), 1)
+        max_tokens = max(int(retrieval_budget * list_capacity), 1) if fixed_budget else max(list_capacity, 1)
         token_pages = max((max_tokens + page_size - 1) // page_size, 1) if max_tokens > 0 else 0
         buffer_size = max(max(buffer_cluster_num, token_pages), 1)
         return RetrievalSizes(

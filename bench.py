@@ -696,6 +696,121 @@ def run_1m(args):
     }
 
 
+# ----------------------------------------------------------------------------
+# Qwen2.5-7B geometry, batch 8 with ragged contexts, S=4
+# ----------------------------------------------------------------------------
+METRIC_QWEN = "sparse_decode_us_per_layer_step@qwen7b_b8"
+CFG3 = dict(layers=28, q_heads=28, kv_heads=4, head_dim=128, theta=1e6, components=128, batch=8, ctx_lo=32768,
+            ctx_hi=131072, ctx_seed=1, subspace_parts=4, retrieval_budget=0.05, buffer_cluster_num=32,
+            static_start=32, static_end=64)
+# the reference's Qwen2.5-7B k-means settings (config/Qwen2.5-7B-Instruct.json); async update off there
+KMEANS3 = {"max_iters": 15, "tol": 0.0005, "early_stop_min_iter": 15, "early_stop_rel_tol": 0.0005}
+
+
+def run_qwen7b(args):
+    """8 sequences, contexts U[32768, 131072] (seed 1),
+    Qwen2.5-7B attention geometry (28 layers, 28 query / 4 KV heads), keys from a
+    128-component mixture with RoPE theta 1e6, IMI S=4, budget ratio 0.05
+    without a fixed token budget (top-nprobe cells; see RetrievalSizes).  The
+    reference's cache is batch-1 (cache_hub/adaptive_imi/cache.py:83-84), so
+    each sequence has its own cache, as a batch-8 server running the reference
+    would.  Each decode step (every layer, every sequence: append + select +
+    attention) is replayed from a CUDA graph captured before the timed region;
+    the value is device time per layer per step for the whole batch."""
+    from adaptiveimi_b200.attn import imi_decode_attn
+    from adaptiveimi_b200.cache import adpimi_cache
+    from adaptiveimi_b200.synthetic import mixture_keys
+
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return None
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    c = CFG3
+    L, kvh, G, D, B = c["layers"], c["kv_heads"], c["q_heads"] // c["kv_heads"], c["head_dim"], c["batch"]
+    g = torch.Generator().manual_seed(c["ctx_seed"])
+    ctxs = [int(x) for x in torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (B,), generator=g)]
+    steps_total = args.warmup + args.steps
+    caches, means = [], []
+    keys_built, build_ms = 0, 0.0
+    for b, ctx in enumerate(ctxs):
+        cache = adpimi_cache(
+            valid_start=[0], layer_num=L, batch_size=1, max_length=ctx + steps_total + 2, num_key_value_heads=kvh,
+            num_heads=kvh * G, head_dim=D, dtype=torch.bfloat16, layer_mapping={str(i): f"cuda:{local}" for i in range(L)},
+            max_new_length=steps_total + 2, input_length=ctx, static_pattern_start=c["static_start"],
+            static_pattern_end=c["static_end"], core=os.cpu_count() or 1, pages_per_cluster=2,
+            retrieval_budget=c["retrieval_budget"], cache_ratio=0.05, buffer_cluster_num=c["buffer_cluster_num"],
+            prefill_bsz=1, num_gpus=1, model_size=7, subspace_parts=c["subspace_parts"],
+            runtime_config={"kmeans": KMEANS3, "retrieval": {"fixed_budget": False}})
+        mb = []
+        for l in range(L):
+            k, m = mixture_keys(kvh, ctx, D, c["components"], 7919 * b + 1000 * l, c["theta"], device=dev)
+            gv = torch.Generator(device=dev).manual_seed(7919 * b + 1000 * l + 7)
+            v = torch.randn(kvh, ctx, D, generator=gv, device=dev)
+            ks = k.to(torch.bfloat16).transpose(0, 1).unsqueeze(0)
+            vs = v.to(torch.bfloat16).transpose(0, 1).unsqueeze(0)
+            del k, v
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            cache.prefill_update_kv_cache(None, ks, vs, l, 0)
+            e1.record()
+            torch.cuda.synchronize()
+            build_ms += e0.elapsed_time(e1)
+            keys_built += kvh * cache.list_stride
+            mb.append(m)
+            del ks, vs
+        cache.prepare_cache()
+        caches.append(cache)
+        means.append(mb)
+        torch.cuda.empty_cache()
+    qds = [decode_inputs(means[b], G, ctxs[b], steps_total, dev, seed=b) for b in range(B)]
+
+    def step(t):
+        for l in range(L):
+            for b in range(B):
+                qd, kd, vd = qds[b]
+                caches[b].decode_update_kv_cache(kd[t, l], vd[t, l], l)
+                imi_decode_attn(qd[t, l], None, None, l, caches[b])
+
+    for t in range(args.warmup):
+        step(t)
+    torch.cuda.synchronize()
+    graphs = []
+    for t in range(args.warmup, steps_total):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step(t)
+        graphs.append(gr)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for gr in graphs:
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    us = ms * 1000.0 / (args.steps * L)
+    rows = [int(cc._dec[f"cuda:{local}"]["row_count"].sum()) for cc in caches]
+    return {
+        "metric": METRIC_QWEN, "value": round(us, 3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (128-component Gaussian-mixture keys + RoPE theta 1e6, N(0,1) values; seeded)",
+        "config": {"workload": "BASELINE configs[3]: Qwen2.5-7B geometry, batch 8 (one batch-1 cache per sequence), "
+                               "ragged contexts U[32768, 131072] seed 1, IMI S=4, budget ratio 0.05 without a fixed "
+                               "token budget (top-nprobe cells; not a reference mode, unpinned)",
+                   "contexts": ctxs, "layers": L, "kv_heads": kvh, "q_heads": c["q_heads"], "head_dim": D,
+                   "global_batch": B, "n_slots": [cc.n_centroids for cc in caches],
+                   "nprobe": [cc.nprobe for cc in caches], "rows_last_layer": rows,
+                   "timing": "CUDA-graph replay of each whole step (28 layers x 8 sequences), device events"},
+        "build": {"metric": "IMI build Mkeys/s", "value": round(keys_built / (build_ms * 1e-3) / 1e6, 3),
+                  "unit": "Mkeys/s", "build_ms_total": round(build_ms, 2), "keys": keys_built, "kmeans": KMEANS3},
+        "clocks": clk.summary(),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -705,8 +820,9 @@ def main():
     ap.add_argument("--layers", type=int, default=CFG["layers"])
     ap.add_argument("--context", type=int, default=None, help="default: 131072 (128k) or 1048576 (1m)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="128k", choices=["128k", "1m"],
-                    help="1m: BASELINE configs[2], the 1M context sequence-sharded over the ranks")
+    ap.add_argument("--workload", default="128k", choices=["128k", "1m", "qwen7b"],
+                    help="1m: BASELINE configs[2], the 1M context sequence-sharded over the ranks; "
+                         "qwen7b: BASELINE configs[3], batch 8 with ragged contexts, S=4")
     args = ap.parse_args()
     if args.context is None:
         args.context = 1_048_576 if args.workload == "1m" else CFG["context"]
@@ -721,6 +837,20 @@ def main():
         if args.warmup < 3:
             args.warmup = 3
         res = run_1m(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if args.workload == "qwen7b":
+        if args.impl == "reference":
+            ws, rank, _ = dist_env()
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "metric": METRIC_QWEN,
+                                  "unavailable": "the reference's CPU decode path for config 3 is not sampled"}),
+                      flush=True)
+            return
+        args.warmup = max(args.warmup, 3)
+        args.steps = min(args.steps, 16)
+        res = run_qwen7b(args)
         if res is not None:
             print(json.dumps(res), flush=True)
         return

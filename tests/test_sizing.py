@@ -50,3 +50,10 @@ def test_ivf_slots_widen_only_when_the_build_overflows_prepare_cache():
     # 8 096 tokens: 506 cells fit prepare_cache's 1 025 slots, which are kept
     s = RetrievalSizes.from_capacity(8096, 0, 0.1, 32, static_capacity=97)
     assert (s.n_centroids, s.nprobe) == (1025, 102)
+
+
+def test_without_a_fixed_budget_only_nprobe_limits():
+    s = RetrievalSizes.from_capacity(81920, 4, 0.05, 32, static_capacity=97, fixed_budget=False)
+    k = adaptive_k(81920, 4)[0]
+    assert s.n_centroids == k ** 4 + 1 and s.nprobe == round(k ** 4 * 0.05)
+    assert s.max_retrieval_tokens == 81920 and s.buffer_size == 81920 // 8
