@@ -32,7 +32,7 @@ class BuildDesc(ctypes.Structure):
         ("cell_sizes", P), ("cell_offsets", P), ("cell_mask", P), ("cell_code", P),
         ("centroids", P), ("sub_centroids", P), ("sub_labels", P), ("n_active", P), ("iters_run", P),
         ("workspace", P), ("workspace_bytes", sz),
-        ("status", P), ("phase_ns", P),
+        ("status", P), ("phase_ns", P), ("ready_event", P),
     ]
 
 

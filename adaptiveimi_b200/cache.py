@@ -131,12 +131,20 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.list_values: List[Optional[torch.Tensor]] = [None] * layer_num
         self.index: List[Optional[ops.IMIIndex]] = [None] * layer_num
         self.imi_pipelines: List[Optional[IMIPipeline]] = []
+        # the device builds run on one side stream per device, next to the
+        # prefill (runtime_config["pipeline"]["async_build"], default on)
+        self.async_build = bool(self.runtime_config["pipeline"].get("async_build", True))
+        self._build_streams: Dict[str, torch.cuda.Stream] = {}
+        if self.build_index_when_prefilling and self.async_build and torch.cuda.is_available():
+            for dev in self.device_list:
+                self._build_streams[dev] = torch.cuda.Stream(device=torch.device(dev))
         if self.build_index_when_prefilling:
             for ldx in range(layer_num):
                 self.imi_pipelines.append(IMIPipeline(
                     layer_idx=ldx, kv_heads=self.kv_head, head_dim=head_dim, dtype=dtype,
                     device_id=int(self.layer_mapping[str(ldx)].split(":")[-1]), max_tokens=self.list_capacity,
                     subspace_parts=self.subspace_parts, n_slots=self.n_centroids,
+                    build_stream=self._build_streams.get(self.layer_mapping[str(ldx)]),
                     runtime_config=IMIRuntimeConfig(pipeline=self.runtime_config["pipeline"],
                                                     kmeans=self.runtime_config["kmeans"])))
         else:

@@ -1889,18 +1889,22 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
             return e;
         if ((e = cudaMemcpyAsync(ws + L.reseed, rs.data(), rs.size() * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
             return e;
-        // pageable copies are staged before return; keep the vectors alive
-        // until the stream has consumed them anyway
-        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
+        // prev_inertia = FLT_MAX
+        std::vector<float> pv(d.T, FLT_MAX);
+        if ((e = cudaMemcpyAsync(d.prev_inertia, pv.data(), pv.size() * 4, cudaMemcpyHostToDevice, st)) !=
+            cudaSuccess)
+            return e;
+        // A copy from pageable host memory returns once the data is staged, so
+        // the vectors may go out of scope here.  It also waits for the work
+        // already in `st` (the previous build on that stream), but not for the
+        // ready event below: the producer of the keys keeps running.
+    }
+    if (a.ready_event) {  // the keys / values are produced on another stream
+        cudaError_t e = cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(a.ready_event), 0);
+        if (e != cudaSuccess) return e;
     }
     cudaMemsetAsync(d.done, 0, (size_t)d.T * 4, st);
     cudaMemsetAsync(d.iters_run, 0, (size_t)d.T * 4, st);
-    {
-        // prev_inertia = FLT_MAX
-        std::vector<float> pv(d.T, FLT_MAX);
-        cudaMemcpyAsync(d.prev_inertia, pv.data(), pv.size() * 4, cudaMemcpyHostToDevice, st);
-        cudaStreamSynchronize(st);
-    }
     cudaError_t e;
     if (a.phase_ns) stamp_kernel<<<1, 32, 0, st>>>(a.phase_ns);
     if (sub == 64) e = run_kmeans_sub<64>(d, a, st);

@@ -15,6 +15,7 @@ device status word reports a give-up (or whose cells overflow the slots) goes to
 """
 from __future__ import annotations
 
+import contextlib
 import enum
 import time
 from dataclasses import dataclass, field
@@ -75,6 +76,12 @@ class IMIPipeline:
     runtime_config: IMIRuntimeConfig = field(default_factory=IMIRuntimeConfig)
     enable_direct_write: bool = True
     n_slots: Optional[int] = None
+    # a side stream for the build: the build waits for the producer's stream
+    # (an event) and then runs next to it, so the prefill of later layers
+    # overlaps this layer's k-means (the reference overlaps its host k-means
+    # the same way, layer_pipeline.cpp:430-700).  None: the build runs on the
+    # caller's stream.
+    build_stream: Optional[torch.cuda.Stream] = None
 
     def __post_init__(self) -> None:
         if self.subspace_parts not in (0, 2, 4):
@@ -142,15 +149,27 @@ class IMIPipeline:
         self._status = torch.zeros((1,), dtype=torch.int32, device=dev)
         self._phase_ns = torch.zeros((3,), dtype=torch.int64, device=dev)
         self._done_event = torch.cuda.Event()
+        side = self.build_stream
         with torch.cuda.device(dev):
+            ready = None
+            if side is not None:  # keys/values (and the words above) are ready once the caller's stream gets here
+                ready = torch.cuda.Event()
+                ready.record(torch.cuda.current_stream(dev))
             try:
-                self.index = ops.build_index(keys, values, parts=self.subspace_parts, ks=ks, n_slots=n_slots,
-                                             list_keys=list_keys, list_values=list_values, status=self._status,
-                                             phase_ns=self._phase_ns, **settings)
+                with torch.cuda.stream(side) if side is not None else contextlib.nullcontext():
+                    self.index = ops.build_index(keys, values, parts=self.subspace_parts, ks=ks, n_slots=n_slots,
+                                                 list_keys=list_keys, list_values=list_values, status=self._status,
+                                                 phase_ns=self._phase_ns, ready_event=ready, **settings)
+                    self._done_event.record()
             except Exception as exc:  # mark_failure (layer_pipeline.cpp:232-236)
                 self._mark_failure(str(exc))
                 raise RuntimeError(f"IMI pipeline failed: {exc}") from exc
-            self._done_event.record()
+            if side is not None:
+                # the producer's tensors (and the words it zeroed) are in use on
+                # the side stream until the build is done
+                for t in (keys, values, self._status, self._phase_ns, list_keys, list_values):
+                    if t is not None:
+                        t.record_stream(side)
         self._token_count = n
 
     def _mark_failure(self, message: str) -> None:
@@ -296,6 +315,13 @@ class IMIPipeline:
             "total_chunks": max(1, self._chunks_seen), "total_tokens": int(token_count),
             "build_ms": kmeans_ms + reorganize_ms,
         }
+        if self.build_stream is not None:
+            # the index was allocated on the build stream and is read on the
+            # caller's stream from here on
+            cur = torch.cuda.current_stream(self._device())
+            for name in ("list_keys", "list_values", "cell_sizes", "cell_offsets", "cell_mask", "cell_code",
+                         "centroids", "sub_centroids", "sub_labels", "n_active", "iters_run"):
+                getattr(idx, name).record_stream(cur)
         if list_keys is not None and list_values is not None and list_keys.data_ptr() != idx.list_keys.data_ptr():
             list_keys[0, :, :token_count].copy_(idx.list_keys)
             list_values[0, :, :token_count].copy_(idx.list_values)

@@ -86,7 +86,7 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
                 early_stop_rel_tol: float = 5e-4, list_keys: Optional[torch.Tensor] = None,
                 list_values: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
                 kmax: Optional[int] = None, status: Optional[torch.Tensor] = None,
-                phase_ns: Optional[torch.Tensor] = None) -> IMIIndex:
+                phase_ns: Optional[torch.Tensor] = None, ready_event: Optional[torch.cuda.Event] = None) -> IMIIndex:
     """Build the IMI of one layer on the device.
 
     keys / values: [heads, n, D] bf16 CUDA views whose last dim is contiguous
@@ -95,7 +95,8 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
     order; allocated when not given.  ``status``: int32 [1] device word, bit 0
     set when the tensor-core E-step gave up (the index is then void).
     ``phase_ns``: int64 [3] device timestamps (k-means start, k-means end,
-    reorganize end).
+    reorganize end).  ``ready_event``: an event recorded after keys/values were
+    produced on another stream; the build (on the current stream) waits for it.
     """
     if keys.dim() != 3 or keys.shape != values.shape:
         raise ValueError("keys/values must be [kv_heads, tokens, head_dim] and share a shape")
@@ -142,6 +143,7 @@ def build_index(keys: torch.Tensor, values: torch.Tensor, *, parts: int, ks: Seq
     d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel()
     d.status = status.data_ptr() if status is not None else None
     d.phase_ns = phase_ns.data_ptr() if phase_ns is not None else None
+    d.ready_event = ready_event.cuda_event if ready_event is not None else None
     L = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(L.imi_build_index(ctypes.byref(d), _stream(dev)), "imi_build_index")

@@ -103,6 +103,10 @@ typedef struct imi_build_desc {
                                               the stream when k-means starts, when it ends and when
                                               the reorganize (CSR lists, padded metadata, list rows)
                                               ends: the per-stage times of PipelineStats */
+    void* ready_event;                     /* cudaEvent_t or NULL: recorded where keys / values are
+                                              produced; the build's stream waits for it after staging
+                                              its seeded draws and before the first kernel, so the
+                                              build can run on a side stream next to the producer */
 } imi_build_desc;
 
 typedef struct imi_select_desc {

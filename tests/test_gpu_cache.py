@@ -175,3 +175,32 @@ def test_cache_decode_matches_reference_simulation(mode):
             worst = max(worst, float(err.max()))
             assert err.max() <= 2e-2 and err.mean() <= 2e-3, (t, l, float(err.max()))
     assert cache.context == ctx + gen
+
+
+def test_build_on_a_side_stream_matches_the_stream_ordered_build():
+    """IMIPipeline with a build stream (the cache's default): the build waits for
+    the producer's stream, runs beside it, and gives the same index as a build on
+    the caller's stream; the producer may drop its K/V right after the call."""
+    from adaptiveimi_b200.imi_adapter import IMIPipeline, IMIRuntimeConfig
+
+    kv, G, ctx = 4, 4, 4096
+    K, V, _ = make_layer(kv, kv * G, ctx, 128, 32, 31, 500000.0)
+    cfg = IMIRuntimeConfig(kmeans={"k1": 16, "k2": 16, "max_iters": 6, "early_stop_min_iter": 6, "tol": 0.0,
+                                   "early_stop_rel_tol": 0.0})
+    out = []
+    for side in (None, torch.cuda.Stream()):
+        pipe = IMIPipeline(layer_idx=0, kv_heads=kv, head_dim=128, dtype=torch.bfloat16, device_id=0,
+                           max_tokens=ctx, runtime_config=cfg, n_slots=257, build_stream=side)
+        ks = K.transpose(0, 1).unsqueeze(0).cuda()
+        vs = V.transpose(0, 1).unsqueeze(0).cuda()
+        torch.cuda._sleep(2_000_000)  # the producer's stream is still busy when the build is issued
+        pipe.start_index_chunked(ks, vs, 32, ctx - 64, 0)
+        del ks, vs  # the build keeps the storage alive (record_stream)
+        torch.empty(64 << 20, dtype=torch.uint8, device="cuda").fill_(7)  # a reuse attempt of freed blocks
+        idx = pipe.finish_index(as_host_metadata=False)
+        st = pipe.get_pipeline_stats()
+        assert st["kmeans_ms"] > 0 and st["reorganize_ms"] > 0
+        out.append(idx)
+    a, b = out
+    for name in ("cell_sizes", "cell_offsets", "cell_code", "centroids", "list_keys", "list_values"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
