@@ -131,13 +131,17 @@ class adpimi_cache:  # noqa: N801  (reference class name)
         self.list_values: List[Optional[torch.Tensor]] = [None] * layer_num
         self.index: List[Optional[ops.IMIIndex]] = [None] * layer_num
         self.imi_pipelines: List[Optional[IMIPipeline]] = []
-        # the device builds run on one side stream per device, next to the
-        # prefill (runtime_config["pipeline"]["async_build"], default on)
-        self.async_build = bool(self.runtime_config["pipeline"].get("async_build", True))
+        # runtime_config["pipeline"]["async_build"] (default off): the device
+        # builds run on one side stream per device, next to the prefill.  Off
+        # by default: beside a prefill whose GEMMs hold every SM the build gains
+        # nothing (bench.py --workload prefill_overlap)
+        self.async_build = bool(self.runtime_config["pipeline"].get("async_build", False))
         self._build_streams: Dict[str, torch.cuda.Stream] = {}
         if self.build_index_when_prefilling and self.async_build and torch.cuda.is_available():
             for dev in self.device_list:
-                self._build_streams[dev] = torch.cuda.Stream(device=torch.device(dev))
+                # high priority: the build is a chain of short dependent kernels;
+                # pending CTAs of the prefill's long GEMMs must not hold it back
+                self._build_streams[dev] = torch.cuda.Stream(device=torch.device(dev), priority=-1)
         if self.build_index_when_prefilling:
             for ldx in range(layer_num):
                 self.imi_pipelines.append(IMIPipeline(

@@ -178,7 +178,7 @@ def test_cache_decode_matches_reference_simulation(mode):
 
 
 def test_build_on_a_side_stream_matches_the_stream_ordered_build():
-    """IMIPipeline with a build stream (the cache's default): the build waits for
+    """IMIPipeline with a build stream (the cache's async_build option): the build waits for
     the producer's stream, runs beside it, and gives the same index as a build on
     the caller's stream; the producer may drop its K/V right after the call."""
     from adaptiveimi_b200.imi_adapter import IMIPipeline, IMIRuntimeConfig
