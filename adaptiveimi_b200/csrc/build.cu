@@ -74,6 +74,7 @@ struct Dev {
     int nx;                // n rounded up to a whole tile of 128
     int npad;              // centroids rounded up to 16 (0 when the tensor-core E-step is not used)
     int32_t* status;       // [1] or null
+    uint32_t* kpp_ticket;  // [T] k-means++ step tickets (zero between steps)
 };
 
 IMI_DEV int task_h(const Dev& b, int t) { return t / b.S; }
@@ -189,17 +190,180 @@ __global__ void kpp_first_kernel(Dev b) {
         b.cent[(size_t)t * b.kmax * b.sub + d] = bf16_bits_to_f32(x[d]);
 }
 
+// Block-wide inclusive scan of one u128 per thread (NT threads); ws: [32] lo
+// and [32] hi scratch.  Returns the inclusive prefix; *total = the block sum.
+template <int NT>
+IMI_DEV u128 kpp_scan_u128(u128 v, unsigned long long* wlo, unsigned long long* whi, u128* total) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    u128 x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        u128 y = u128_shfl_up(x, o);
+        if (lane >= o) x = u128_add(x, y);
+    }
+    if (lane == 31) {
+        wlo[w] = x.lo;
+        whi[w] = x.hi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        u128 y = lane < NW ? u128{wlo[lane], whi[lane]} : u128{0ull, 0ull};
+        for (int o = 1; o < 32; o <<= 1) {
+            u128 z = u128_shfl_up(y, o);
+            if (lane >= o) y = u128_add(y, z);
+        }
+        if (lane < NW) {
+            wlo[lane] = y.lo;
+            whi[lane] = y.hi;
+        }
+    }
+    __syncthreads();
+    if (w > 0) x = u128_add(x, u128{wlo[w - 1], whi[w - 1]});
+    *total = u128{wlo[NW - 1], whi[NW - 1]};
+    __syncthreads();
+    return x;
+}
+
+// The k-means++ draw of centroid c of task t (kmeans_core.cpp:160-182): the
+// exact Q64.64 total of the min-distances (the blocks' partials), the target
+// u * total, the first sample whose inclusive cumulative weight reaches it;
+// that sample becomes centroid c.  When the reference's sequential double
+// cumsum could round (an unrepresentable value, or more than 53 significant
+// bits) the reference's own loop runs instead.  All NT threads of the block
+// call it; smem holds 16 * NB bytes.
+template <int NT>
+IMI_DEV void kpp_pick_block(const Dev& b, int t, int c, unsigned char* smem) {
+    constexpr int NW = NT / 32;
+    constexpr int PER = SPB / NT;  // samples per thread in the crossing block
+    const int s = task_s(b, t);
+    unsigned long long* plo = reinterpret_cast<unsigned long long*>(smem);  // inclusive prefix per block
+    unsigned long long* phi = plo + b.NB;
+    __shared__ int s_minl, s_bad, s_sel, s_blk;
+    __shared__ unsigned long long wlo[32], whi[32];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    u128 carry{0ull, 0ull};
+    int ml = INT_MAX, bb = 0;
+    for (int q0 = 0; q0 < b.NB; q0 += NT) {  // inclusive prefix of the block partials
+        const int q = q0 + tid;
+        u128 v{0ull, 0ull};
+        if (q < b.NB) {
+            const size_t o = (size_t)t * b.NB + q;
+            v = u128{__ldcg(b.part_lo + o), __ldcg(b.part_hi + o)};
+            ml = min(ml, __ldcg(b.part_minl + o));
+            bb |= __ldcg(b.part_bad + o);
+        }
+        u128 tot;
+        u128 x = u128_add(kpp_scan_u128<NT>(v, wlo, whi, &tot), carry);
+        if (q < b.NB) {
+            plo[q] = x.lo;
+            phi[q] = x.hi;
+        }
+        carry = u128_add(carry, tot);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        ml = min(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+        bb |= __shfl_xor_sync(0xffffffffu, bb, o);
+    }
+    if (lane == 0) {
+        wlo[w] = (unsigned long long)(unsigned)ml;
+        whi[w] = (unsigned long long)bb;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int m2 = INT_MAX, b2 = 0;
+        for (int q = 0; q < NW; ++q) {
+            m2 = min(m2, (int)(unsigned)wlo[q]);
+            b2 |= (int)whi[q];
+        }
+        s_minl = m2;
+        s_bad = b2;
+        s_sel = -1;
+        s_blk = b.NB - 1;
+    }
+    __syncthreads();
+    const u128 total = carry;
+    const float* md = b.md + (size_t)t * b.n;
+    const double u = b.draws_u[s * b.kst + c];
+    bool exact = !s_bad;
+    if (exact && (total.lo | total.hi)) exact = (u128_bitlen(total) - (s_minl + 64)) <= 53;
+    if (!exact) {
+        if (tid == 0) {  // the reference's own sequential double loop (kmeans_core.cpp:164-182)
+            double tot = 0.0;
+            for (int i = 0; i < b.n; ++i) tot += (double)__ldcg(md + i);
+            const double target = u * tot + 0.0;
+            double run = 0.0;
+            int sel = 0;
+            for (int i = 0; i < b.n; ++i) {
+                run += (double)__ldcg(md + i);
+                if (run >= target) {
+                    sel = i;
+                    break;
+                }
+            }
+            s_sel = sel;
+        }
+    } else {
+        const double totd = u128_to_double_units(total);
+        const double target = u * totd + 0.0;
+        const u128 tgt = ceil_units(target);
+        for (int q = tid; q < b.NB; q += NT)
+            if (u128_ge(u128{plo[q], phi[q]}, tgt)) atomicMin(&s_blk, q);  // the first block reaching the target
+        __syncthreads();
+        const int blk = s_blk;
+        const u128 base = blk > 0 ? u128{plo[blk - 1], phi[blk - 1]} : u128{0ull, 0ull};
+        // the crossing block's samples in order: PER consecutive ones per thread
+        const int i0 = blk * SPB + tid * PER;
+        u128 loc[PER];
+        u128 sum{0ull, 0ull};
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            int l, bad = 0;
+            const int i = i0 + r;
+            const u128 v = i < b.n ? to_units(__ldcg(md + i), l, bad) : u128{0ull, 0ull};
+            sum = u128_add(sum, v);
+            loc[r] = sum;
+        }
+        u128 btot;
+        const u128 incl = kpp_scan_u128<NT>(sum, wlo, whi, &btot);
+        // exclusive prefix of this thread = incl - sum (two's-complement 128-bit)
+        u128 ex;
+        ex.lo = incl.lo - sum.lo;
+        ex.hi = incl.hi - sum.hi - (incl.lo < sum.lo ? 1ull : 0ull);
+        ex = u128_add(ex, base);
+#pragma unroll
+        for (int r = 0; r < PER; ++r) {
+            const int i = i0 + r;
+            if (i < b.n && u128_ge(u128_add(ex, loc[r]), tgt)) {
+                atomicMin(reinterpret_cast<unsigned int*>(&s_sel), (unsigned int)i);  // -1 -> 0xffffffff
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    int sel = s_sel;
+    if (sel < 0 || sel >= b.n) sel = 0;
+    const uint16_t* xs = sample_ptr(b, t, sel);
+    for (int d = tid; d < b.sub; d += NT) b.cent[((size_t)t * b.kmax + c) * b.sub + d] = bf16_bits_to_f32(xs[d]);
+}
+
 // Distances of every sample to the newest centroid; min with the running
 // min-distance; the block's exact Q64.64 sum.  The sample rows are staged in
 // shared memory 256 at a time by coalesced 16-byte cp.async (8-16 threads per
 // row), double-buffered, so the pass streams at DRAM speed; each thread then
 // reads its own row (a 16-byte pad per row keeps those reads conflict-free).
+// One k-means++ step of tasks [t0, t0 + gridDim.y) in one launch: every block updates
+// its samples' min-distances and writes its exact partial sum; the last block
+// of each task (an atomic ticket) then draws the task's next centroid.
 template <int SUB>
-__global__ void __launch_bounds__(BT) kpp_update_kernel(Dev b, int c) {
+__global__ void __launch_bounds__(BT) kpp_step_kernel(Dev b, int c, int t0) {
     constexpr int CPR = SUB / 8;    // 16-byte chunks per row
     constexpr int PITCH = SUB + 8;  // bf16 per staged row
-    const int t = blockIdx.y;
-    if (c >= b.ks[task_s(b, t)]) return;
+    const int t = t0 + blockIdx.y;
+    // a programmatic dependent of the previous step: nothing is read before
+    // the previous step (its min-distances and its centroid) has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (t >= b.T || c >= b.ks[task_s(b, t)]) return;
     extern __shared__ __align__(16) uint16_t kst[];  // [2][BT][PITCH]
     __shared__ __align__(16) float cp[SUB];
     __shared__ unsigned long long rlo[BT / 32], rhi[BT / 32];
@@ -292,162 +456,29 @@ __global__ void __launch_bounds__(BT) kpp_update_kernel(Dev b, int c) {
         b.part_minl[o] = ml;
         b.part_bad[o] = bb;
     }
+    // The last block of the task to finish draws centroid c: the block
+    // barrier orders every thread's min-distance stores (and thread 0's
+    // partial) before thread 0's release; its acquire plus the barrier order
+    // the drawing block's loads after all of them.
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned old;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;\n" : "=r"(old) : "l"(b.kpp_ticket + t) : "memory");
+        s_last = old == (unsigned)(gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    kpp_pick_block<BT>(b, t, c, reinterpret_cast<unsigned char*>(kst));
+    if (threadIdx.x == 0) b.kpp_ticket[t] = 0;  // re-armed for the next step
 }
+
+
 
 template <int SUB>
-size_t kpp_update_smem() {
-    return (size_t)2 * BT * (SUB + 8) * 2;
-}
-
-// One CTA (1024 threads) per task: exact total, target, first crossing index.
-__global__ void __launch_bounds__(1024) kpp_pick_kernel(Dev b, int c) {
-    const int t = blockIdx.x;
-    const int s = task_s(b, t);
-    if (c >= b.ks[s]) return;
-    extern __shared__ __align__(16) unsigned char ksm[];
-    unsigned long long* plo = reinterpret_cast<unsigned long long*>(ksm);  // inclusive prefix per block
-    unsigned long long* phi = plo + b.NB;
-    __shared__ int s_minl, s_bad, s_sel, s_blk;
-    __shared__ unsigned long long s_tlo, s_thi;
-    __shared__ unsigned long long wlo[32], whi[32];
-    const int tid = threadIdx.x;
-    {   // inclusive prefix of the block partials (one per thread, in chunks of 1024),
-        // their minimum lsb and any unrepresentable value
-        const int lane = tid & 31, w = tid >> 5;
-        u128 carry{0ull, 0ull};
-        int ml = INT_MAX, bb = 0;
-        for (int q0 = 0; q0 < b.NB; q0 += 1024) {
-            const int q = q0 + tid;
-            u128 v{0ull, 0ull};
-            if (q < b.NB) {
-                const size_t o = (size_t)t * b.NB + q;
-                v = u128{b.part_lo[o], b.part_hi[o]};
-                ml = min(ml, b.part_minl[o]);
-                bb |= b.part_bad[o];
-            }
-            u128 x = v;
-            for (int o = 1; o < 32; o <<= 1) {
-                u128 y = u128_shfl_up(x, o);
-                if (lane >= o) x = u128_add(x, y);
-            }
-            if (lane == 31) {
-                wlo[w] = x.lo;
-                whi[w] = x.hi;
-            }
-            __syncthreads();
-            if (w == 0) {
-                u128 y{wlo[lane], whi[lane]};
-                for (int o = 1; o < 32; o <<= 1) {
-                    u128 z = u128_shfl_up(y, o);
-                    if (lane >= o) y = u128_add(y, z);
-                }
-                wlo[lane] = y.lo;
-                whi[lane] = y.hi;
-            }
-            __syncthreads();
-            if (w > 0) x = u128_add(x, u128{wlo[w - 1], whi[w - 1]});
-            x = u128_add(x, carry);
-            if (q < b.NB) {
-                plo[q] = x.lo;
-                phi[q] = x.hi;
-            }
-            carry = u128_add(carry, u128{wlo[31], whi[31]});
-            __syncthreads();
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            ml = min(ml, __shfl_xor_sync(0xffffffffu, ml, o));
-            bb |= __shfl_xor_sync(0xffffffffu, bb, o);
-        }
-        if (lane == 0) {
-            wlo[w] = (unsigned long long)(unsigned)ml;
-            whi[w] = (unsigned long long)bb;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            int m2 = INT_MAX, b2 = 0;
-            for (int q = 0; q < 32; ++q) {
-                m2 = min(m2, (int)(unsigned)wlo[q]);
-                b2 |= (int)whi[q];
-            }
-            s_minl = m2;
-            s_bad = b2;
-            s_sel = -1;
-            s_blk = -1;
-            s_tlo = carry.lo;
-            s_thi = carry.hi;
-        }
-    }
-    __syncthreads();
-    const u128 total{s_tlo, s_thi};
-    const float* md = b.md + (size_t)t * b.n;
-    const double u = b.draws_u[s * b.kst + c];
-    bool exact = !s_bad;
-    if (exact && (total.lo | total.hi)) exact = (u128_bitlen(total) - (s_minl + 64)) <= 53;
-    if (!exact) {
-        // the reference's own sequential double loop (kmeans_core.cpp:164-182)
-        if (tid == 0) {
-            double tot = 0.0;
-            for (int i = 0; i < b.n; ++i) tot += (double)md[i];
-            const double target = u * tot + 0.0;
-            double run = 0.0;
-            int sel = 0;
-            for (int i = 0; i < b.n; ++i) {
-                run += (double)md[i];
-                if (run >= target) {
-                    sel = i;
-                    break;
-                }
-            }
-            s_sel = sel;
-        }
-    } else {
-        const double totd = u128_to_double_units(total);
-        const double target = u * totd + 0.0;
-        const u128 tgt = ceil_units(target);
-        if (tid == 0) s_blk = b.NB - 1;
-        __syncthreads();
-        for (int q = tid; q < b.NB; q += blockDim.x)
-            if (u128_ge(u128{plo[q], phi[q]}, tgt)) atomicMin(&s_blk, q);  // the first block reaching the target
-        __syncthreads();
-        const int blk = s_blk;
-        u128 base{0ull, 0ull};
-        if (blk > 0) base = u128{plo[blk - 1], phi[blk - 1]};
-        // inclusive scan of this block's samples in order (1 per thread)
-        const int i = blk * SPB + tid;
-        int l, bad = 0;
-        u128 v = (i < b.n) ? to_units(md[i], l, bad) : u128{0ull, 0ull};
-        u128 x = v;
-        const int lane = tid & 31, w = tid >> 5;
-        for (int o = 1; o < 32; o <<= 1) {
-            u128 y = u128_shfl_up(x, o);
-            if (lane >= o) x = u128_add(x, y);
-        }
-        if (lane == 31) {
-            wlo[w] = x.lo;
-            whi[w] = x.hi;
-        }
-        __syncthreads();
-        if (w == 0) {
-            u128 y{wlo[lane], whi[lane]};
-            for (int o = 1; o < 32; o <<= 1) {
-                u128 z = u128_shfl_up(y, o);
-                if (lane >= o) y = u128_add(y, z);
-            }
-            wlo[lane] = y.lo;
-            whi[lane] = y.hi;
-        }
-        __syncthreads();
-        if (w > 0) x = u128_add(x, u128{wlo[w - 1], whi[w - 1]});
-        x = u128_add(x, base);
-        const bool hit = (i < b.n) && u128_ge(x, tgt);
-        if (hit) atomicMin(reinterpret_cast<unsigned int*>(&s_sel), (unsigned int)i);  // s_sel = -1 -> 0xffffffff
-    }
-    __syncthreads();
-    int sel = s_sel;
-    if (sel < 0 || sel >= b.n) sel = 0;
-    const uint16_t* xs = sample_ptr(b, t, sel);
-    for (int d = tid; d < b.sub; d += blockDim.x)
-        b.cent[((size_t)t * b.kmax + c) * b.sub + d] = bf16_bits_to_f32(xs[d]);
+size_t kpp_step_smem(int NB) {
+    const size_t stage = (size_t)2 * BT * (SUB + 8) * 2, pick = (size_t)16 * NB;
+    return stage > pick ? stage : pick;
 }
 
 // ---------------------------------------------------------------------------
@@ -1592,7 +1623,7 @@ namespace {
 
 struct Layout {
     size_t labels, md, perm_a, perm_b, part_lo, part_hi, part_minl, part_bad, hist, dig_off, dig_tot, counts, offs,
-        erank, order, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, xn, total;
+        erank, order, draws_u, first, reseed, done, prev, iters, used, g2c, chi, clo, cn, xn, tick, total;
     int npad;
 };
 
@@ -1646,6 +1677,7 @@ Layout layout(int heads, int n, int dim, int parts, const int* ks, int max_iters
     L.clo = take((size_t)T * L.npad * (sub + 16) * 2);
     L.cn = take((size_t)T * L.npad * 4);
     L.xn = take(L.npad > 0 ? (size_t)T * ((n + 127) / 128 * 128) * 4 : 0);
+    L.tick = take((size_t)T * 4);
     L.total = o;
     return L;
 }
@@ -1664,18 +1696,17 @@ static cudaError_t run_kmeans_sub(Dev& d, const BuildArgs& a, cudaStream_t st) {
     kpp_first_kernel<<<d.T, 128, 0, st>>>(d);
     int kmax_all = 0;
     for (int s = 0; s < d.S; ++s) kmax_all = std::max(kmax_all, d.ks[s]);
-    const size_t pick_smem = (size_t)d.NB * 16;
-    if ((e = cudaFuncSetAttribute(kpp_pick_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pick_smem)) !=
-        cudaSuccess)
+    const size_t step_smem = kpp_step_smem<SUB>(d.NB);
+    if ((e = cudaFuncSetAttribute(kpp_step_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)step_smem)) != cudaSuccess)
         return e;
-    const size_t upd_smem = kpp_update_smem<SUB>();
-    if ((e = cudaFuncSetAttribute(kpp_update_kernel<SUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)upd_smem)) != cudaSuccess)
-        return e;
-    for (int c = 1; c < kmax_all; ++c) {
-        kpp_update_kernel<SUB><<<dim3(d.NB, d.T), BT, upd_smem, st>>>(d, c);
-        kpp_pick_kernel<<<d.T, 1024, pick_smem, st>>>(d, c);
-    }
+    // One launch per step over every task.  (Steps over groups of tasks whose
+    // samples stay resident in L2 were measured slower: 4 groups of 4 tasks
+    // took 148.7 ms against 116.3 ms for 8 config-1 layers -- the per-step
+    // launch and draw latency outweighs the saved HBM traffic.)
+    for (int c = 1; c < kmax_all; ++c)
+        if ((e = launch_pdl(kpp_step_kernel<SUB>, dim3(d.NB, d.T), dim3(BT), step_smem, st, d, c, 0)) != cudaSuccess)
+            return e;
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // ---- Lloyd
     const int chunk = std::min(kmax_all, 32768 / SUB);
@@ -1859,6 +1890,7 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
     d.xn = reinterpret_cast<float*>(ws + L.xn);
     d.nx = (d.n + 127) / 128 * 128;
     d.status = a.status;
+    d.kpp_ticket = reinterpret_cast<uint32_t*>(ws + L.tick);
     d.G = (int)G;
     // per-cell work arrays use stride d.kst (max k); sub-centroids use a.kmax
     // ---- host draws (the reference's seeds, the same <random> algorithms)
@@ -1904,6 +1936,7 @@ cudaError_t run_build(const BuildArgs& a, cudaStream_t st, const char** why) {
         if (e != cudaSuccess) return e;
     }
     cudaMemsetAsync(d.done, 0, (size_t)d.T * 4, st);
+    cudaMemsetAsync(d.kpp_ticket, 0, (size_t)d.T * 4, st);
     cudaMemsetAsync(d.iters_run, 0, (size_t)d.T * 4, st);
     cudaError_t e;
     if (a.phase_ns) stamp_kernel<<<1, 32, 0, st>>>(a.phase_ns);
