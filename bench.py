@@ -881,19 +881,76 @@ def run_prefill_overlap(args):
                     "layer's dense prefill work); keys/values synthetic; the build reads them in place"}
 
 
+# ----------------------------------------------------------------------------
+# random-init Qwen2.5-72B, 8 GPUs, 128 greedy tokens
+# ----------------------------------------------------------------------------
+METRIC_E2E = "decode_tokens_per_s@qwen72b_128K"
+# the reference's Qwen2.5-72B k-means settings (config/Qwen2.5-72B-Instruct.json)
+KMEANS4 = {"max_iters": 5, "tol": 0.0005, "early_stop_min_iter": 5, "early_stop_rel_tol": 0.0005}
+
+
+def run_qwen72b_e2e(args):
+    """Tensor-parallel random-init Qwen2.5-72B (80 layers, hidden 8192, 64 query
+    / 8 KV heads, head_dim 128; one KV head per GPU at 8 GPUs): a prompt of
+    random token ids (vocabulary 152064), prefill with the IMI of every layer
+    built at the end of its prefill, then greedy decoding through the cache
+    (adaptiveimi_b200.model_e2e, the reference's inference loop).  Reports
+    decode tokens/s, prefill seconds and the device build time (max over
+    ranks)."""
+    import torch.distributed as dist
+
+    from adaptiveimi_b200.model_e2e import DecoderConfig, TPDecoder, generate
+    from adaptiveimi_b200.sharding import max_over_ranks
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        dist.init_process_group("nccl", init_method="env://")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    base = DecoderConfig.qwen25_72b()
+    cfg = DecoderConfig(layers=min(args.layers, base.layers) if args.layers else base.layers)
+    ctx = args.context
+    new_tokens = 128
+    model = TPDecoder(cfg, dev, seed=0, attention="imi")
+    ids = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(0)).to(dev)
+    model.make_cache(ctx, new_tokens, budget=0.1, parts=2, kmeans=KMEANS4)
+    with Clocks(local) as clk:
+        r = generate(model, ids, new_tokens)
+    prefill_s, decode_s, build_ms = max_over_ranks([r["prefill_s"], r["decode_s"], r["build_ms"]], dev)
+    if rank != 0:
+        if ws > 1:
+            dist.destroy_process_group()
+        return None
+    steps = new_tokens - 1
+    res = {"metric": METRIC_E2E, "value": round(steps / decode_s, 3), "unit": "tokens/s", "n_gpus": ws,
+           "steps": steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic: random-init weights, random prompt token ids (no checkpoint, no dataset)",
+           "config": {"workload": "BASELINE configs[4]: Qwen2.5-72B geometry, random init, 131072-token prompt, "
+                                  "128 greedy tokens, KV heads split over the GPUs, budget 0.1, S=2",
+                      "layers": cfg.layers, "context": ctx, "kv_heads_per_gpu": model.kvh,
+                      "parallelism": f"tensor parallel x{ws} (NCCL all-reduce after o_proj and down_proj)"},
+           "prefill_s": round(prefill_s, 3), "decode_ms_per_token": round(decode_s * 1000 / steps, 3),
+           "imi_build_ms_total": round(build_ms, 2), "tokens_head": r["tokens"][:8], "clocks": clk.summary()}
+    if ws > 1:
+        dist.destroy_process_group()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=CFG["layers"])
+    ap.add_argument("--layers", type=int, default=None, help="default: the workload's model (32, or 80 for qwen72b_e2e)")
     ap.add_argument("--context", type=int, default=None, help="default: 131072 (128k) or 1048576 (1m)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="128k", choices=["128k", "1m", "qwen7b", "prefill_overlap"],
+    ap.add_argument("--workload", default="128k", choices=["128k", "1m", "qwen7b", "prefill_overlap", "qwen72b_e2e"],
                     help="1m: BASELINE configs[2], the 1M context sequence-sharded over the ranks; "
                          "qwen7b: BASELINE configs[3], batch 8 with ragged contexts, S=4")
     args = ap.parse_args()
+    if args.layers is None:
+        args.layers = 80 if args.workload == "qwen72b_e2e" else CFG["layers"]
     if args.context is None:
         args.context = 1_048_576 if args.workload == "1m" else CFG["context"]
     if args.workload == "1m":
@@ -907,6 +964,18 @@ def main():
         if args.warmup < 3:
             args.warmup = 3
         res = run_1m(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if args.workload == "qwen72b_e2e":
+        if args.impl == "reference":
+            ws, rank, _ = dist_env()
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "metric": METRIC_E2E,
+                                  "unavailable": "the reference's model loop needs HF checkpoints and its CPU page "
+                                                 "cache; not run"}), flush=True)
+            return
+        res = run_qwen72b_e2e(args)
         if res is not None:
             print(json.dumps(res), flush=True)
         return
