@@ -36,6 +36,22 @@
 
 namespace imi {
 
+#ifdef ATT_STAMPS  // profiling aid: globaltimer per CTA phase past the partials (part_o is sized twice)
+#define ATT_STAMP(k)                                                                                    \
+    do {                                                                                                \
+        if (threadIdx.x == 0) {                                                                         \
+            unsigned long long t_;                                                                      \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            reinterpret_cast<unsigned long long*>(a.part_o + (size_t)a.bg * a.splits * a.G * 128)      \
+                [((size_t)blockIdx.y * a.splits + blockIdx.x) * 8 + (k)] = t_;                          \
+        }                                                                                               \
+    } while (0)
+#else
+#define ATT_STAMP(k) \
+    do {             \
+    } while (0)
+#endif
+
 __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) {
     extern __shared__ __align__(128) unsigned char att_smem[];
     const int h = blockIdx.y;
@@ -44,7 +60,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
     const uint32_t ring = smem_u32(att_smem);
     // Launched as a programmatic dependent of the select kernel: everything
     // above overlaps its tail; every global read comes after this wait.
+    ATT_STAMP(0);
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    ATT_STAMP(1);
     // the next layer's append (a programmatic dependent) may start launching
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
@@ -72,10 +90,14 @@ __global__ void __launch_bounds__(AT_WARPS * 32, 1) imi_attn_kernel(AttnArgs a) 
         const int r = t * AT_TILE + (lane & 15);
         return (t < ct1 && r < rows_total) ? rlist[r] : -1;
     };
+    ATT_STAMP(2);
     attn_stream(a, h, warp, lane, ring, ct0, ct1, rows_total, qa, entry, m_run, l_run, o);
+    ATT_STAMP(3);
     attn_write_partial(a, h, split, att_smem, m_run, l_run, o);
+    ATT_STAMP(4);
     if (!a.counters) return;  // a separate merge launch follows
-    attn_ticket_merge(a, h, att_smem);
+    if (attn_ticket_merge(a, h, att_smem)) ATT_STAMP(6);
+    else ATT_STAMP(5);
 }
 
 __global__ void imi_combine_kernel(AttnArgs a) {
