@@ -136,6 +136,8 @@ class TPDecoder:
         self.norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
         self.cache = None
         self.dense_kv: List[Optional[tuple]] = [None] * cfg.layers
+        self._graphs = None
+        self.last_hidden: Optional[torch.Tensor] = None   # hidden state after the last decode step
 
     # -- pieces -------------------------------------------------------------------
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
@@ -224,11 +226,80 @@ class TPDecoder:
         return self._greedy(h[-1])
 
     def decode(self, token: torch.Tensor, position: int) -> torch.Tensor:
+        if self._graphs is not None:
+            return self._decode_graphed(token, position)
         h = self._embed(token)
         pos = torch.full((1,), position, device=self.device, dtype=torch.int64)
         for l in range(self.cfg.layers):
             self._layer(l, h, pos, False)
+        self.last_hidden = h
         return self._greedy(h[0])
+
+    # -- CUDA graphs of a decode step's dense work ----------------------------------
+    def _pre(self, l: int):
+        """Graph body before the cache: norm, QKV projection, RoPE (static buffers)."""
+        lw, D = self.layers[l], self.cfg.head_dim
+        x = rms_norm(self._g_h, lw["ln1"], self.cfg.rms_eps)
+        qkv = F.linear(x, lw["wqkv"], lw["bqkv"])
+        q = qkv[:, :self.qh * D].view(-1, self.qh, D)
+        k = qkv[:, self.qh * D:(self.qh + self.kvh) * D].view(-1, self.kvh, D)
+        v = qkv[:, (self.qh + self.kvh) * D:].reshape(-1, self.kvh, D).contiguous()
+        return apply_rope(q, self._g_cos, self._g_sin), apply_rope(k, self._g_cos, self._g_sin), v
+
+    def _post(self, l: int) -> None:
+        """Graph body after the cache: o_proj + all-reduce, the MLP (in place on h)."""
+        lw = self.layers[l]
+        self._g_h += _all_reduce(F.linear(self._g_o, lw["wo"]))
+        self._mlp(lw, self._g_h)
+
+    def capture_decode_graphs(self) -> None:
+        """Capture, per layer, the dense work before and after the cache calls as
+        two CUDA graphs over static buffers (the hidden state, RoPE cos/sin, the
+        attention output), so a decode step is 2 graph launches per layer plus
+        the cache's own launches instead of ~50 eager kernel launches per layer.
+        The cache calls (append, selection, attention) stay eager: their
+        descriptors carry the step's position and the asynchronous centroid
+        update schedule, which change from step to step.  Every rank captures
+        the same sequence, so the all-reduces inside the graphs pair up."""
+        if self.device.type != "cuda":
+            raise RuntimeError("decode graphs need a CUDA device")
+        H, D = self.cfg.hidden, self.cfg.head_dim
+        dev = self.device
+        self._g_h = torch.zeros((1, H), dtype=torch.bfloat16, device=dev)
+        self._g_o = torch.zeros((1, self.qh * D), dtype=torch.bfloat16, device=dev)
+        self._g_cos = torch.zeros((1, D // 2), dtype=torch.float32, device=dev)
+        self._g_sin = torch.zeros((1, D // 2), dtype=torch.float32, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):         # warm-up outside capture (library handles, workspaces)
+            for _ in range(3):
+                self._pre(0)
+                self._post(0)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        pool = torch.cuda.graph_pool_handle()
+        graphs = []
+        for l in range(self.cfg.layers):
+            ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, pool=pool):
+                qkv = self._pre(l)
+            with torch.cuda.graph(gb, pool=pool):
+                self._post(l)
+            graphs.append((ga, qkv, gb))
+        torch.cuda.synchronize(dev)
+        self._graphs = graphs
+
+    def _decode_graphed(self, token: torch.Tensor, position: int) -> torch.Tensor:
+        self._g_h.copy_(self._embed(token))
+        pos = torch.full((1,), position, device=self.device, dtype=torch.int64)
+        cos, sin = rope_cos_sin(pos, self.cfg.head_dim, self.cfg.rope_theta)
+        self._g_cos.copy_(cos)
+        self._g_sin.copy_(sin)
+        for l, (ga, (q, k, v), gb) in enumerate(self._graphs):
+            ga.replay()
+            self._g_o.copy_(self._decode_attention(l, q, k, v))
+            gb.replay()
+        self.last_hidden = self._g_h
+        return self._greedy(self._g_h[0])
 
     def make_cache(self, prompt_len: int, new_tokens: int, *, budget: float = 0.1, parts: int = 2,
                    kmeans: Optional[dict] = None):
@@ -247,11 +318,13 @@ class TPDecoder:
         return self.cache
 
 
-def generate(model: TPDecoder, ids: torch.Tensor, new_tokens: int) -> dict:
+def generate(model: TPDecoder, ids: torch.Tensor, new_tokens: int, graphs: bool = False) -> dict:
     """model_hub/base.py:407-496 ``inference`` with greedy sampling: prefill,
     ``prepare_cache`` (the reference's ``move``), then new_tokens - 1 decode
     steps.  Returns the tokens and the timings (wall clock around synchronised
-    device work, as the reference reports them)."""
+    device work, as the reference reports them).  ``graphs`` captures the
+    dense part of each decode layer as CUDA graphs after ``prepare_cache``
+    (counted in the prefill time)."""
     dev = model.device
 
     def sync():
@@ -264,6 +337,8 @@ def generate(model: TPDecoder, ids: torch.Tensor, new_tokens: int) -> dict:
     out = [tok]
     if model.cache is not None:
         model.cache.prepare_cache()
+    if graphs:
+        model.capture_decode_graphs()
     sync()
     t1 = time.perf_counter()
     T = ids.shape[0]
