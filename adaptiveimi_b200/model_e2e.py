@@ -259,10 +259,15 @@ class TPDecoder:
         the cache's own launches instead of ~50 eager kernel launches per layer.
         The cache calls (append, selection, attention) stay eager: their
         descriptors carry the step's position and the asynchronous centroid
-        update schedule, which change from step to step.  Every rank captures
-        the same sequence, so the all-reduces inside the graphs pair up."""
+        update schedule, which change from step to step.  For a
+        single process only (there are no all-reduces inside the graphs then)."""
         if self.device.type != "cuda":
             raise RuntimeError("decode graphs need a CUDA device")
+        if self.ws > 1:
+            # An 8-rank run with the all-reduces captured inside these graphs
+            # stalled without output on B200 (cause not found), so multi-rank
+            # decoding keeps its dense work eager.
+            raise RuntimeError("decode graphs are single-process only; tensor-parallel decoding runs eagerly")
         H, D = self.cfg.hidden, self.cfg.head_dim
         dev = self.device
         self._g_h = torch.zeros((1, H), dtype=torch.bfloat16, device=dev)

@@ -915,7 +915,7 @@ def run_qwen72b_e2e(args):
     ids = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(0)).to(dev)
     model.make_cache(ctx, new_tokens, budget=0.1, parts=2, kmeans=KMEANS4)
     with Clocks(local) as clk:
-        r = generate(model, ids, new_tokens, graphs=not args.eager_decode)
+        r = generate(model, ids, new_tokens, graphs=ws == 1 and not args.eager_decode)
     prefill_s, decode_s, build_ms = max_over_ranks([r["prefill_s"], r["decode_s"], r["build_ms"]], dev)
     if rank != 0:
         if ws > 1:
@@ -929,7 +929,7 @@ def run_qwen72b_e2e(args):
                                   "128 greedy tokens, KV heads split over the GPUs, budget 0.1, S=2",
                       "layers": cfg.layers, "context": ctx, "kv_heads_per_gpu": model.kvh,
                       "parallelism": f"tensor parallel x{ws} (NCCL all-reduce after o_proj and down_proj)",
-                      "decode_dense_work": "eager" if args.eager_decode else "CUDA graphs per layer (cache calls eager)"},
+                      "decode_dense_work": "eager" if (ws > 1 or args.eager_decode) else "CUDA graphs per layer (cache calls eager)"},
            "prefill_s": round(prefill_s, 3), "decode_ms_per_token": round(decode_s * 1000 / steps, 3),
            "imi_build_ms_total": round(build_ms, 2), "tokens_head": r["tokens"][:8], "clocks": clk.summary()}
     if ws > 1:
@@ -947,7 +947,8 @@ def main():
     ap.add_argument("--context", type=int, default=None, help="default: 131072 (128k) or 1048576 (1m)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager-decode", action="store_true",
-                    help="qwen72b_e2e: run the decode layers' dense work eagerly instead of as CUDA graphs")
+                    help="qwen72b_e2e on one GPU: run the decode layers' dense work eagerly instead of as "
+                         "CUDA graphs (multi-GPU runs are always eager)")
     ap.add_argument("--workload", default="128k", choices=["128k", "1m", "qwen7b", "prefill_overlap", "qwen72b_e2e"],
                     help="1m: BASELINE configs[2], the 1M context sequence-sharded over the ranks; "
                          "qwen7b: BASELINE configs[3], batch 8 with ragged contexts, S=4")
