@@ -447,10 +447,11 @@ def _ref_modules():
     return imi_ref, AdpIMI_Index
 
 
-def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
+def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2, sample_warmup=1):
     """The reference's CPU path on a bounded sample: build of `build_heads` heads
-    of one 128K layer with every host thread, and `sample_steps` decode steps of
-    `sample_layers` layers (8 KV heads)."""
+    of one 128K layer with every host thread, and `sample_steps` timed decode
+    steps of `sample_layers` layers (8 KV heads) after `sample_warmup` untimed
+    ones."""
     import numpy as np
 
     from adaptiveimi_b200.sizing import RetrievalSizes, adaptive_k
@@ -519,9 +520,11 @@ def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
         lv[h] = r["list_values"][src]
     trunc = PageTruncation(mods[1], sizes_t, offs_t, sizes.nprobe, sizes.buffer_size, threads=min(cores, 8))
     steps_total = sample_steps * sample_layers
-    qs, _, _ = decode_inputs([means], G, ctx, steps_total, "cpu", seed=0)
-    t0 = time.perf_counter()
-    for t in range(steps_total):
+    warm_total = sample_warmup * sample_layers
+    qs, _, _ = decode_inputs([means], G, ctx, warm_total + steps_total, "cpu", seed=0)
+    for t in range(warm_total + steps_total):
+        if t == warm_total:
+            t0 = time.perf_counter()
         q = qs[t, 0, 0, 0].reshape(kvh, G, D)
         qb = O.bf16_bits(q)
         sims = torch.from_numpy(np.stack([O.scores(qb[h], cents[h], mask[h]) for h in range(kvh)]))
@@ -536,7 +539,8 @@ def cpu_baseline(args, sample_layers=1, sample_steps=2, build_heads=2):
     dec_s = time.perf_counter() - t0
     us = dec_s * 1e6 / steps_total
     return {"value": round(us, 1), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"decode: {sample_steps} step(s) x {sample_layers} layer(s), 8 KV heads, {ctx}-token context, "
+            "sample": f"decode: {sample_steps} step(s) x {sample_layers} layer(s) after {sample_warmup} untimed, "
+                      f"8 KV heads, {ctx}-token context, "
                       f"mixture queries; scorer = C port of compute_impl.cu, top-k/budget = the reference's torch "
                       f"calls, page truncation = the reference's AdpIMI_Index.batch_access (C++), gather + "
                       f"attention = torch fp32",
@@ -550,9 +554,9 @@ def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
         return None
-    warm = max(0, min(args.warmup, 1))
-    steps = max(1, min(args.steps, 3))
-    cb = cpu_baseline(args, sample_layers=1, sample_steps=steps + warm)
+    warm = max(0, min(args.warmup, 5))      # a decode step of the sample is ~30 ms on the host cores
+    steps = max(1, min(args.steps, 20))
+    cb = cpu_baseline(args, sample_layers=1, sample_steps=steps, sample_warmup=warm)
     res = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": ws,
         "steps": steps, "warmup": warm, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
